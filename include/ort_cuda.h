@@ -1,0 +1,203 @@
+/*
+ * ort_cuda.h — C ABI of the B200 matmul hot path for onnx_runtime_dart.
+ *
+ * The reference (CrispStrobe/onnx_runtime_dart 0.10.3, pure Dart) computes
+ * MatMulNBits, MatMul and Gemm inside OnnxGraphExecutor._dispatch
+ * (lib/src/onnx_graph.dart:961).  This library replaces the bodies of those
+ * three cases: a dart:ffi binding calls the functions below, which launch
+ * hand-written sm_100a CUDA kernels.  No Python, no PyTorch and no CPU
+ * compute sits behind these entry points.
+ *
+ * Conventions
+ *  - Every function returns an int status (ORT_CUDA_OK == 0).  On failure
+ *    ort_cuda_last_error() returns a thread-local message.  The Dart side
+ *    maps ORT_CUDA_ERR_UNSUPPORTED to UnsupportedError (as
+ *    lib/src/onnx_qlinear_ops.dart:117-119 and onnx_graph.dart:1585-1588
+ *    throw) and every other code to StateError (onnx_graph.dart:789-795).
+ *  - All matrices are row-major fp32 unless stated, like the reference's
+ *    Float32List tensors (lib/src/tensor.dart:14-59).
+ *  - Weights are uploaded once per session and addressed by initializer
+ *    name, as the reference caches prepacked Gemm B by name
+ *    (onnx_graph.dart:53-56, :1160).
+ *  - A/C/Y pointers are device pointers (stream-ordered, asynchronous on
+ *    the session stream) unless ORT_CUDA_HOST_IO is set, in which case they
+ *    are host pointers and the call returns after Y has been written.
+ */
+#ifndef ORT_CUDA_H_
+#define ORT_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORT_CUDA_API __attribute__((visibility("default")))
+
+/* ---- status codes ---------------------------------------------------- */
+#define ORT_CUDA_OK 0
+#define ORT_CUDA_ERR_INVALID_ARG 1 /* bad shape / size / pointer      */
+#define ORT_CUDA_ERR_UNSUPPORTED 2 /* bits != 4, g_idx/bias, ...      */
+#define ORT_CUDA_ERR_CUDA 3        /* CUDA runtime or launch failure  */
+#define ORT_CUDA_ERR_NCCL 4        /* NCCL failure                    */
+#define ORT_CUDA_ERR_TIMEOUT 5     /* collective / device wait timed out */
+#define ORT_CUDA_ERR_NOT_FOUND 6   /* no weight uploaded under name   */
+#define ORT_CUDA_ERR_OOM 7         /* device allocation failed        */
+
+/* ---- arithmetic modes ------------------------------------------------ */
+/* fp32 inputs, fp32 dequantisation, fp32 FFMA accumulation.  Within 1e-5
+ * max-relative error (max|dY| / max|Y_ref|) of the reference. */
+#define ORT_CUDA_MODE_EXACT 0
+/* The reference's own rounding sequence (k-ascending, separate fp32
+ * multiply and add, double-accumulated tail columns of
+ * gemm_kernel_simd.dart:299-307): bitwise equal to the Dart VM result.
+ * Slow; meant for parity checks. */
+#define ORT_CUDA_MODE_STRICT 1
+/* tcgen05 tensor-core MMA on 16-bit operands with fp32 accumulation in
+ * TMEM.  F16 operands use per-row / per-column power-of-two range
+ * normalisation and meet 2e-3 max-relative error with cosine >= 0.99999;
+ * BF16 operands are offered for callers that accept bf16 rounding
+ * (about 2.5e-3 max-relative on N(0,1) inputs). */
+#define ORT_CUDA_MODE_MMA_F16 2
+#define ORT_CUDA_MODE_MMA_BF16 3
+
+/* ---- call flags ------------------------------------------------------ */
+#define ORT_CUDA_HOST_IO 0x1 /* A, C, Y are host pointers; synchronous   */
+#define ORT_CUDA_MODE_OVERRIDE 0x100 /* bits 12..15 carry a mode for this call */
+#define ORT_CUDA_FLAGS_MODE(m) (ORT_CUDA_MODE_OVERRIDE | (((m)&0xF) << 12))
+#define ORT_CUDA_TRANS_A 0x2 /* Gemm transA=1: A is [K x M]              */
+
+/* ---- upload flags ---------------------------------------------------- */
+#define ORT_CUDA_SCALES_F32 0
+#define ORT_CUDA_SCALES_F16 1 /* fp16 bit patterns, widened bit-exactly on
+                                 the device like
+                                 onnx_proto_loader.dart:29-47 */
+/* Zero points indexed flat, nibble (n*nb + blk) — the reference's layout
+ * (onnx_qlinear_ops.dart:133-138).  Default. */
+#define ORT_CUDA_ZP_FLAT 0x0
+/* Zero points per column, ceil(nb/2) bytes per column (the ORT
+ * com.microsoft spec).  Differs from the reference only when nb is odd. */
+#define ORT_CUDA_ZP_PER_COLUMN 0x10
+
+typedef struct ort_cuda_session ort_cuda_session;
+
+/* Thread-local text of the last failure on this thread ("" if none). */
+ORT_CUDA_API const char* ort_cuda_last_error(void);
+
+/* Library version string. */
+ORT_CUDA_API const char* ort_cuda_version(void);
+
+/* Number of visible CUDA devices. */
+ORT_CUDA_API int ort_cuda_device_count(int* count);
+
+/* ---- sessions -------------------------------------------------------- */
+/* Opens a single-GPU session on `device` with default arithmetic `mode`.
+ * Replaces the in-process state OnnxGraphExecutor builds at load
+ * (onnx_graph.dart:80-98) for the three hot ops. */
+ORT_CUDA_API int ort_cuda_open(int device, int mode, ort_cuda_session** out);
+
+/* Writes a 128-byte NCCL unique id (call on one rank, share the bytes). */
+ORT_CUDA_API int ort_cuda_nccl_unique_id(void* id128);
+
+/* Opens rank `rank` of a `world`-rank session, one process per GPU.
+ * Weights uploaded afterwards are sharded along N (output columns): rank r
+ * keeps columns [r*Ns, min(N, (r+1)*Ns)), Ns = ceil(N/world) rounded up
+ * to 4, the B200 counterpart of GemmPool's column split
+ * (parallel_pool.dart:121-147).  Every matmul then all-gathers Y over
+ * NCCL so each rank holds the full [M x N] result, as GemmPool.matmul
+ * reassembles column slices (parallel_pool.dart:179-205).
+ * `timeout_ms` bounds NCCL initialisation and every collective; on expiry
+ * the communicator is aborted and ORT_CUDA_ERR_TIMEOUT returned. */
+ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void* nccl_id128,
+                                    int mode, int timeout_ms, ort_cuda_session** out);
+
+/* Frees every device buffer of the session (OnnxModel.dispose,
+ * lib/onnx_runtime_dart.dart:140). */
+ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s);
+
+/* Changes the session's default mode. */
+ORT_CUDA_API int ort_cuda_set_mode(ort_cuda_session* s, int mode);
+
+/* Makes the session launch on an existing cudaStream_t (NULL restores the
+ * session's own stream).  For hosts that already own a stream. */
+ORT_CUDA_API int ort_cuda_set_stream(ort_cuda_session* s, void* cuda_stream);
+
+/* Blocks until all work queued on the session stream has finished. */
+ORT_CUDA_API int ort_cuda_sync(ort_cuda_session* s);
+
+/* Rank / world of the session (1-GPU sessions: 0 / 1). */
+ORT_CUDA_API int ort_cuda_rank_info(ort_cuda_session* s, int* rank, int* world);
+
+/* ---- weight residency ---------------------------------------------- */
+/* Uploads a MatMulNBits weight once per session (the reference reads it
+ * from _initializers every call, onnx_qlinear_ops.dart:120-149).
+ *   B       uint8 [N, nb, block_size/2], nb = ceil(K/block_size), packed
+ *           low nibble first
+ *   scales  [N*nb] fp32, or fp16 bit patterns with ORT_CUDA_SCALES_F16
+ *   zp      NULL (implicit 8) or packed uint4 zero points (see ZP flags)
+ * bits must be 4 (else ORT_CUDA_ERR_UNSUPPORTED, as
+ * onnx_qlinear_ops.dart:117-119); block_size a power of two >= 16.
+ * Host pointers; the call is synchronous.  Re-uploading a name replaces
+ * the previous weight. */
+ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, const uint8_t* B,
+                                       const void* scales, const uint8_t* zp, int64_t K,
+                                       int64_t N, int bits, int block_size, int flags);
+
+/* Uploads a dense fp32 MatMul/Gemm weight.  `B` is [rows x cols]; with
+ * trans_b=1 it is stored transposed ([K,N] = B^T), the prepack of
+ * onnx_graph.dart:1156-1173 done once at upload instead of at first run.
+ * Host pointer, synchronous. */
+ORT_CUDA_API int ort_cuda_upload_dense(ort_cuda_session* s, const char* name, const float* B,
+                                       int64_t rows, int64_t cols, int trans_b);
+
+/* Releases one weight. */
+ORT_CUDA_API int ort_cuda_drop_weight(ort_cuda_session* s, const char* name);
+
+/* Shape of an uploaded weight ([K, N], full unsharded N). */
+ORT_CUDA_API int ort_cuda_weight_shape(ort_cuda_session* s, const char* name, int64_t* K,
+                                       int64_t* N);
+
+/* ---- device tensors (activations kept resident between ops) --------- */
+ORT_CUDA_API int ort_cuda_alloc(ort_cuda_session* s, int64_t bytes, void** dptr);
+ORT_CUDA_API int ort_cuda_free(ort_cuda_session* s, void* dptr);
+ORT_CUDA_API int ort_cuda_h2d(ort_cuda_session* s, void* dst, const void* src, int64_t bytes);
+ORT_CUDA_API int ort_cuda_d2h(ort_cuda_session* s, void* dst, const void* src, int64_t bytes);
+
+/* ---- the hot ops ---------------------------------------------------- */
+/* MatMulNBits (com.microsoft), onnx_qlinear_ops.dart:114-156 and its
+ * dispatch case onnx_graph.dart:1584-1596:  Y[M,N] = A[M,K] . W[K,N],
+ * W[k,n] = (q - zp) * scale.  M = element count of A / K. */
+ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, const float* A,
+                                       int64_t M, float* Y, int flags);
+
+/* MatMul with an uploaded [K,N] weight, onnx_ops.dart:1375-1431 with the
+ * shared-weight batch collapse of :1389-1400 (pass M = batch*m). */
+ORT_CUDA_API int ort_cuda_matmul(ort_cuda_session* s, const char* name, const float* A,
+                                 int64_t M, float* Y, int flags);
+
+/* Gemm, onnx_ops.dart:1777-1793 on the prepacked B of
+ * onnx_graph.dart:1156-1173:  Y = alpha * A' . B + beta * C.
+ * C is NULL or [c_rows x c_cols] with c_rows in {1, M}, c_cols in {1, N}
+ * (numpy broadcast as opAdd does, onnx_ops.dart:218-250).  With
+ * ORT_CUDA_TRANS_A, A is stored [K x M]. */
+ORT_CUDA_API int ort_cuda_gemm(ort_cuda_session* s, const char* name, const float* A, int64_t M,
+                               const float* C, int64_t c_rows, int64_t c_cols, float alpha,
+                               float beta, float* Y, int flags);
+
+/* Batched activation x activation MatMul (no uploaded weight), the
+ * per-batch loop of onnx_ops.dart:1402-1429 for equal batch counts:
+ * Y[b] = A[b] . B[b], A [batch,m,k], B [batch,k,n] (b_batch_stride = 0
+ * broadcasts one B).  Device or host pointers as per flags. */
+ORT_CUDA_API int ort_cuda_matmul_batched(ort_cuda_session* s, const float* A, const float* B,
+                                         int64_t batch, int64_t m, int64_t k, int64_t n,
+                                         int64_t b_batch_stride, float* Y, int flags);
+
+/* Kernel launches issued by this session since it was opened (all of
+ * them this library's own kernels). */
+ORT_CUDA_API int ort_cuda_launch_count(ort_cuda_session* s, int64_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORT_CUDA_H_ */

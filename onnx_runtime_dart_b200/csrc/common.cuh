@@ -1,0 +1,119 @@
+// Internal declarations shared by the ort_cuda translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+
+#include "../../include/ort_cuda.h"
+
+namespace ortc {
+
+// ---- error plumbing ------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define ORTC_CUDA(call)                                  \
+  do {                                                   \
+    cudaError_t _e = (call);                             \
+    if (_e != cudaSuccess) return ::ortc::cuda_fail(_e, #call); \
+  } while (0)
+
+#define ORTC_CHECK(cond, code, msg)                      \
+  do {                                                   \
+    if (!(cond)) return ::ortc::fail((code), (msg));     \
+  } while (0)
+
+// ---- weights -------------------------------------------------------------
+enum WeightKind { W_NBITS = 1, W_DENSE = 2 };
+
+// One uploaded initializer, resident for the session.  For an N-sharded
+// session only this rank's columns [n0, n0 + nl) are stored.
+struct Weight {
+  WeightKind kind = W_NBITS;
+  int64_t K = 0, N = 0;   // logical shape [K, N] of the full weight
+  int64_t n0 = 0, nl = 0; // this rank's column range
+  int64_t ns = 0;         // padded per-rank column count (all-gather unit)
+  // MatMulNBits
+  int bs = 0, nb = 0;
+  bool has_zp = false;
+  uint8_t* B = nullptr;     // [nl][nb*bs/2] packed uint4, low nibble first
+  float* scales = nullptr;  // [nl][nb] fp32
+  uint8_t* zp = nullptr;    // packed uint4, nibble (c*nb + blk), local c
+  // dense fp32 MatMul / Gemm operand, effective [K][nl] row-major
+  float* W = nullptr;
+  // Lazily built MMA operand: 16-bit [nl_pad][K_pad] K-major plus the
+  // per-column power-of-two exponent that was factored out (F16 only).
+  void* W16 = nullptr;
+  int w16_mode = -1;
+  int64_t w16_rows = 0, w16_k = 0;
+  int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
+  float* scales16 = nullptr; // nbits MMA: per-(col,blk) scale * 2^-col_exp
+};
+
+}  // namespace ortc
+
+struct ort_cuda_session {
+  int device = 0;
+  int mode = ORT_CUDA_MODE_EXACT;
+  int rank = 0, world = 1;
+  int timeout_ms = 60000;
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  void* nccl = nullptr;  // ncclComm_t when world > 1
+  std::unordered_map<std::string, ortc::Weight> weights;
+  std::unordered_set<void*> allocs;
+  // grow-only device scratch (A staging, per-rank Y before the gather ...)
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  // grow-only pinned host staging for ORT_CUDA_HOST_IO calls
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  int64_t launches = 0;
+};
+
+namespace ortc {
+
+// Scratch helpers (session-owned, stream-ordered reuse).
+int ensure_ws(ort_cuda_session* s, size_t bytes);
+int ensure_pinned(ort_cuda_session* s, size_t bytes);
+
+// ---- kernel launchers (each returns an ORT status) -----------------------
+// All pointers are device pointers; launches go to `st`.
+
+// Y[M, ldy] (columns [0, nl)) = A[M, K] . dequant(W); exact (FFMA) mode.
+int launch_nbits_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
+                      cudaStream_t st, int64_t* launches);
+// General CUDA-core tiled GEMM over an nbits or dense weight (any M).
+// strict=true reproduces the reference's rounding bit for bit.
+int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,
+                     int64_t ldy, bool strict, float alpha, float beta, const float* C,
+                     int64_t c_rows, int64_t c_cols, int64_t c_col0, cudaStream_t st,
+                     int64_t* launches);
+int launch_simt_batched(const float* A, const float* B, int64_t batch, int64_t m, int64_t k,
+                        int64_t n, int64_t b_batch_stride, float* Y, bool strict,
+                        cudaStream_t st, int64_t* launches);
+// Upload-time device prepack helpers.
+int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,
+                         int64_t* launches);
+int launch_transpose(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st,
+                     int64_t* launches);
+// [G, M, Ns] (gathered shards) -> Y[M, N]
+int launch_unshard(const float* g, float* Y, int64_t world, int64_t M, int64_t Ns, int64_t N,
+                   cudaStream_t st, int64_t* launches);
+
+// tcgen05 MMA path (16-bit operands, fp32 accumulation in TMEM).
+int mma_supported_shape(int64_t M, int64_t K);
+int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
+                     int64_t ldy, int mode, cudaStream_t st);
+int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, bool transA,
+                     float* Y, int64_t ldy, int mode, float alpha, float beta, const float* C,
+                     int64_t c_rows, int64_t c_cols, int64_t c_col0, cudaStream_t st);
+
+}  // namespace ortc

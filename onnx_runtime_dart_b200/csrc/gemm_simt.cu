@@ -1,0 +1,365 @@
+// CUDA-core tiled GEMM for every M, over a packed int4 (MatMulNBits) or a
+// dense fp32 (MatMul / Gemm) weight, plus the small helper kernels.
+//
+// Each output is accumulated by one thread in ascending k from 0, which is
+// the order of every path of the reference's matmulKernel
+// (gemm_kernel_simd.dart:27-169).  Two arithmetic variants:
+//   exact  (ORT_CUDA_MODE_EXACT)  acc = fma(a, w, acc)
+//   strict (ORT_CUDA_MODE_STRICT) acc = fl(acc + fl(a * w))  -- the
+//          reference's two roundings, so the result is bitwise equal.
+// In both, the int4 weight tile is dequantised exactly as
+// onnx_qlinear_ops.dart:144-147 does: w = fl((q - zp) * scale).
+// The Gemm epilogue follows onnx_ops.dart:1785-1792: multiply by alpha
+// (when alpha != 1), add beta * C (beta applied only when != 1), each an
+// fp32 rounding of its own.
+#include "common.cuh"
+
+namespace ortc {
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 32, TM = 4, TN = 4;  // 256 threads
+
+template <bool STRICT>
+__device__ __forceinline__ float mac(float acc, float a, float b) {
+  if (STRICT) return __fadd_rn(acc, __fmul_rn(a, b));
+  return __fmaf_rn(a, b, acc);
+}
+
+struct NbitsSrc {
+  const uint8_t* B;
+  const float* S;
+  const uint8_t* Z;
+  int64_t col_bytes;
+  int nb, bs;
+};
+struct DenseSrc {
+  const float* W;  // [K][ldw]
+  int64_t ldw;
+};
+
+// Fill Ws[BK][BN] with the dequantised weight tile (k0.., n0..).
+__device__ __forceinline__ void load_w_tile(float (&Ws)[BK][BN + 4], const NbitsSrc& src,
+                                            int k0, int n0, int K, int N) {
+  // 64 columns x 32 k = 64 x 4 words of 8 nibbles; one word per thread.
+  const int t = threadIdx.x;
+  const int c = t >> 2, wd = t & 3;
+  const int n = n0 + c;
+  const int kw = k0 + wd * 8;
+  float v[8];
+  if (n < N && kw < K) {
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(src.B + (int64_t)n * src.col_bytes + (kw >> 1)));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int kk = kw + i;
+      const int blk = kk / src.bs;
+      if (kk < K) {
+        const int64_t si = (int64_t)n * src.nb + blk;
+        const float scale = __ldg(src.S + si);
+        float z = 8.0f;
+        if (src.Z) {
+          const uint32_t byte = __ldg(src.Z + (si >> 1));
+          z = (float)((byte >> ((si & 1) * 4)) & 0xFu);
+        }
+        const float q = (float)((w >> (4 * i)) & 0xFu);
+        v[i] = __fmul_rn(__fsub_rn(q, z), scale);
+      } else {
+        v[i] = 0.0f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = 0.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) Ws[wd * 8 + i][c] = v[i];
+}
+
+__device__ __forceinline__ void load_w_tile(float (&Ws)[BK][BN + 4], const DenseSrc& src,
+                                            int k0, int n0, int K, int N) {
+  for (int i = threadIdx.x; i < BK * BN; i += 256) {
+    const int kk = i / BN, c = i % BN;
+    const int k = k0 + kk, n = n0 + c;
+    Ws[kk][c] = (k < K && n < N) ? __ldg(src.W + (int64_t)k * src.ldw + n) : 0.0f;
+  }
+}
+
+// Batched activation x activation MatMul: batch b reads B + b * stride.
+__device__ __forceinline__ NbitsSrc batch_offset(const NbitsSrc& s, int64_t) { return s; }
+__device__ __forceinline__ DenseSrc batch_offset(const DenseSrc& s, int64_t off) {
+  return DenseSrc{s.W + off, s.ldw};
+}
+
+struct Epi {
+  float alpha, beta;
+  const float* C;
+  int64_t c_rows, c_cols, c_col0;  // C indexed with global column c_col0 + n
+  bool has_c;
+};
+
+template <bool STRICT, typename Src>
+__global__ void __launch_bounds__(256)
+    simt_gemm_kernel(const float* __restrict__ A, int64_t M, int K, int N, bool transA, Src src,
+                     float* __restrict__ Y, int64_t ldy, Epi epi, int64_t batch_a, int64_t batch_y,
+                     int64_t batch_w) {
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Ws[BK][BN + 4];
+  const int bz = blockIdx.z;
+  A += bz * batch_a;
+  Y += bz * batch_y;
+  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+  const int tx = threadIdx.x % (BN / TN), ty = threadIdx.x / (BN / TN);
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; i++)
+#pragma unroll
+    for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
+
+  const Src s2 = batch_offset(src, bz * batch_w);
+
+  for (int k0 = 0; k0 < K; k0 += BK) {
+    // A tile: As[k][m] = A[m0+m][k0+k]
+    for (int i = threadIdx.x; i < BK * BM; i += 256) {
+      int kk, mm;
+      if (!transA) {
+        mm = i / BK;
+        kk = i % BK;
+      } else {
+        kk = i / BM;
+        mm = i % BM;
+      }
+      const int64_t m = m0 + mm;
+      const int k = k0 + kk;
+      float v = 0.0f;
+      if (m < M && k < K) v = transA ? __ldg(A + (int64_t)k * M + m) : __ldg(A + m * K + k);
+      As[kk][mm] = v;
+    }
+    load_w_tile(Ws, s2, k0, n0, K, N);
+    __syncthreads();
+    const int kmax = (K - k0) < BK ? (K - k0) : BK;
+    for (int kk = 0; kk < kmax; kk++) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; i++) a[i] = As[kk][ty * TM + i];
+#pragma unroll
+      for (int j = 0; j < TN; j++) b[j] = Ws[kk][tx * TN + j];
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = mac<STRICT>(acc[i][j], a[i], b[j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < TM; i++) {
+    const int64_t m = m0 + ty * TM + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; j++) {
+      const int n = n0 + tx * TN + j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
+      if (epi.has_c) {
+        const int64_t cn = epi.c_col0 + n;
+        float c = epi.C[(epi.c_rows == 1 ? 0 : m) * epi.c_cols + (epi.c_cols == 1 ? 0 : cn)];
+        if (epi.beta != 1.0f) c = __fmul_rn(c, epi.beta);
+        v = __fadd_rn(v, c);
+      }
+      Y[m * ldy + n] = v;
+    }
+  }
+}
+
+// Strict mode, M == 1, the last N % 4 (global) columns: the reference's
+// _gemvScalar tail accumulates in double (gemm_kernel_simd.dart:299-307).
+// One thread per column; [col_lo, col_hi) are local column indices.
+template <typename Src>
+__global__ void strict_tail_kernel(const float* __restrict__ A, int K, Src src, int col_lo,
+                                   int col_hi, float* __restrict__ Y, Epi epi);
+
+template <>
+__global__ void strict_tail_kernel<NbitsSrc>(const float* __restrict__ A, int K, NbitsSrc src,
+                                             int col_lo, int col_hi, float* __restrict__ Y,
+                                             Epi epi) {
+  const int n = col_lo + threadIdx.x;
+  if (n >= col_hi) return;
+  double acc = 0.0;
+  for (int k = 0; k < K; k++) {
+    const int blk = k / src.bs, j = k % src.bs;
+    const int64_t si = (int64_t)n * src.nb + blk;
+    const uint8_t byte = src.B[(int64_t)n * src.col_bytes + (int64_t)blk * (src.bs / 2) + (j >> 1)];
+    const float q = (float)((j & 1) ? (byte >> 4) : (byte & 0xF));
+    float z = 8.0f;
+    if (src.Z) z = (float)((src.Z[si >> 1] >> ((si & 1) * 4)) & 0xF);
+    const float w = __fmul_rn(__fsub_rn(q, z), src.S[si]);
+    acc = __dadd_rn(acc, __dmul_rn((double)A[k], (double)w));
+  }
+  Y[n] = (float)acc;
+}
+
+template <>
+__global__ void strict_tail_kernel<DenseSrc>(const float* __restrict__ A, int K, DenseSrc src,
+                                             int col_lo, int col_hi, float* __restrict__ Y,
+                                             Epi epi) {
+  const int n = col_lo + threadIdx.x;
+  if (n >= col_hi) return;
+  double acc = 0.0;
+  for (int k = 0; k < K; k++)
+    acc = __dadd_rn(acc, __dmul_rn((double)A[k], (double)src.W[(int64_t)k * src.ldw + n]));
+  float v = (float)acc;
+  if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
+  if (epi.has_c) {
+    const int64_t cn = epi.c_col0 + n;
+    float c = epi.C[epi.c_cols == 1 ? 0 : cn];
+    if (epi.beta != 1.0f) c = __fmul_rn(c, epi.beta);
+    v = __fadd_rn(v, c);
+  }
+  Y[n] = v;
+}
+
+__global__ void half_to_float_kernel(const uint16_t* __restrict__ h, float* __restrict__ out,
+                                     int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __half2float(__ushort_as_half(h[i]));  // exact widening
+}
+
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                 int64_t rows, int64_t cols) {
+  __shared__ float t[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) t[i][threadIdx.x] = in[r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) out[c * rows + r] = t[threadIdx.x][i];
+  }
+}
+
+__global__ void unshard_kernel(const float* __restrict__ g, float* __restrict__ Y, int64_t world,
+                               int64_t M, int64_t Ns, int64_t N) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i % N;
+    const int64_t r = n / Ns, c = n % Ns;
+    Y[i] = g[(r * M + m) * Ns + c];
+  }
+}
+
+template <bool STRICT, typename Src>
+int run_simt(const float* A, int64_t M, int K, int N, bool transA, const Src& src, float* Y,
+             int64_t ldy, const Epi& epi, int64_t batch, int64_t batch_a, int64_t batch_y,
+             int64_t batch_w, cudaStream_t st, int64_t* launches) {
+  const int64_t gy = (M + BM - 1) / BM;
+  if (gy > 65535 || batch > 65535) return fail(ORT_CUDA_ERR_INVALID_ARG, "simt gemm: grid too large");
+  dim3 grid((N + BN - 1) / BN, (unsigned)gy, (unsigned)batch);
+  simt_gemm_kernel<STRICT, Src><<<grid, 256, 0, st>>>(A, M, K, N, transA, src, Y, ldy, epi,
+                                                      batch_a, batch_y, batch_w);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+}  // namespace
+
+int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,
+                     int64_t ldy, bool strict, float alpha, float beta, const float* C,
+                     int64_t c_rows, int64_t c_cols, int64_t c_col0, cudaStream_t st,
+                     int64_t* launches) {
+  if (w.nl == 0 || M == 0) return ORT_CUDA_OK;
+  Epi epi{alpha, beta, C, c_rows, c_cols, c_col0, C != nullptr};
+  const int K = (int)w.K, N = (int)w.nl;
+  int rc;
+  // Strict M == 1: the reference's double-accumulated tail columns are the
+  // last N % 4 of the FULL weight (global columns >= N - N % 4).
+  int tail_lo = N;
+  if (strict && M == 1 && (w.N & 3) != 0) {
+    const int64_t g_lo = w.N - (w.N & 3) - w.n0;  // local index of first tail column
+    tail_lo = (int)(g_lo < 0 ? 0 : (g_lo > N ? N : g_lo));
+  }
+  if (w.kind == W_NBITS) {
+    NbitsSrc src{w.B, w.scales, w.zp, (int64_t)w.nb * w.bs / 2, w.nb, w.bs};
+    rc = strict ? run_simt<true>(A, M, K, tail_lo, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches)
+                : run_simt<false>(A, M, K, N, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches);
+    if (rc == ORT_CUDA_OK && tail_lo < N) {
+      strict_tail_kernel<NbitsSrc><<<1, 32, 0, st>>>(A, K, src, tail_lo, N, Y, epi);
+      ORTC_CUDA(cudaGetLastError());
+      (*launches)++;
+    }
+  } else {
+    DenseSrc src{w.W, w.nl};
+    rc = strict ? run_simt<true>(A, M, K, tail_lo, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches)
+                : run_simt<false>(A, M, K, N, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches);
+    if (rc == ORT_CUDA_OK && tail_lo < N) {
+      strict_tail_kernel<DenseSrc><<<1, 32, 0, st>>>(A, K, src, tail_lo, N, Y, epi);
+      ORTC_CUDA(cudaGetLastError());
+      (*launches)++;
+    }
+  }
+  return rc;
+}
+
+int launch_simt_batched(const float* A, const float* B, int64_t batch, int64_t m, int64_t k,
+                        int64_t n, int64_t b_batch_stride, float* Y, bool strict,
+                        cudaStream_t st, int64_t* launches) {
+  if (batch == 0 || m == 0 || n == 0) return ORT_CUDA_OK;
+  Epi epi{1.0f, 1.0f, nullptr, 0, 0, 0, false};
+  DenseSrc src{B, n};
+  int rc;
+  // m == 1 per batch runs the reference's _gemv, whose tail columns
+  // (n % 4) accumulate in double (gemm_kernel_simd.dart:299-307).
+  const int tail_lo = (strict && m == 1) ? (int)(n - (n & 3)) : (int)n;
+  if (strict)
+    rc = run_simt<true>(A, m, (int)k, tail_lo, false, src, Y, n, epi, batch, m * k, m * n,
+                        b_batch_stride, st, launches);
+  else
+    rc = run_simt<false>(A, m, (int)k, (int)n, false, src, Y, n, epi, batch, m * k, m * n,
+                         b_batch_stride, st, launches);
+  if (rc == ORT_CUDA_OK && tail_lo < n) {
+    for (int64_t b = 0; b < batch; b++) {
+      DenseSrc sb{B + b * b_batch_stride, n};
+      strict_tail_kernel<DenseSrc><<<1, 32, 0, st>>>(A + b * k, (int)k, sb, tail_lo, (int)n,
+                                                     Y + b * n, epi);
+      ORTC_CUDA(cudaGetLastError());
+      (*launches)++;
+    }
+  }
+  return rc;
+}
+
+int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,
+                         int64_t* launches) {
+  if (n == 0) return ORT_CUDA_OK;
+  half_to_float_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(h, out, n);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+int launch_transpose(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st,
+                     int64_t* launches) {
+  if (rows == 0 || cols == 0) return ORT_CUDA_OK;
+  if ((rows + 31) / 32 > 65535) return fail(ORT_CUDA_ERR_INVALID_ARG, "transpose: too many rows");
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32));
+  transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(in, out, rows, cols);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+int launch_unshard(const float* g, float* Y, int64_t world, int64_t M, int64_t Ns, int64_t N,
+                   cudaStream_t st, int64_t* launches) {
+  if (M * N == 0) return ORT_CUDA_OK;
+  int64_t blocks = (M * N + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  unshard_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, Y, world, M, Ns, N);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+}  // namespace ortc

@@ -1,0 +1,788 @@
+// C ABI (include/ort_cuda.h): sessions, weight residency, device tensors
+// and operator dispatch for MatMulNBits / MatMul / Gemm.
+//
+// This is the B200 counterpart of the three OnnxGraphExecutor._dispatch
+// cases (lib/src/onnx_graph.dart:1154-1173, :1584-1596) together with the
+// state the reference keeps for them (_initializers, _prepackedGemmB,
+// onnx_graph.dart:51-56) and its column-split worker pool
+// (lib/src/parallel_pool.dart:108-205), which becomes NCCL N-sharding.
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ortc {
+
+static thread_local std::string g_err;
+
+void set_error(const std::string& msg) { g_err = msg; }
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  g_err = std::string("CUDA error ") + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) +
+          ") in " + what;
+  if (e == cudaErrorMemoryAllocation) return ORT_CUDA_ERR_OOM;
+  return ORT_CUDA_ERR_CUDA;
+}
+
+int ensure_ws(ort_cuda_session* s, size_t bytes) {
+  if (bytes <= s->ws_bytes) return ORT_CUDA_OK;
+  size_t want = bytes + bytes / 4 + (1 << 20);
+  if (s->ws) {
+    ORTC_CUDA(cudaStreamSynchronize(s->stream));
+    ORTC_CUDA(cudaFree(s->ws));
+    s->ws = nullptr;
+    s->ws_bytes = 0;
+  }
+  ORTC_CUDA(cudaMalloc(&s->ws, want));
+  s->ws_bytes = want;
+  return ORT_CUDA_OK;
+}
+
+int ensure_pinned(ort_cuda_session* s, size_t bytes) {
+  if (bytes <= s->pinned_bytes) return ORT_CUDA_OK;
+  size_t want = bytes + bytes / 4 + (1 << 20);
+  if (s->pinned) {
+    ORTC_CUDA(cudaStreamSynchronize(s->stream));
+    ORTC_CUDA(cudaFreeHost(s->pinned));
+    s->pinned = nullptr;
+    s->pinned_bytes = 0;
+  }
+  ORTC_CUDA(cudaMallocHost(&s->pinned, want));
+  s->pinned_bytes = want;
+  return ORT_CUDA_OK;
+}
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool is_pinned_host(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+
+int free_weight(ortc::Weight& w) {
+  void* ptrs[] = {w.B, w.scales, w.zp, w.W, w.W16, w.col_exp, w.scales16};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  w = ortc::Weight();
+  return ORT_CUDA_OK;
+}
+
+int mode_of(ort_cuda_session* s, int flags) {
+  if (flags & ORT_CUDA_MODE_OVERRIDE) return (flags >> 12) & 0xF;
+  return s->mode;
+}
+
+bool valid_mode(int m) { return m >= ORT_CUDA_MODE_EXACT && m <= ORT_CUDA_MODE_MMA_BF16; }
+
+// Per-rank column range of an N-column weight: Ns = ceil(N/world) rounded
+// up to 4 (16-byte aligned slices for the all-gather), rank r owns
+// [r*Ns, min(N, (r+1)*Ns)).
+void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_t* ns) {
+  int64_t per = (N + world - 1) / world;
+  per = (per + 3) / 4 * 4;
+  if (world == 1) per = N;
+  int64_t a = per * rank;
+  if (a > N) a = N;
+  int64_t b = a + per;
+  if (b > N) b = N;
+  *n0 = a;
+  *nl = b - a;
+  *ns = per;
+}
+
+// Bounded wait on the session stream.  Polls an event so that a collective
+// whose peer never arrives is detected on the host (no device spin); on
+// expiry the NCCL communicator is aborted, which ends its kernels.
+int bounded_sync(ort_cuda_session* s) {
+  if (s->world == 1 || !s->nccl) {
+    ORTC_CUDA(cudaStreamSynchronize(s->stream));
+    return ORT_CUDA_OK;
+  }
+  cudaEvent_t ev;
+  ORTC_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  cudaError_t e = cudaEventRecord(ev, s->stream);
+  if (e != cudaSuccess) {
+    cudaEventDestroy(ev);
+    return cuda_fail(e, "cudaEventRecord");
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    e = cudaEventQuery(ev);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      cudaEventDestroy(ev);
+      return cuda_fail(e, "cudaEventQuery");
+    }
+    ncclResult_t ar = ncclSuccess;
+    ncclCommGetAsyncError((ncclComm_t)s->nccl, &ar);
+    if (ar != ncclSuccess && ar != ncclInProgress) {
+      cudaEventDestroy(ev);
+      ncclCommAbort((ncclComm_t)s->nccl);
+      s->nccl = nullptr;
+      return fail(ORT_CUDA_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > s->timeout_ms) {
+      ncclCommAbort((ncclComm_t)s->nccl);
+      s->nccl = nullptr;
+      cudaEventDestroy(ev);
+      return fail(ORT_CUDA_ERR_TIMEOUT, "collective did not complete within " +
+                                            std::to_string(s->timeout_ms) +
+                                            " ms; communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  cudaEventDestroy(ev);
+  return ORT_CUDA_OK;
+}
+
+int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = ncclCommGetAsyncError(comm, &st);
+    if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(r));
+    if (st == ncclSuccess) return ORT_CUDA_OK;
+    if (st != ncclInProgress) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(st));
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > timeout_ms)
+      return fail(ORT_CUDA_ERR_TIMEOUT, "NCCL did not finish within " +
+                                            std::to_string(timeout_ms) + " ms");
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+// All-gather this rank's [M, Ns] slice (at `local`) into Y [M, N].
+int gather_y(ort_cuda_session* s, const float* local, float* gathered, float* Y, int64_t M,
+             int64_t Ns, int64_t N) {
+  if (!s->nccl) return fail(ORT_CUDA_ERR_NCCL, "session communicator is not usable");
+  ncclResult_t r = ncclAllGather(local, gathered, (size_t)(M * Ns), ncclFloat,
+                                 (ncclComm_t)s->nccl, s->stream);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+  return launch_unshard(gathered, Y, s->world, M, Ns, N, s->stream, &s->launches);
+}
+
+// Host-IO staging: copies `bytes` from host `src` to device `dst` on the
+// session stream (directly if src is pinned, else through the pinned
+// staging buffer at offset `pin_off`).
+int stage_in(ort_cuda_session* s, void* dst, const void* src, size_t bytes, size_t pin_off) {
+  if (bytes == 0) return ORT_CUDA_OK;
+  if (is_pinned_host(src)) {
+    ORTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s->stream));
+    return ORT_CUDA_OK;
+  }
+  std::memcpy((char*)s->pinned + pin_off, src, bytes);
+  ORTC_CUDA(cudaMemcpyAsync(dst, (char*)s->pinned + pin_off, bytes, cudaMemcpyHostToDevice,
+                            s->stream));
+  return ORT_CUDA_OK;
+}
+
+struct IoPlan {
+  // device-side views used by the kernels
+  const float* A = nullptr;
+  const float* C = nullptr;
+  float* Y = nullptr;
+  // host destination (HOST_IO)
+  float* Yhost = nullptr;
+  size_t ybytes = 0;
+  bool yhost_pinned = false;
+  size_t pin_y_off = 0;
+};
+
+}  // namespace
+}  // namespace ortc
+
+using namespace ortc;
+
+extern "C" {
+
+ORT_CUDA_API const char* ort_cuda_last_error(void) { return g_err.c_str(); }
+
+ORT_CUDA_API const char* ort_cuda_version(void) { return "ort_cuda_b200 0.1.0 (sm_100a)"; }
+
+ORT_CUDA_API int ort_cuda_device_count(int* count) {
+  ORTC_CHECK(count, ORT_CUDA_ERR_INVALID_ARG, "count is NULL");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *count = 0;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return ORT_CUDA_OK;
+    return cuda_fail(e, "cudaGetDeviceCount");
+  }
+  *count = n;
+  return ORT_CUDA_OK;
+}
+
+static int open_common(int device, int mode, ort_cuda_session** out) {
+  ORTC_CHECK(out, ORT_CUDA_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  int n = 0;
+  int rc = ort_cuda_device_count(&n);
+  if (rc) return rc;
+  ORTC_CHECK(n > 0, ORT_CUDA_ERR_CUDA, "no CUDA device visible");
+  ORTC_CHECK(device >= 0 && device < n, ORT_CUDA_ERR_INVALID_ARG,
+             "device index " + std::to_string(device) + " out of range");
+  ORTC_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  ORTC_CUDA(cudaGetDeviceProperties(&prop, device));
+  ORTC_CHECK(prop.major == 10 && prop.minor == 0, ORT_CUDA_ERR_UNSUPPORTED,
+             std::string("this library is built for sm_100a (B200); device is ") + prop.name);
+  auto* s = new ort_cuda_session();
+  s->device = device;
+  s->mode = mode;
+  s->sm_count = prop.multiProcessorCount;
+  cudaError_t e = cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete s;
+    return cuda_fail(e, "cudaStreamCreate");
+  }
+  s->stream = s->own_stream;
+  *out = s;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_open(int device, int mode, ort_cuda_session** out) {
+  return open_common(device, mode, out);
+}
+
+ORT_CUDA_API int ort_cuda_nccl_unique_id(void* id128) {
+  ORTC_CHECK(id128, ORT_CUDA_ERR_INVALID_ARG, "id buffer is NULL");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(r));
+  std::memcpy(id128, &id, 128);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void* nccl_id128,
+                                    int mode, int timeout_ms, ort_cuda_session** out) {
+  ORTC_CHECK(world >= 1 && rank >= 0 && rank < world, ORT_CUDA_ERR_INVALID_ARG,
+             "rank/world out of range");
+  ORTC_CHECK(world == 1 || nccl_id128, ORT_CUDA_ERR_INVALID_ARG, "NCCL id is NULL");
+  ORTC_CHECK(timeout_ms > 0, ORT_CUDA_ERR_INVALID_ARG, "timeout_ms must be > 0");
+  int rc = open_common(device, mode, out);
+  if (rc) return rc;
+  ort_cuda_session* s = *out;
+  s->rank = rank;
+  s->world = world;
+  s->timeout_ms = timeout_ms;
+  if (world == 1) return ORT_CUDA_OK;
+  ncclUniqueId id;
+  std::memcpy(&id, nccl_id128, 128);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    ort_cuda_close(s);
+    *out = nullptr;
+    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+  }
+  rc = nccl_wait_ready(comm, timeout_ms);
+  if (rc) {
+    std::string msg = ort_cuda_last_error();
+    ncclCommAbort(comm);
+    ort_cuda_close(s);
+    *out = nullptr;
+    return fail(rc, "NCCL init (rank " + std::to_string(rank) + "/" + std::to_string(world) +
+                        "): " + msg);
+  }
+  s->nccl = comm;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
+  if (!s) return ORT_CUDA_OK;
+  DeviceGuard g(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  for (auto& kv : s->weights) free_weight(kv.second);
+  s->weights.clear();
+  for (void* p : s->allocs) cudaFree(p);
+  s->allocs.clear();
+  if (s->ws) cudaFree(s->ws);
+  if (s->pinned) cudaFreeHost(s->pinned);
+  if (s->nccl) {
+    ncclCommFinalize((ncclComm_t)s->nccl);
+    nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
+    ncclCommDestroy((ncclComm_t)s->nccl);
+  }
+  if (s->own_stream) cudaStreamDestroy(s->own_stream);
+  delete s;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_set_mode(ort_cuda_session* s, int mode) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  s->mode = mode;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_set_stream(ort_cuda_session* s, void* stream) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  s->stream = stream ? (cudaStream_t)stream : s->own_stream;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_sync(ort_cuda_session* s) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  DeviceGuard g(s->device);
+  return bounded_sync(s);
+}
+
+ORT_CUDA_API int ort_cuda_rank_info(ort_cuda_session* s, int* rank, int* world) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  if (rank) *rank = s->rank;
+  if (world) *world = s->world;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_launch_count(ort_cuda_session* s, int64_t* count) {
+  ORTC_CHECK(s && count, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  *count = s->launches;
+  return ORT_CUDA_OK;
+}
+
+// ---- weights ---------------------------------------------------------------
+
+ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, const uint8_t* B,
+                                       const void* scales, const uint8_t* zp, int64_t K,
+                                       int64_t N, int bits, int block_size, int flags) {
+  ORTC_CHECK(s && name && B && scales, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  if (bits != 4)
+    return fail(ORT_CUDA_ERR_UNSUPPORTED,
+                "MatMulNBits: only bits=4 supported, got " + std::to_string(bits));
+  ORTC_CHECK(K > 0 && N > 0 && K < (1ll << 31) && N < (1ll << 31), ORT_CUDA_ERR_INVALID_ARG,
+             "MatMulNBits: K and N must be in [1, 2^31)");
+  ORTC_CHECK(block_size >= 16 && (block_size & (block_size - 1)) == 0, ORT_CUDA_ERR_INVALID_ARG,
+             "MatMulNBits: block_size must be a power of two >= 16, got " +
+                 std::to_string(block_size));
+  DeviceGuard g(s->device);
+  const int64_t nb = (K + block_size - 1) / block_size;
+  const int64_t col_bytes = nb * block_size / 2;
+  Weight w;
+  w.kind = W_NBITS;
+  w.K = K;
+  w.N = N;
+  w.bs = block_size;
+  w.nb = (int)nb;
+  shard_cols(N, s->rank, s->world, &w.n0, &w.nl, &w.ns);
+  w.has_zp = zp != nullptr;
+  const int64_t nl = w.nl;
+  const bool f16 = (flags & ORT_CUDA_SCALES_F16) != 0;
+  auto cleanup = [&](int rc) {
+    free_weight(w);
+    return rc;
+  };
+  cudaError_t e;
+  if (nl > 0) {
+    e = cudaMalloc(&w.B, (size_t)(nl * col_bytes));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(B)"));
+    e = cudaMemcpyAsync(w.B, B + w.n0 * col_bytes, (size_t)(nl * col_bytes),
+                        cudaMemcpyHostToDevice, s->stream);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy B"));
+    e = cudaMalloc(&w.scales, (size_t)(nl * nb * 4));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(scales)"));
+    if (f16) {
+      uint16_t* tmp = nullptr;
+      e = cudaMalloc(&tmp, (size_t)(nl * nb * 2));
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(scales16)"));
+      e = cudaMemcpyAsync(tmp, (const uint16_t*)scales + w.n0 * nb, (size_t)(nl * nb * 2),
+                          cudaMemcpyHostToDevice, s->stream);
+      int rc = e == cudaSuccess ? launch_half_to_float(tmp, w.scales, nl * nb, s->stream, &s->launches)
+                                : cuda_fail(e, "copy scales");
+      cudaStreamSynchronize(s->stream);
+      cudaFree(tmp);
+      if (rc) return cleanup(rc);
+    } else {
+      e = cudaMemcpyAsync(w.scales, (const float*)scales + w.n0 * nb, (size_t)(nl * nb * 4),
+                          cudaMemcpyHostToDevice, s->stream);
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy scales"));
+    }
+    if (zp) {
+      // Re-index zero points to the local flat layout: nibble (c*nb + blk)
+      // of this rank's column c (the reference's flat indexing,
+      // onnx_qlinear_ops.dart:135-137), from either input layout.
+      const int64_t nz = nl * nb;
+      std::vector<uint8_t> z((size_t)((nz + 1) / 2), 0);
+      const bool per_col = (flags & ORT_CUDA_ZP_PER_COLUMN) != 0;
+      const int64_t col_zbytes = (nb + 1) / 2;
+      for (int64_t c = 0; c < nl; c++) {
+        for (int64_t b = 0; b < nb; b++) {
+          uint8_t v;
+          const int64_t gc = w.n0 + c;
+          if (per_col) {
+            const uint8_t byte = zp[gc * col_zbytes + (b >> 1)];
+            v = (b & 1) ? (byte >> 4) : (byte & 0xF);
+          } else {
+            const int64_t zi = gc * nb + b;
+            const uint8_t byte = zp[zi >> 1];
+            v = (zi & 1) ? (byte >> 4) : (byte & 0xF);
+          }
+          const int64_t li = c * nb + b;
+          z[(size_t)(li >> 1)] |= (uint8_t)(v << ((li & 1) * 4));
+        }
+      }
+      e = cudaMalloc(&w.zp, z.size());
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(zp)"));
+      e = cudaMemcpy(w.zp, z.data(), z.size(), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy zp"));
+    }
+    e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "upload sync"));
+  }
+  auto it = s->weights.find(name);
+  if (it != s->weights.end()) {
+    free_weight(it->second);
+    s->weights.erase(it);
+  }
+  s->weights.emplace(name, w);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_upload_dense(ort_cuda_session* s, const char* name, const float* B,
+                                       int64_t rows, int64_t cols, int trans_b) {
+  ORTC_CHECK(s && name && B, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(rows > 0 && cols > 0 && rows < (1ll << 31) && cols < (1ll << 31),
+             ORT_CUDA_ERR_INVALID_ARG, "dense weight: bad shape");
+  DeviceGuard g(s->device);
+  Weight w;
+  w.kind = W_DENSE;
+  w.K = trans_b ? cols : rows;
+  w.N = trans_b ? rows : cols;
+  shard_cols(w.N, s->rank, s->world, &w.n0, &w.nl, &w.ns);
+  auto cleanup = [&](int rc) {
+    free_weight(w);
+    return rc;
+  };
+  cudaError_t e;
+  if (w.nl > 0) {
+    e = cudaMalloc(&w.W, (size_t)(w.K * w.nl * 4));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(W)"));
+    if (trans_b) {
+      // B [N, K]: this rank's rows [n0, n0+nl) are contiguous; transpose
+      // them on the device into [K, nl] (the prepack of
+      // onnx_graph.dart:1159-1161, once per session).
+      float* tmp = nullptr;
+      e = cudaMalloc(&tmp, (size_t)(w.nl * w.K * 4));
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(tmp)"));
+      e = cudaMemcpyAsync(tmp, B + w.n0 * w.K, (size_t)(w.nl * w.K * 4), cudaMemcpyHostToDevice,
+                          s->stream);
+      int rc = e == cudaSuccess ? launch_transpose(tmp, w.W, w.nl, w.K, s->stream, &s->launches)
+                                : cuda_fail(e, "copy B");
+      cudaStreamSynchronize(s->stream);
+      cudaFree(tmp);
+      if (rc) return cleanup(rc);
+    } else {
+      e = cudaMemcpy2DAsync(w.W, (size_t)(w.nl * 4), B + w.n0, (size_t)(w.N * 4),
+                            (size_t)(w.nl * 4), (size_t)w.K, cudaMemcpyHostToDevice, s->stream);
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy B"));
+    }
+    e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "upload sync"));
+  }
+  auto it = s->weights.find(name);
+  if (it != s->weights.end()) {
+    free_weight(it->second);
+    s->weights.erase(it);
+  }
+  s->weights.emplace(name, w);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_drop_weight(ort_cuda_session* s, const char* name) {
+  ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  DeviceGuard g(s->device);
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  cudaStreamSynchronize(s->stream);
+  free_weight(it->second);
+  s->weights.erase(it);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_weight_shape(ort_cuda_session* s, const char* name, int64_t* K,
+                                       int64_t* N) {
+  ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  if (K) *K = it->second.K;
+  if (N) *N = it->second.N;
+  return ORT_CUDA_OK;
+}
+
+// ---- device tensors ----------------------------------------------------------
+
+ORT_CUDA_API int ort_cuda_alloc(ort_cuda_session* s, int64_t bytes, void** dptr) {
+  ORTC_CHECK(s && dptr, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(bytes >= 0, ORT_CUDA_ERR_INVALID_ARG, "negative size");
+  DeviceGuard g(s->device);
+  void* p = nullptr;
+  ORTC_CUDA(cudaMalloc(&p, bytes > 0 ? (size_t)bytes : 16));
+  s->allocs.insert(p);
+  *dptr = p;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_free(ort_cuda_session* s, void* dptr) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  if (!dptr) return ORT_CUDA_OK;
+  DeviceGuard g(s->device);
+  auto it = s->allocs.find(dptr);
+  ORTC_CHECK(it != s->allocs.end(), ORT_CUDA_ERR_INVALID_ARG,
+             "pointer was not allocated by this session");
+  cudaStreamSynchronize(s->stream);
+  ORTC_CUDA(cudaFree(dptr));
+  s->allocs.erase(it);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_h2d(ort_cuda_session* s, void* dst, const void* src, int64_t bytes) {
+  ORTC_CHECK(s && dst && src && bytes >= 0, ORT_CUDA_ERR_INVALID_ARG, "bad argument");
+  DeviceGuard g(s->device);
+  ORTC_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyHostToDevice, s->stream));
+  return bounded_sync(s);
+}
+
+ORT_CUDA_API int ort_cuda_d2h(ort_cuda_session* s, void* dst, const void* src, int64_t bytes) {
+  ORTC_CHECK(s && dst && src && bytes >= 0, ORT_CUDA_ERR_INVALID_ARG, "bad argument");
+  DeviceGuard g(s->device);
+  ORTC_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
+}
+
+// ---- the hot ops --------------------------------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+// Workspace layout for one op call (byte offsets into s->ws, 256-aligned).
+struct WsLayout {
+  size_t a = 0, c = 0, yloc = 0, gath = 0, y = 0, total = 0;
+};
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Runs one matmul-family op: stages host IO, computes this rank's columns,
+// all-gathers across ranks, writes back.  `compute` gets device A, C, the
+// local output pointer and its leading dimension.
+template <typename F>
+int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems, const float* C,
+           int64_t c_elems, float* Y, int64_t M, int flags, F&& compute) {
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  const int64_t N = w.N;
+  const bool sharded = s->world > 1;
+  WsLayout L;
+  size_t off = 0;
+  if (host) {
+    L.a = off;
+    off += al256((size_t)a_elems * 4);
+    L.c = off;
+    off += al256((size_t)c_elems * 4);
+    L.y = off;
+    off += al256((size_t)(M * N) * 4);
+  }
+  if (sharded) {
+    L.yloc = off;
+    off += al256((size_t)(M * w.ns) * 4);
+    L.gath = off;
+    off += al256((size_t)(M * w.ns * s->world) * 4);
+  }
+  L.total = off;
+  int rc = ensure_ws(s, L.total);
+  if (rc) return rc;
+  char* ws = (char*)s->ws;
+  const float* dA = A;
+  const float* dC = C;
+  float* dY = Y;
+  bool y_pinned = false;
+  if (host) {
+    size_t pin_need = (size_t)(a_elems + c_elems + M * N) * 4 + 512;
+    rc = ensure_pinned(s, pin_need);
+    if (rc) return rc;
+    rc = stage_in(s, ws + L.a, A, (size_t)a_elems * 4, 0);
+    if (rc) return rc;
+    dA = (const float*)(ws + L.a);
+    if (C && c_elems) {
+      rc = stage_in(s, ws + L.c, C, (size_t)c_elems * 4, al256((size_t)a_elems * 4));
+      if (rc) return rc;
+      dC = (const float*)(ws + L.c);
+    }
+    dY = (float*)(ws + L.y);
+    y_pinned = is_pinned_host(Y);
+  }
+  float* yloc = sharded ? (float*)(ws + L.yloc) : dY;
+  const int64_t ldy = sharded ? w.ns : N;
+  rc = compute(dA, dC, yloc, ldy);
+  if (rc) return rc;
+  if (sharded) {
+    rc = gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
+    if (rc) return rc;
+  }
+  if (host) {
+    const size_t yb = (size_t)(M * N) * 4;
+    if (y_pinned) {
+      ORTC_CUDA(cudaMemcpyAsync(Y, dY, yb, cudaMemcpyDeviceToHost, s->stream));
+      return bounded_sync(s);
+    }
+    const size_t pin_y = al256((size_t)(a_elems + c_elems) * 4 + 256);
+    ORTC_CUDA(cudaMemcpyAsync((char*)s->pinned + pin_y, dY, yb, cudaMemcpyDeviceToHost,
+                              s->stream));
+    rc = bounded_sync(s);
+    if (rc) return rc;
+    std::memcpy(Y, (char*)s->pinned + pin_y, yb);
+  }
+  return ORT_CUDA_OK;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, const float* A,
+                                       int64_t M, float* Y, int flags) {
+  ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 0, ORT_CUDA_ERR_INVALID_ARG, "M must be >= 0");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  Weight& w = it->second;
+  ORTC_CHECK(w.kind == W_NBITS, ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + name + "' is not a MatMulNBits weight");
+  if (M == 0) return ORT_CUDA_OK;
+  ORTC_CHECK(A && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL A or Y");
+  const int mode = mode_of(s, flags);
+  ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  DeviceGuard g(s->device);
+  return run_op(s, w, A, M * w.K, nullptr, 0, Y, M, flags,
+                [&](const float* dA, const float*, float* yl, int64_t ldy) -> int {
+                  if (mode == ORT_CUDA_MODE_STRICT)
+                    return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
+                                            0, 0, 0, s->stream, &s->launches);
+                  const bool gemv_ok = M <= 4 && (w.K % 32) == 0 && aligned16(dA);
+                  if (gemv_ok) return launch_nbits_gemv(w, dA, M, yl, ldy, s->stream, &s->launches);
+                  if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
+                      mma_supported_shape(M, w.K))
+                    return launch_mma_nbits(s, w, dA, M, yl, ldy, mode, s->stream);
+                  return launch_simt_gemm(w, dA, M, false, yl, ldy, false, 1.0f, 1.0f, nullptr, 0,
+                                          0, 0, s->stream, &s->launches);
+                });
+}
+
+static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64_t M,
+                    const float* C, int64_t c_rows, int64_t c_cols, float alpha, float beta,
+                    float* Y, int flags) {
+  ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 0, ORT_CUDA_ERR_INVALID_ARG, "M must be >= 0");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  Weight& w = it->second;
+  ORTC_CHECK(w.kind == W_DENSE, ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + name + "' is not a dense MatMul/Gemm weight");
+  if (C) {
+    ORTC_CHECK((c_rows == 1 || c_rows == M) && (c_cols == 1 || c_cols == w.N),
+               ORT_CUDA_ERR_INVALID_ARG,
+               "Gemm: C [" + std::to_string(c_rows) + "," + std::to_string(c_cols) +
+                   "] does not broadcast to [" + std::to_string(M) + "," +
+                   std::to_string(w.N) + "]");
+  }
+  if (M == 0) return ORT_CUDA_OK;
+  ORTC_CHECK(A && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL A or Y");
+  const int mode = mode_of(s, flags);
+  ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  const bool transA = (flags & ORT_CUDA_TRANS_A) != 0;
+  DeviceGuard g(s->device);
+  return run_op(s, w, A, M * w.K, C, C ? c_rows * c_cols : 0, Y, M, flags,
+                [&](const float* dA, const float* dC, float* yl, int64_t ldy) -> int {
+                  const bool mma = mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16;
+                  if (mma && mma_supported_shape(M, w.K))
+                    return launch_mma_dense(s, w, dA, M, transA, yl, ldy, mode, alpha, beta, dC,
+                                            c_rows, c_cols, w.n0, s->stream);
+                  return launch_simt_gemm(w, dA, M, transA, yl, ldy, mode == ORT_CUDA_MODE_STRICT,
+                                          alpha, beta, dC, c_rows, c_cols, w.n0, s->stream,
+                                          &s->launches);
+                });
+}
+
+ORT_CUDA_API int ort_cuda_matmul(ort_cuda_session* s, const char* name, const float* A,
+                                 int64_t M, float* Y, int flags) {
+  return dense_op(s, name, A, M, nullptr, 0, 0, 1.0f, 1.0f, Y, flags & ~ORT_CUDA_TRANS_A);
+}
+
+ORT_CUDA_API int ort_cuda_gemm(ort_cuda_session* s, const char* name, const float* A, int64_t M,
+                               const float* C, int64_t c_rows, int64_t c_cols, float alpha,
+                               float beta, float* Y, int flags) {
+  return dense_op(s, name, A, M, C, c_rows, c_cols, alpha, beta, Y, flags);
+}
+
+ORT_CUDA_API int ort_cuda_matmul_batched(ort_cuda_session* s, const float* A, const float* B,
+                                         int64_t batch, int64_t m, int64_t k, int64_t n,
+                                         int64_t b_batch_stride, float* Y, int flags) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  ORTC_CHECK(batch >= 0 && m >= 0 && k >= 0 && n >= 0, ORT_CUDA_ERR_INVALID_ARG,
+             "negative dimension");
+  ORTC_CHECK(b_batch_stride == 0 || b_batch_stride == k * n, ORT_CUDA_ERR_INVALID_ARG,
+             "b_batch_stride must be 0 or k*n");
+  if (batch * m * n == 0) return ORT_CUDA_OK;
+  ORTC_CHECK(A && B && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL pointer");
+  const int mode = mode_of(s, flags);
+  DeviceGuard g(s->device);
+  const bool strict = mode == ORT_CUDA_MODE_STRICT;
+  if (!(flags & ORT_CUDA_HOST_IO))
+    return launch_simt_batched(A, B, batch, m, k, n, b_batch_stride, Y, strict, s->stream,
+                               &s->launches);
+  const int64_t bB = b_batch_stride ? batch * k * n : k * n;
+  const size_t oa = 0, ob = al256((size_t)(batch * m * k) * 4),
+               oy = ob + al256((size_t)bB * 4), tot = oy + al256((size_t)(batch * m * n) * 4);
+  int rc = ensure_ws(s, tot);
+  if (rc) return rc;
+  char* ws = (char*)s->ws;
+  ORTC_CUDA(cudaMemcpyAsync(ws + oa, A, (size_t)(batch * m * k) * 4, cudaMemcpyHostToDevice, s->stream));
+  ORTC_CUDA(cudaMemcpyAsync(ws + ob, B, (size_t)bB * 4, cudaMemcpyHostToDevice, s->stream));
+  rc = launch_simt_batched((const float*)(ws + oa), (const float*)(ws + ob), batch, m, k, n,
+                           b_batch_stride, (float*)(ws + oy), strict, s->stream, &s->launches);
+  if (rc) return rc;
+  ORTC_CUDA(cudaMemcpyAsync(Y, ws + oy, (size_t)(batch * m * n) * 4, cudaMemcpyDeviceToHost, s->stream));
+  ORTC_CUDA(cudaStreamSynchronize(s->stream));
+  return ORT_CUDA_OK;
+}
+
+}  // extern "C"

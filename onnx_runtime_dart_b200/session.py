@@ -1,0 +1,368 @@
+"""Host mirror of the reference's operator interface for the matmul hot path.
+
+The reference dispatches nodes in ``OnnxGraphExecutor._dispatch``
+(lib/src/onnx_graph.dart:961) and keeps weights in ``_initializers`` plus
+prepacked Gemm B in ``_prepackedGemmB`` (:51-56).  ``CudaSession`` is the
+B200 counterpart for the three hot ops: weights are uploaded once (keyed
+by initializer name), activations may stay on the device between ops
+(``DeviceTensor``), and ``dispatch`` mirrors the ``'MatMul'``, ``'Gemm'``
+and ``'MatMulNBits'`` cases (:1154-1173, :1584-1596) including their
+error behaviour.  The module-level ``op_*`` functions mirror the pure op
+functions (``opMatMulNBits`` onnx_qlinear_ops.dart:114-156, ``opGemm``
+onnx_ops.dart:1777-1793, ``opMatMul`` :1375-1431) on a throwaway session.
+
+Every compute call goes through libort_cuda.so (CUDA, sm_100a); nothing in
+this module computes a matmul on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Sequence, Union
+
+import numpy as np
+
+from . import _lib
+from ._lib import StateError, UnsupportedError, check
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array, a torch CUDA tensor or a DeviceTensor."""
+    if a is None:
+        return 0
+    if isinstance(a, DeviceTensor):
+        return a.ptr
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return int(a.data_ptr())
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+class DeviceTensor:
+    """An fp32 activation resident in the session's device memory."""
+
+    def __init__(self, session: "CudaSession", shape: Sequence[int], ptr: Optional[int] = None):
+        self.session = session
+        self.shape = tuple(int(d) for d in shape)
+        self.nbytes = int(np.prod(self.shape, dtype=np.int64)) * 4 if self.shape else 4
+        if ptr is None:
+            p = ctypes.c_void_p()
+            check(_lib.load().ort_cuda_alloc(session.handle, self.nbytes, ctypes.byref(p)),
+                  "ort_cuda_alloc")
+            self.ptr = p.value or 0
+            self._owned = True
+        else:
+            self.ptr = ptr
+            self._owned = False
+
+    @classmethod
+    def from_host(cls, session: "CudaSession", a: np.ndarray) -> "DeviceTensor":
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        t = cls(session, a.shape)
+        check(_lib.load().ort_cuda_h2d(session.handle, t.ptr, a.ctypes.data, a.nbytes),
+              "ort_cuda_h2d")
+        return t
+
+    def numpy(self) -> np.ndarray:
+        out = np.empty(self.shape, np.float32)
+        check(_lib.load().ort_cuda_d2h(self.session.handle, out.ctypes.data, self.ptr,
+                                       self.nbytes), "ort_cuda_d2h")
+        return out
+
+    def free(self) -> None:
+        if self._owned and self.ptr and self.session.handle:
+            check(_lib.load().ort_cuda_free(self.session.handle, self.ptr), "ort_cuda_free")
+        self.ptr = 0
+
+    @property
+    def rank(self) -> int:
+        return len(self.shape)
+
+
+Tensorish = Union[np.ndarray, DeviceTensor]
+
+
+class CudaSession:
+    """One GPU (or one rank of an N-sharded group) running the hot ops.
+
+    mode: "exact" (fp32 FFMA), "strict" (bitwise reference rounding),
+    "mma_f16" / "mma_bf16" (tcgen05 tensor cores)."""
+
+    def __init__(self, device: int = 0, mode: str = "exact", rank: int = 0, world: int = 1,
+                 nccl_id: Optional[bytes] = None, timeout_ms: int = 60000):
+        L = _lib.load()
+        h = ctypes.c_void_p()
+        m = _lib.MODES[mode]
+        if world == 1:
+            check(L.ort_cuda_open(device, m, ctypes.byref(h)), "ort_cuda_open")
+        else:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("a 128-byte NCCL unique id is required for world > 1")
+            buf = ctypes.create_string_buffer(nccl_id, 128)
+            check(L.ort_cuda_open_rank(device, rank, world, buf, m, timeout_ms, ctypes.byref(h)),
+                  "ort_cuda_open_rank")
+        self.handle = h.value
+        self.device, self.rank, self.world, self.mode = device, rank, world, mode
+        # initializer name -> ("nbits" | "dense", K, N)
+        self.weights: Dict[str, tuple] = {}
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(_lib.load().ort_cuda_nccl_unique_id(buf), "ort_cuda_nccl_unique_id")
+        return buf.raw
+
+    # -- lifecycle -------------------------------------------------------
+    def close(self) -> None:
+        if self.handle:
+            check(_lib.load().ort_cuda_close(self.handle), "ort_cuda_close")
+            self.handle = None
+
+    dispose = close  # OnnxModel.dispose (lib/onnx_runtime_dart.dart:140)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_mode(self, mode: str) -> None:
+        check(_lib.load().ort_cuda_set_mode(self.handle, _lib.MODES[mode]), "ort_cuda_set_mode")
+        self.mode = mode
+
+    def set_stream(self, stream_ptr: int) -> None:
+        check(_lib.load().ort_cuda_set_stream(self.handle, stream_ptr or None),
+              "ort_cuda_set_stream")
+
+    def sync(self) -> None:
+        check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")
+
+    def launch_count(self) -> int:
+        c = ctypes.c_int64()
+        check(_lib.load().ort_cuda_launch_count(self.handle, ctypes.byref(c)))
+        return c.value
+
+    # -- weight residency (uploaded once per session) ----------------------
+    def upload_nbits(self, name: str, b_q: np.ndarray, scales: np.ndarray,
+                     zero_points: Optional[np.ndarray], *, k: int, n: int, bits: int = 4,
+                     block_size: int, zp_per_column: bool = False) -> None:
+        b_q = np.ascontiguousarray(b_q, dtype=np.uint8)
+        flags = _lib.ZP_PER_COLUMN if zp_per_column else _lib.ZP_FLAT
+        if scales.dtype == np.float16:
+            sc = np.ascontiguousarray(scales).view(np.uint16)
+            flags |= _lib.SCALES_F16
+        else:
+            sc = np.ascontiguousarray(scales, dtype=np.float32)
+        zp = None if zero_points is None else np.ascontiguousarray(zero_points, dtype=np.uint8)
+        if bits == 4:
+            nb = (k + block_size - 1) // block_size if block_size > 0 else 0
+            if b_q.size < n * nb * (block_size // 2):
+                raise ValueError(f"MatMulNBits: B has {b_q.size} bytes, expected "
+                                 f"{n * nb * (block_size // 2)}")
+            if sc.size < n * nb:
+                raise ValueError(f"MatMulNBits: scales has {sc.size} values, expected {n * nb}")
+            if zp is not None:
+                need = (n * ((nb + 1) // 2)) if zp_per_column else (n * nb + 1) // 2
+                if zp.size < need:
+                    raise ValueError(f"MatMulNBits: zero_points has {zp.size} bytes, "
+                                     f"expected {need}")
+        check(_lib.load().ort_cuda_upload_nbits(self.handle, name.encode(), b_q.ctypes.data,
+                                                sc.ctypes.data, _ptr(zp), k, n, bits,
+                                                block_size, flags), "ort_cuda_upload_nbits")
+        self.weights[name] = ("nbits", k, n)
+
+    def upload_dense(self, name: str, b: np.ndarray, trans_b: bool = False) -> None:
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        if b.ndim != 2:
+            raise ValueError("dense weight must be rank 2")
+        check(_lib.load().ort_cuda_upload_dense(self.handle, name.encode(), b.ctypes.data,
+                                                b.shape[0], b.shape[1], int(trans_b)),
+              "ort_cuda_upload_dense")
+        k, n = (b.shape[1], b.shape[0]) if trans_b else b.shape
+        self.weights[name] = ("dense", k, n)
+
+    def drop_weight(self, name: str) -> None:
+        check(_lib.load().ort_cuda_drop_weight(self.handle, name.encode()), "drop_weight")
+        self.weights.pop(name, None)
+
+    # -- ops -----------------------------------------------------------------
+    def _run(self, fn, name, a: Tensorish, m: int, k: int, n: int, out_shape, extra=(),
+             flags: int = 0, out: Optional[DeviceTensor] = None):
+        L = _lib.load()
+        if isinstance(a, DeviceTensor):
+            y = out if out is not None else DeviceTensor(self, out_shape)
+            check(fn(self.handle, name.encode(), a.ptr, m, *extra, y.ptr, flags), fn.__name__)
+            return y
+        if hasattr(a, "data_ptr"):  # torch CUDA tensor: device pointers
+            y = out
+            if y is None:
+                import torch
+                y = torch.empty(out_shape, dtype=torch.float32, device=a.device)
+            check(fn(self.handle, name.encode(), a.data_ptr(), m, *extra, _ptr(y), flags),
+                  fn.__name__)
+            return y
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        y = np.empty(out_shape, np.float32)
+        check(fn(self.handle, name.encode(), a.ctypes.data, m, *extra, y.ctypes.data,
+                 flags | _lib.HOST_IO), fn.__name__)
+        del L
+        return y
+
+    def matmul_nbits(self, name: str, a: Tensorish, flags: int = 0, out=None):
+        kind, k, n = self.weights[name]
+        shape = tuple(a.shape)
+        if shape[-1] != k:
+            raise ValueError(f"MatMulNBits: A last dim {shape[-1]} != K {k}")
+        m = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        return self._run(_lib.load().ort_cuda_matmul_nbits, name, a, m, k, n,
+                         shape[:-1] + (n,), flags=flags, out=out)
+
+    def matmul(self, name: str, a: Tensorish, flags: int = 0, out=None):
+        kind, k, n = self.weights[name]
+        shape = tuple(a.shape)
+        assert len(shape) >= 2 and shape[-1] == k, f"MatMul inner dims mismatch: {shape[-1]} vs {k}"
+        m = int(np.prod(shape[:-1], dtype=np.int64))
+        return self._run(_lib.load().ort_cuda_matmul, name, a, m, k, n, shape[:-1] + (n,),
+                         flags=flags, out=out)
+
+    def gemm(self, name: str, a: Tensorish, c=None, *, alpha: float = 1.0, beta: float = 1.0,
+             trans_a: bool = False, flags: int = 0, out=None):
+        kind, k, n = self.weights[name]
+        if len(a.shape) != 2:
+            raise ValueError("Gemm: A must be rank 2")
+        m = a.shape[1] if trans_a else a.shape[0]
+        ka = a.shape[0] if trans_a else a.shape[1]
+        if ka != k:
+            raise ValueError(f"Gemm: inner dims mismatch: {ka} vs {k}")
+        if c is not None:
+            cs = tuple(c.shape)
+            c2 = (1,) * (2 - len(cs)) + cs if len(cs) < 2 else cs
+            if len(c2) != 2:
+                raise ValueError(f"Gemm: C rank {len(cs)} not supported")
+            cr, cc = c2
+        else:
+            cr = cc = 0
+        if c is not None and not isinstance(c, DeviceTensor) and not hasattr(c, "data_ptr"):
+            c = np.ascontiguousarray(c, dtype=np.float32)
+        fl = flags | (_lib.TRANS_A if trans_a else 0)
+        return self._run(_lib.load().ort_cuda_gemm, name, a, m, k, n, (m, n),
+                         extra=(_ptr(c), cr, cc, float(alpha), float(beta)), flags=fl, out=out)
+
+    def matmul_batched(self, a: np.ndarray, b: np.ndarray, flags: int = 0) -> np.ndarray:
+        """Activation x activation MatMul with equal (or absent) batch dims."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        m, k = a.shape[-2:]
+        k2, n = b.shape[-2:]
+        if k != k2:
+            raise ValueError(f"MatMul inner dims mismatch: {k} vs {k2}")
+        a_batch, b_batch = a.shape[:-2], b.shape[:-2]
+        out_batch = np.broadcast_shapes(a_batch, b_batch)
+        count = int(np.prod(out_batch)) if out_batch else 1
+        b_count = int(np.prod(b_batch)) if b_batch else 1
+        stride = 0 if b_count == 1 else k * n
+        ab = np.ascontiguousarray(np.broadcast_to(a, tuple(out_batch) + (m, k)))
+        if stride:
+            b = np.ascontiguousarray(np.broadcast_to(b, tuple(out_batch) + (k, n)))
+        y = np.empty(tuple(out_batch) + (m, n), np.float32)
+        check(_lib.load().ort_cuda_matmul_batched(self.handle, ab.ctypes.data, b.ctypes.data,
+                                                  count, m, k, n, stride, y.ctypes.data,
+                                                  flags | _lib.HOST_IO), "matmul_batched")
+        return y
+
+    # -- the _dispatch cases -----------------------------------------------
+    def register_initializers(self, nodes: List[dict], initializers: Dict[str, np.ndarray]):
+        """Load-time upload of every hot-op weight (the residency hook of the
+        OnnxGraphExecutor constructor, onnx_graph.dart:90-97).  ``nodes`` are
+        dicts with op_type / inputs / attrs."""
+        for node in nodes:
+            op, ins, attrs = node["op_type"], node["inputs"], node.get("attrs", {})
+            if op == "MatMulNBits":
+                if len(ins) > 4:
+                    raise UnsupportedError("MatMulNBits: g_idx/bias inputs not supported")
+                zp = initializers.get(ins[3]) if len(ins) > 3 and ins[3] else None
+                self.upload_nbits(ins[1], initializers[ins[1]], initializers[ins[2]], zp,
+                                  k=attrs["K"], n=attrs["N"], bits=attrs.get("bits", 4),
+                                  block_size=attrs["block_size"])
+            elif op == "Gemm" and ins[1] in initializers:
+                self.upload_dense(ins[1], initializers[ins[1]],
+                                  trans_b=bool(attrs.get("transB", 0)))
+            elif op == "MatMul" and ins[1] in initializers and initializers[ins[1]].ndim == 2:
+                self.upload_dense(ins[1], initializers[ins[1]], trans_b=False)
+
+    def dispatch(self, node: dict, values: Dict[str, Tensorish]) -> List[Tensorish]:
+        """One node of OnnxGraphExecutor._dispatch for the hot ops."""
+        op, ins, attrs = node["op_type"], node["inputs"], node.get("attrs", {})
+        a = values[ins[0]]
+        if op == "MatMulNBits":
+            if len(ins) > 4:
+                raise UnsupportedError("MatMulNBits: g_idx/bias inputs not supported")
+            if attrs.get("bits", 4) != 4:
+                raise UnsupportedError(f"MatMulNBits: only bits=4 supported, got {attrs['bits']}")
+            return [self.matmul_nbits(ins[1], a)]
+        if op == "Gemm":
+            c = values.get(ins[2]) if len(ins) > 2 and ins[2] else None
+            return [self.gemm(ins[1], a, c, alpha=attrs.get("alpha", 1.0),
+                              beta=attrs.get("beta", 1.0),
+                              trans_a=bool(attrs.get("transA", 0)))]
+        if op == "MatMul":
+            if ins[1] in self.weights:
+                return [self.matmul(ins[1], a)]
+            return [self.matmul_batched(np.asarray(a), np.asarray(values[ins[1]]))]
+        raise UnsupportedError(f"op {op} is not on the CUDA matmul path")
+
+
+# ---- pure-function mirrors on a throwaway session ----------------------------
+_default: Optional[CudaSession] = None
+
+
+def default_session() -> CudaSession:
+    global _default
+    if _default is None:
+        _default = CudaSession(0)
+    return _default
+
+
+def op_matmul_nbits(a: np.ndarray, b_q: np.ndarray, scales: np.ndarray,
+                    zero_points: Optional[np.ndarray], *, k: int, n: int, bits: int,
+                    block_size: int, mode: str = "exact") -> np.ndarray:
+    """opMatMulNBits (onnx_qlinear_ops.dart:114-156) on the GPU."""
+    if bits != 4:
+        raise UnsupportedError(f"MatMulNBits: only bits=4 supported, got {bits}")
+    s = default_session()
+    s.upload_nbits("__op_matmul_nbits", b_q, scales, zero_points, k=k, n=n, bits=bits,
+                   block_size=block_size)
+    try:
+        return s.matmul_nbits("__op_matmul_nbits", a, flags=_lib.flags_mode(_lib.MODES[mode]))
+    finally:
+        s.drop_weight("__op_matmul_nbits")
+
+
+def op_gemm(a: np.ndarray, b: np.ndarray, c: Optional[np.ndarray] = None, *, alpha: float = 1.0,
+            beta: float = 1.0, trans_a: bool = False, trans_b: bool = False,
+            mode: str = "exact") -> np.ndarray:
+    """opGemm (onnx_ops.dart:1777-1793) on the GPU."""
+    s = default_session()
+    s.upload_dense("__op_gemm", b, trans_b=trans_b)
+    try:
+        return s.gemm("__op_gemm", a, c, alpha=alpha, beta=beta, trans_a=trans_a,
+                      flags=_lib.flags_mode(_lib.MODES[mode]))
+    finally:
+        s.drop_weight("__op_gemm")
+
+
+def op_matmul(a: np.ndarray, b: np.ndarray, mode: str = "exact") -> np.ndarray:
+    """opMatMul (onnx_ops.dart:1375-1431) on the GPU."""
+    s = default_session()
+    fl = _lib.flags_mode(_lib.MODES[mode])
+    if b.ndim == 2:
+        s.upload_dense("__op_matmul", b)
+        try:
+            return s.matmul("__op_matmul", a, flags=fl)
+        finally:
+            s.drop_weight("__op_matmul")
+    return s.matmul_batched(a, b, flags=fl)
+
+
+__all__ = ["CudaSession", "DeviceTensor", "UnsupportedError", "StateError", "op_matmul_nbits",
+           "op_gemm", "op_matmul", "default_session"]

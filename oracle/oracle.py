@@ -1,0 +1,207 @@
+"""CPU ORACLE wrapper — test infrastructure only, never the product path.
+
+ctypes front-end over ``oracle/liboracle.so`` (built from ``oracle.c`` by
+``oracle/Makefile``), plus numpy helpers that generate the seeded synthetic
+inputs of each benchmark configuration.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py`` (its CPU-baseline leg and its
+``--impl reference`` arm) may import this module; the CUDA path in
+``onnx_runtime_dart_b200`` never does.
+
+Each function names the reference (CrispStrobe/onnx_runtime_dart 0.10.3)
+file:line whose arithmetic it restates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+
+
+def build() -> str:
+    """Compile liboracle.so with the committed Makefile (gcc, no GPU)."""
+    subprocess.run(["make", "-s", "-C", _HERE, "liboracle.so"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or (
+            os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "oracle.c"))
+        ):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.orc_half_to_float_bits.restype = ctypes.c_uint32
+        L.orc_half_to_float_bits.argtypes = [ctypes.c_uint32]
+        L.orc_half_to_float_array.argtypes = [_u16p, _f32p, ctypes.c_int64]
+        L.orc_dequant_nbits.argtypes = [_u8p, _f32p, _u8p, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, _f32p]
+        L.orc_matmul_kernel.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int]
+        L.orc_matmul_kernel_scalar.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64,
+                                               ctypes.c_int, ctypes.c_int]
+        L.orc_matmul_nbits.restype = ctypes.c_int
+        L.orc_matmul_nbits.argtypes = [_f32p, ctypes.c_int64, _u8p, _f32p, _u8p, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
+                                       ctypes.c_int]
+        L.orc_transpose.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.orc_gemm.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_float, ctypes.c_float, _f32p, ctypes.c_int64,
+                               ctypes.c_int64, _f32p, ctypes.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a, t):
+    return a.ctypes.data_as(t) if a is not None else ctypes.cast(None, t)
+
+
+def half_to_float(h: np.ndarray) -> np.ndarray:
+    """onnx_proto_loader.dart:29-47 halfToFloat32Bits over an array of
+    fp16 bit patterns (uint16) -> fp32."""
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    out = np.empty(h.shape, np.float32)
+    lib().orc_half_to_float_array(_p(h, _u16p), _p(out, _f32p), h.size)
+    return out
+
+
+def dequant_nbits(B, scales, zp, K, N, block_size) -> np.ndarray:
+    """onnx_qlinear_ops.dart:127-149: the [K, N] fp32 weight opMatMulNBits
+    builds before its GEMM."""
+    B = np.ascontiguousarray(B, np.uint8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    zp = None if zp is None else np.ascontiguousarray(zp, np.uint8)
+    W = np.empty((K, N), np.float32)
+    lib().orc_dequant_nbits(_p(B, _u8p), _p(scales, _f32p), _p(zp, _u8p), K, N, block_size,
+                            _p(W, _f32p))
+    return W
+
+
+def matmul_kernel(a, b, threads: int = 1) -> np.ndarray:
+    """gemm_kernel_simd.dart:27-309 matmulKernel for a [m, k] x [k, n]."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2
+    out = np.empty((m, n), np.float32)
+    lib().orc_matmul_kernel(_p(a, _f32p), _p(b, _f32p), _p(out, _f32p), m, k, n, threads)
+    return out
+
+
+def matmul_kernel_scalar(a, b) -> np.ndarray:
+    """gemm_kernel_scalar.dart:10-41 (the web build's kernel)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    out = np.empty((m, n), np.float32)
+    lib().orc_matmul_kernel_scalar(_p(a, _f32p), _p(b, _f32p), _p(out, _f32p), m, k, n)
+    return out
+
+
+def matmul_nbits(A, B, scales, zp, K, N, bits, block_size, threads: int = 1) -> np.ndarray:
+    """onnx_qlinear_ops.dart:114-156 opMatMulNBits.  A has any rank with a
+    trailing K; Y has shape A.shape[:-1] + [N]."""
+    if bits != 4:
+        raise NotImplementedError(f"MatMulNBits: only bits=4 supported, got {bits}")
+    A = np.ascontiguousarray(A, np.float32)
+    M = A.size // K
+    B = np.ascontiguousarray(B, np.uint8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    zp = None if zp is None else np.ascontiguousarray(zp, np.uint8)
+    Y = np.empty((M, N), np.float32)
+    rc = lib().orc_matmul_nbits(_p(A, _f32p), M, _p(B, _u8p), _p(scales, _f32p), _p(zp, _u8p),
+                                K, N, bits, block_size, _p(Y, _f32p), threads)
+    if rc != 0:
+        raise RuntimeError(f"orc_matmul_nbits failed: {rc}")
+    return Y.reshape(tuple(A.shape[:-1]) + (N,))
+
+
+def gemm(A, B, C=None, alpha=1.0, beta=1.0, transA=False, transB=False, threads: int = 1):
+    """onnx_ops.dart:1777-1793 opGemm (with the transposes of :1782-1783
+    materialised, as onnx_graph.dart:1156-1173 prepacks B)."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    if transA:
+        A = np.ascontiguousarray(A.T)
+    if transB:
+        B = np.ascontiguousarray(B.T)
+    M, K = A.shape
+    N = B.shape[1]
+    Y = np.empty((M, N), np.float32)
+    if C is not None:
+        C = np.ascontiguousarray(C, np.float32)
+        c2 = C.reshape((1,) * (2 - C.ndim) + C.shape) if C.ndim < 2 else C
+        cr, cc = c2.shape
+        if cr not in (1, M) or cc not in (1, N):
+            raise ValueError(f"Gemm: C shape {C.shape} does not broadcast to {(M, N)}")
+        c2 = np.ascontiguousarray(c2)
+    else:
+        c2, cr, cc = None, 0, 0
+    lib().orc_gemm(_p(A, _f32p), _p(B, _f32p), M, K, N, float(alpha), float(beta),
+                   _p(c2, _f32p), cr, cc, _p(Y, _f32p), threads)
+    return Y
+
+
+def matmul(a, b, threads: int = 1) -> np.ndarray:
+    """onnx_ops.dart:1375-1431 opMatMul (float path): numpy-style batch
+    broadcast, with the shared-weight collapse of :1389-1400 (B without
+    batch dims turns all A batches into one [batch*m, k] GEMM)."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    m, k = a.shape[-2:]
+    k2, n = b.shape[-2:]
+    assert k == k2, f"MatMul inner dims mismatch: {k} vs {k2}"
+    a_batch, b_batch = a.shape[:-2], b.shape[:-2]
+    out_batch = np.broadcast_shapes(a_batch, b_batch)
+    count = int(np.prod(out_batch)) if out_batch else 1
+    if count > 1 and int(np.prod(b_batch) if b_batch else 1) == 1:
+        out = matmul_kernel(a.reshape(count * m, k), b.reshape(k, n), threads)
+        return out.reshape(tuple(out_batch) + (m, n))
+    ab = np.broadcast_to(a, tuple(out_batch) + (m, k)).reshape(count, m, k)
+    bb = np.broadcast_to(b, tuple(out_batch) + (k, n)).reshape(count, k, n)
+    out = np.stack([matmul_kernel(ab[i], bb[i], threads) for i in range(count)])
+    return out.reshape(tuple(out_batch) + (m, n))
+
+
+# ---------------------------------------------------------------------------
+# Seeded synthetic inputs (the shapes and distributions of the benchmark
+# configurations; no dataset is involved).
+# ---------------------------------------------------------------------------
+
+def pack_nibbles(q: np.ndarray) -> np.ndarray:
+    """Pack uint4 values [..., 2j] (low nibble) and [..., 2j+1] (high)."""
+    q = q.astype(np.uint8)
+    return (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
+
+
+def make_nbits_weight(rng: np.random.Generator, K: int, N: int, block_size: int,
+                      zero_points: bool, scale_sigma: float = 0.02,
+                      scale_dtype=np.float32, scale_mean: float = 0.0):
+    """Packed uint4 B [N, nb, bs/2] (nibbles uniform 0..15), scales
+    |N(mean, sigma)| [N*nb], optional packed uint4 zero points (flat,
+    low nibble first, uniform 0..15)."""
+    nb = (K + block_size - 1) // block_size
+    q = rng.integers(0, 16, size=(N, nb * block_size), dtype=np.uint8)
+    q[:, K:] = 0
+    B = pack_nibbles(q.reshape(N, nb, block_size))
+    s = rng.standard_normal(N * nb) * scale_sigma + scale_mean
+    if scale_mean == 0.0:
+        s = np.abs(s)
+    scales = s.astype(scale_dtype)
+    zp = None
+    if zero_points:
+        z = rng.integers(0, 16, size=N * nb + (N * nb) % 2, dtype=np.uint8)
+        zp = pack_nibbles(z)
+    return B, scales, zp
