@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""MatMulNBits decode benchmark (B200) — one JSON line on rank 0.
+
+Workload (`config.workload`): one decode step of Llama-3-8B-shaped int4
+projections at M=1 — qkv 4096->6144, o 4096->4096, gate_up 4096->28672,
+down 14336->4096, lm_head 4096->128256 — bits 4, block 128, fp16 scales,
+packed uint4 zero points, random-init weights (seed 5), A ~ N(0,1).
+Weights are uploaded once; activations stay on the device.  With N GPUs
+the output columns of every weight are sharded over the ranks and Y is
+all-gathered over NCCL inside each op (strong scaling: total work fixed).
+
+`value` = whole-job algorithmic bytes per step / device time per step
+(max over ranks), GB/s.  Algorithmic bytes per op = packed B + scales +
+zero points + 4*M*K (A) + 4*M*N_local (Y), summed over ranks.
+`e2e` = the same metric through the C ABI with host buffers (pinned), the
+host<->device copies inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MatMulNBits eff. HBM GB/s (M=1) and TFLOP/s (M=2048) at 1/2/4/8 B200"
+BS = 128
+SEED = 5
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="exact", choices=["exact", "mma_f16", "mma_bf16"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline time budget (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+        os.unlink(self.path)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_weights(projs):
+    from onnx_runtime_dart_b200.workloads import make_nbits_weight
+    rng = np.random.default_rng(SEED)
+    return {p.name: make_nbits_weight(rng, p.K, p.N, BS, zero_points=True,
+                                      scale_dtype=np.float16) for p in projs}
+
+
+def cpu_sample(projs, weights, budget_s, threads):
+    """The reference arithmetic (CPU oracle, port of the Dart path) on a
+    bounded sample of the same workload: every projection at M=1 with its
+    first min(N, 4096) output columns, repeated for about `budget_s`."""
+    from oracle import oracle as O
+    from onnx_runtime_dart_b200.workloads import nbits_bytes
+    rng = np.random.default_rng(SEED + 1)
+    samples = []
+    for p in projs:
+        B, s, z = weights[p.name]
+        nb = p.K // BS
+        n = min(p.N, 4096)
+        zv = np.stack([z & 0xF, z >> 4], 1).ravel()[:p.N * nb]
+        zs = (zv[:n * nb:2] | (zv[1:n * nb:2] << 4)).astype(np.uint8)
+        samples.append((p.K, n, np.ascontiguousarray(B[:n]), s[:n * nb].astype(np.float32), zs,
+                        rng.standard_normal((1, p.K)).astype(np.float32)))
+    bytes_per = sum(nbits_bytes(K, n, BS, 1, 2, True) for K, n, *_ in samples)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for K, n, B, s, z, A in samples:
+            O.matmul_nbits(A, B, s, z, K, n, 4, BS, threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return reps * bytes_per / dt / 1e9, reps, dt, bytes_per
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU arithmetic (oracle port; the
+    Dart VM is not installed) on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from onnx_runtime_dart_b200.workloads import LLAMA3_8B
+    threads = os.cpu_count() or 1
+    weights = make_weights(LLAMA3_8B)
+    budget = 2.0
+    for _ in range(args.warmup):
+        cpu_sample(LLAMA3_8B, weights, 0.0, threads)
+    vals, t_all = [], 0.0
+    for _ in range(args.steps):
+        v, reps, dt, b = cpu_sample(LLAMA3_8B, weights, 0.0, threads)
+        vals.append(v)
+        t_all += dt
+    value = statistics.median(vals)
+    sample = ("per step: qkv,o,gate_up,down,lm_head at M=1 on their first min(N,4096) "
+              "columns (C restatement of the reference's dequant + SIMD GEMM; Dart VM absent)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * t_all / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg5 decode M=1 Llama-3-8B int4 projections (column sample)",
+                       "parallelism": "host threads (column split)"},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+
+    import torch
+    import torch.distributed as dist
+    from onnx_runtime_dart_b200 import CudaSession
+    from onnx_runtime_dart_b200.workloads import LLAMA3_8B, nbits_bytes, shard_range
+
+    torch.cuda.set_device(local)
+    nccl_id = None
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        obj = [CudaSession.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    sess = CudaSession(local, mode=args.mode, rank=rank, world=world, nccl_id=nccl_id,
+                       timeout_ms=120000)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sess.set_stream(stream.cuda_stream)
+
+    projs = LLAMA3_8B
+    weights = make_weights(projs)
+    for p in projs:
+        B, s, z = weights[p.name]
+        sess.upload_nbits(p.name, B, s, z, k=p.K, n=p.N, block_size=BS)
+    M = 1
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(SEED)
+    A = {K: torch.randn(M, K, device=dev, generator=gen) for K in sorted({p.K for p in projs})}
+    Y = {p.name: torch.empty(M, p.N, device=dev) for p in projs}
+
+    # algorithmic bytes this rank moves per step (its column shard)
+    rank_bytes = 0
+    for p in projs:
+        a, b = shard_range(p.N, rank, world)
+        rank_bytes += nbits_bytes(p.K, b - a, BS, M, 2, True)
+    big = max(projs, key=lambda p: p.K * p.N)
+    ba, bb = shard_range(big.N, rank, world)
+    big_bytes = nbits_bytes(big.K, bb - ba, BS, M, 2, True)
+
+    def step(ev=None):
+        for p in projs:
+            if ev is not None and p.name == big.name:
+                ev[0].record(stream)
+            sess.matmul_nbits(p.name, A[p.K], out=Y[p.name])
+            if ev is not None and p.name == big.name:
+                ev[1].record(stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    launches0 = sess.launch_count()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(kev[i])
+    e1.record(stream)
+    barrier()
+    launches = sess.launch_count() - launches0
+    clk = clocks.stop()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    big_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+
+    # ---- end to end through the C ABI with host buffers -----------------
+    hostA = {K: torch.randn(M, K, generator=torch.Generator().manual_seed(K)).pin_memory().numpy()
+             for K in A}
+    hostY = {p.name: torch.empty(M, p.N).pin_memory().numpy() for p in projs}
+
+    def step_e2e():
+        for p in projs:
+            sess.matmul_nbits(p.name, hostA[p.K], out=hostY[p.name])
+
+    for _ in range(args.warmup):
+        step_e2e()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step_e2e()
+    barrier()
+    e2e_ms = 1000 * (time.perf_counter() - t0) / args.steps
+    h2d = sum(4 * M * p.K for p in projs)
+    d2h = sum(4 * M * p.N for p in projs)
+
+    stats = torch.tensor([ms_step, e2e_ms, big_ms], dtype=torch.float64)
+    tot = torch.tensor([rank_bytes, launches], dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    ms_step, e2e_ms, big_ms = stats.tolist()
+    job_bytes, launches = tot.tolist()
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = big_bytes / (big_ms * 1e-3) / 1e9
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "gemv_lm_head_traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get("dram_bytes_per_launch")
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            v, reps, dt, b = cpu_sample(projs, weights, args.cpu_seconds, threads)
+            cpu = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": f"{reps} reps x (qkv,o,gate_up,down,lm_head at M=1 on their first "
+                             f"min(N,4096) columns, {b} B each) in {dt:.1f} s; C restatement of "
+                             "the reference's dequant + SIMD GEMM (Dart VM absent)"}
+        line = {
+            "metric": METRIC, "value": job_bytes / (ms_step * 1e-3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init Llama-3-8B-shaped int4 weights, seed 5)",
+            "config": {"workload": "cfg5 decode step at M=1: MatMulNBits qkv 4096x6144, o "
+                                   "4096x4096, gate_up 4096x28672, down 14336x4096, lm_head "
+                                   "4096x128256; bits 4, block 128, fp16 scales, packed zp",
+                       "mode": args.mode,
+                       "parallelism": f"N-sharded x{world}" + (" + NCCL all-gather of Y"
+                                                              if world > 1 else ""),
+                       "l2": "inputs larger than L2 (about 387 MB of weights per step)"},
+            "roofline": {"bound": "hbm", "kernel": f"int4 GEMV ({big.name})",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": traffic, "bytes_per_launch": big_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    sess.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -4,8 +4,8 @@
 
 Each .cu under csrc/ is compiled separately (parallel), then linked into a
 shared library whose exported symbols are exactly the ort_cuda_* functions
-of include/ort_cuda.h.  The CUDA runtime is linked statically; NCCL
-dynamically.
+of include/ort_cuda.h.  The CUDA runtime is linked statically; NCCL is
+loaded with dlopen on first multi-GPU use (csrc/nccl_dl.cu).
 """
 from __future__ import annotations
 
@@ -56,7 +56,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as ex:
         objs = list(ex.map(_compile, _sources()))
-    cmd = [NVCC] + ARCH + ["-shared", "-o", LIB + ".tmp"] + objs + ["-lnccl"]
+    cmd = [NVCC] + ARCH + ["-shared", "-o", LIB + ".tmp"] + objs + ["-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

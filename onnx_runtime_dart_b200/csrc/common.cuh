@@ -1,6 +1,7 @@
 // Internal declarations shared by the ort_cuda translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -45,6 +46,9 @@ struct Weight {
   uint8_t* B = nullptr;     // [nl][nb*bs/2] packed uint4, low nibble first
   float* scales = nullptr;  // [nl][nb] fp32
   uint8_t* zp = nullptr;    // packed uint4, nibble (c*nb + blk), local c
+  // TMA view of B as uint32 [nl rows][col_bytes/4] (valid when tmB_ok).
+  CUtensorMap tmB;
+  bool tmB_ok = false;
   // dense fp32 MatMul / Gemm operand, effective [K][nl] row-major
   float* W = nullptr;
   // Lazily built MMA operand: 16-bit [nl_pad][K_pad] K-major plus the
@@ -75,6 +79,17 @@ struct ort_cuda_session {
   // grow-only pinned host staging for ORT_CUDA_HOST_IO calls
   void* pinned = nullptr;
   size_t pinned_bytes = 0;
+  // grow-only kernel scratch for split-K partials (no initial value needed)
+  void* kscratch = nullptr;
+  size_t kscratch_bytes = 0;
+  // grow-only arrival counters, zero between calls (kernels reset the
+  // counters they use; re-zeroed after a kernel reported an error)
+  unsigned* kcnt = nullptr;
+  size_t kcnt_words = 0;
+  bool kcnt_dirty = false;
+  // host-mapped error word kernels write when a bounded wait gives up
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
   int64_t launches = 0;
 };
 
@@ -83,13 +98,25 @@ namespace ortc {
 // Scratch helpers (session-owned, stream-ordered reuse).
 int ensure_ws(ort_cuda_session* s, size_t bytes);
 int ensure_pinned(ort_cuda_session* s, size_t bytes);
+int ensure_kscratch(ort_cuda_session* s, size_t bytes);
+int ensure_kcnt(ort_cuda_session* s, size_t words);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point: a 2-D
+// row-major tensor [d1][d0] with row pitch stride1 bytes, box b0 x b1.
+int encode_tma_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t d0,
+                  uint64_t d1, uint64_t stride1, uint32_t b0, uint32_t b1,
+                  CUtensorMapSwizzle swz);
 
 // ---- kernel launchers (each returns an ORT status) -----------------------
 // All pointers are device pointers; launches go to `st`.
 
 // Y[M, ldy] (columns [0, nl)) = A[M, K] . dequant(W); exact (FFMA) mode.
 int launch_nbits_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
+                      float* partials, unsigned* counters, int* err, int sm_count,
                       cudaStream_t st, int64_t* launches);
+// Split-K scratch of the GEMV: partial floats and arrival-counter words.
+size_t gemv_partial_floats(int64_t K, int64_t nl, int64_t M);
+size_t gemv_counter_words(int64_t K, int64_t nl);
 // General CUDA-core tiled GEMM over an nbits or dense weight (any M).
 // strict=true reproduces the reference's rounding bit for bit.
 int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,

@@ -254,6 +254,7 @@ template <bool STRICT, typename Src>
 int run_simt(const float* A, int64_t M, int K, int N, bool transA, const Src& src, float* Y,
              int64_t ldy, const Epi& epi, int64_t batch, int64_t batch_a, int64_t batch_y,
              int64_t batch_w, cudaStream_t st, int64_t* launches) {
+  if (M == 0 || N == 0) return ORT_CUDA_OK;
   const int64_t gy = (M + BM - 1) / BM;
   if (gy > 65535 || batch > 65535) return fail(ORT_CUDA_ERR_INVALID_ARG, "simt gemm: grid too large");
   dim3 grid((N + BN - 1) / BN, (unsigned)gy, (unsigned)batch);

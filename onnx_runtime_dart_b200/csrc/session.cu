@@ -6,8 +6,6 @@
 // state the reference keeps for them (_initializers, _prepackedGemmB,
 // onnx_graph.dart:51-56) and its column-split worker pool
 // (lib/src/parallel_pool.dart:108-205), which becomes NCCL N-sharding.
-#include <nccl.h>
-
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -15,6 +13,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "nccl_dl.cuh"
 
 namespace ortc {
 
@@ -57,6 +56,38 @@ int ensure_pinned(ort_cuda_session* s, size_t bytes) {
   }
   ORTC_CUDA(cudaMallocHost(&s->pinned, want));
   s->pinned_bytes = want;
+  return ORT_CUDA_OK;
+}
+
+int ensure_kscratch(ort_cuda_session* s, size_t bytes) {
+  if (bytes <= s->kscratch_bytes) return ORT_CUDA_OK;
+  size_t want = bytes + bytes / 4 + (1 << 20);
+  if (s->kscratch) {
+    ORTC_CUDA(cudaStreamSynchronize(s->stream));
+    ORTC_CUDA(cudaFree(s->kscratch));
+    s->kscratch = nullptr;
+    s->kscratch_bytes = 0;
+  }
+  ORTC_CUDA(cudaMalloc(&s->kscratch, want));
+  s->kscratch_bytes = want;
+  return ORT_CUDA_OK;
+}
+
+int ensure_kcnt(ort_cuda_session* s, size_t words) {
+  if (words <= s->kcnt_words && !s->kcnt_dirty) return ORT_CUDA_OK;
+  if (words > s->kcnt_words) {
+    size_t want = words + words / 4 + 4096;
+    if (s->kcnt) {
+      ORTC_CUDA(cudaStreamSynchronize(s->stream));
+      ORTC_CUDA(cudaFree(s->kcnt));
+      s->kcnt = nullptr;
+      s->kcnt_words = 0;
+    }
+    ORTC_CUDA(cudaMalloc(&s->kcnt, want * 4));
+    s->kcnt_words = want;
+  }
+  ORTC_CUDA(cudaMemsetAsync(s->kcnt, 0, s->kcnt_words * 4, s->stream));
+  s->kcnt_dirty = false;
   return ORT_CUDA_OK;
 }
 
@@ -115,13 +146,26 @@ void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_
   *ns = per;
 }
 
+// A kernel whose bounded wait gave up wrote a code into the host-mapped
+// error word; report it once and mark the kernel scratch for re-zeroing.
+int check_kernel_error(ort_cuda_session* s) {
+  volatile int* e = s->err_host;
+  if (!e || *e == 0) return ORT_CUDA_OK;
+  const int code = *e;
+  *e = 0;
+  s->kcnt_dirty = true;
+  return fail(ORT_CUDA_ERR_TIMEOUT,
+              "a kernel wait exceeded its bound (code " + std::to_string(code) +
+                  "); the kernel stopped and returned");
+}
+
 // Bounded wait on the session stream.  Polls an event so that a collective
 // whose peer never arrives is detected on the host (no device spin); on
 // expiry the NCCL communicator is aborted, which ends its kernels.
 int bounded_sync(ort_cuda_session* s) {
   if (s->world == 1 || !s->nccl) {
     ORTC_CUDA(cudaStreamSynchronize(s->stream));
-    return ORT_CUDA_OK;
+    return check_kernel_error(s);
   }
   cudaEvent_t ev;
   ORTC_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
@@ -139,18 +183,18 @@ int bounded_sync(ort_cuda_session* s) {
       return cuda_fail(e, "cudaEventQuery");
     }
     ncclResult_t ar = ncclSuccess;
-    ncclCommGetAsyncError((ncclComm_t)s->nccl, &ar);
+    nccl()->CommGetAsyncError((ncclComm_t)s->nccl, &ar);
     if (ar != ncclSuccess && ar != ncclInProgress) {
       cudaEventDestroy(ev);
-      ncclCommAbort((ncclComm_t)s->nccl);
+      nccl()->CommAbort((ncclComm_t)s->nccl);
       s->nccl = nullptr;
-      return fail(ORT_CUDA_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
+      return fail(ORT_CUDA_ERR_NCCL, std::string("NCCL async error: ") + nccl()->GetErrorString(ar));
     }
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                         std::chrono::steady_clock::now() - t0)
                         .count();
     if (ms > s->timeout_ms) {
-      ncclCommAbort((ncclComm_t)s->nccl);
+      nccl()->CommAbort((ncclComm_t)s->nccl);
       s->nccl = nullptr;
       cudaEventDestroy(ev);
       return fail(ORT_CUDA_ERR_TIMEOUT, "collective did not complete within " +
@@ -160,17 +204,17 @@ int bounded_sync(ort_cuda_session* s) {
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
   cudaEventDestroy(ev);
-  return ORT_CUDA_OK;
+  return check_kernel_error(s);
 }
 
 int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
     ncclResult_t st = ncclSuccess;
-    ncclResult_t r = ncclCommGetAsyncError(comm, &st);
-    if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(r));
+    ncclResult_t r = nccl()->CommGetAsyncError(comm, &st);
+    if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, nccl()->GetErrorString(r));
     if (st == ncclSuccess) return ORT_CUDA_OK;
-    if (st != ncclInProgress) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(st));
+    if (st != ncclInProgress) return fail(ORT_CUDA_ERR_NCCL, nccl()->GetErrorString(st));
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                         std::chrono::steady_clock::now() - t0)
                         .count();
@@ -185,10 +229,10 @@ int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
 int gather_y(ort_cuda_session* s, const float* local, float* gathered, float* Y, int64_t M,
              int64_t Ns, int64_t N) {
   if (!s->nccl) return fail(ORT_CUDA_ERR_NCCL, "session communicator is not usable");
-  ncclResult_t r = ncclAllGather(local, gathered, (size_t)(M * Ns), ncclFloat,
+  ncclResult_t r = nccl()->AllGather(local, gathered, (size_t)(M * Ns), ncclFloat,
                                  (ncclComm_t)s->nccl, s->stream);
   if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclAllGather: ") + nccl()->GetErrorString(r));
   return launch_unshard(gathered, Y, s->world, M, Ns, N, s->stream, &s->launches);
 }
 
@@ -269,6 +313,15 @@ static int open_common(int device, int mode, ort_cuda_session** out) {
     return cuda_fail(e, "cudaStreamCreate");
   }
   s->stream = s->own_stream;
+  e = cudaHostAlloc((void**)&s->err_host, 64, cudaHostAllocMapped);
+  if (e == cudaSuccess) e = cudaHostGetDevicePointer((void**)&s->err_dev, s->err_host, 0);
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(s->own_stream);
+    if (s->err_host) cudaFreeHost(s->err_host);
+    delete s;
+    return cuda_fail(e, "cudaHostAlloc(error word)");
+  }
+  *s->err_host = 0;
   *out = s;
   return ORT_CUDA_OK;
 }
@@ -280,9 +333,10 @@ ORT_CUDA_API int ort_cuda_open(int device, int mode, ort_cuda_session** out) {
 ORT_CUDA_API int ort_cuda_nccl_unique_id(void* id128) {
   ORTC_CHECK(id128, ORT_CUDA_ERR_INVALID_ARG, "id buffer is NULL");
   static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  if (!nccl()) return ORT_CUDA_ERR_NCCL;
   ncclUniqueId id;
-  ncclResult_t r = ncclGetUniqueId(&id);
-  if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, ncclGetErrorString(r));
+  ncclResult_t r = nccl()->GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(ORT_CUDA_ERR_NCCL, nccl()->GetErrorString(r));
   std::memcpy(id128, &id, 128);
   return ORT_CUDA_OK;
 }
@@ -293,6 +347,7 @@ ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void*
              "rank/world out of range");
   ORTC_CHECK(world == 1 || nccl_id128, ORT_CUDA_ERR_INVALID_ARG, "NCCL id is NULL");
   ORTC_CHECK(timeout_ms > 0, ORT_CUDA_ERR_INVALID_ARG, "timeout_ms must be > 0");
+  if (world > 1 && !nccl()) return ORT_CUDA_ERR_NCCL;
   int rc = open_common(device, mode, out);
   if (rc) return rc;
   ort_cuda_session* s = *out;
@@ -305,16 +360,16 @@ ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void*
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
   ncclComm_t comm = nullptr;
-  ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+  ncclResult_t r = nccl()->CommInitRankConfig(&comm, world, id, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
     ort_cuda_close(s);
     *out = nullptr;
-    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    return fail(ORT_CUDA_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + nccl()->GetErrorString(r));
   }
   rc = nccl_wait_ready(comm, timeout_ms);
   if (rc) {
     std::string msg = ort_cuda_last_error();
-    ncclCommAbort(comm);
+    nccl()->CommAbort(comm);
     ort_cuda_close(s);
     *out = nullptr;
     return fail(rc, "NCCL init (rank " + std::to_string(rank) + "/" + std::to_string(world) +
@@ -333,11 +388,14 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   for (void* p : s->allocs) cudaFree(p);
   s->allocs.clear();
   if (s->ws) cudaFree(s->ws);
+  if (s->kscratch) cudaFree(s->kscratch);
+  if (s->kcnt) cudaFree(s->kcnt);
   if (s->pinned) cudaFreeHost(s->pinned);
+  if (s->err_host) cudaFreeHost(s->err_host);
   if (s->nccl) {
-    ncclCommFinalize((ncclComm_t)s->nccl);
+    nccl()->CommFinalize((ncclComm_t)s->nccl);
     nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
-    ncclCommDestroy((ncclComm_t)s->nccl);
+    nccl()->CommDestroy((ncclComm_t)s->nccl);
   }
   if (s->own_stream) cudaStreamDestroy(s->own_stream);
   delete s;
@@ -463,6 +521,13 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
     }
     e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "upload sync"));
+    if (K % 32 == 0 && col_bytes % 16 == 0) {
+      // TMA view for the decode GEMV: uint32 [nl][col_bytes/4], 32 x 512 B boxes.
+      int rc = encode_tma_2d(&w.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT32, w.B, (uint64_t)(col_bytes / 4),
+                             (uint64_t)nl, (uint64_t)col_bytes, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return cleanup(rc);
+      w.tmB_ok = true;
+    }
   }
   auto it = s->weights.find(name);
   if (it != s->weights.end()) {
@@ -696,8 +761,14 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if (mode == ORT_CUDA_MODE_STRICT)
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
-                  const bool gemv_ok = M <= 4 && (w.K % 32) == 0 && aligned16(dA);
-                  if (gemv_ok) return launch_nbits_gemv(w, dA, M, yl, ldy, s->stream, &s->launches);
+                  const bool gemv_ok = M <= 4 && w.tmB_ok && (w.K % 32) == 0 && aligned16(dA);
+                  if (gemv_ok) {
+                    int rc = ensure_kscratch(s, gemv_partial_floats(w.K, w.nl, M) * 4);
+                    if (!rc) rc = ensure_kcnt(s, gemv_counter_words(w.K, w.nl));
+                    if (rc) return rc;
+                    return launch_nbits_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->kcnt,
+                                             s->err_dev, s->sm_count, s->stream, &s->launches);
+                  }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K))
                     return launch_mma_nbits(s, w, dA, M, yl, ldy, mode, s->stream);

@@ -130,9 +130,15 @@ class CudaSession:
         check(_lib.load().ort_cuda_set_mode(self.handle, _lib.MODES[mode]), "ort_cuda_set_mode")
         self.mode = mode
 
-    def set_stream(self, stream_ptr: int) -> None:
-        check(_lib.load().ort_cuda_set_stream(self.handle, stream_ptr or None),
-              "ort_cuda_set_stream")
+    def set_stream(self, stream_ptr: Optional[int]) -> None:
+        """Launch on an existing cudaStream_t.  0 is the legacy default
+        stream (torch's default stream), passed as cudaStreamLegacy; None
+        restores the session's own stream."""
+        if stream_ptr is None:
+            arg = None
+        else:
+            arg = stream_ptr if stream_ptr else 1  # cudaStreamLegacy == (cudaStream_t)0x1
+        check(_lib.load().ort_cuda_set_stream(self.handle, arg), "ort_cuda_set_stream")
 
     def sync(self) -> None:
         check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")
@@ -202,7 +208,13 @@ class CudaSession:
                   fn.__name__)
             return y
         a = np.ascontiguousarray(a, dtype=np.float32)
-        y = np.empty(out_shape, np.float32)
+        if out is not None:
+            if (not isinstance(out, np.ndarray) or out.dtype != np.float32
+                    or not out.flags.c_contiguous or out.size != int(np.prod(out_shape))):
+                raise ValueError("out must be a contiguous float32 array of the output size")
+            y = out
+        else:
+            y = np.empty(out_shape, np.float32)
         check(fn(self.handle, name.encode(), a.ctypes.data, m, *extra, y.ctypes.data,
                  flags | _lib.HOST_IO), fn.__name__)
         del L

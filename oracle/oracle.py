@@ -175,33 +175,6 @@ def matmul(a, b, threads: int = 1) -> np.ndarray:
     return out.reshape(tuple(out_batch) + (m, n))
 
 
-# ---------------------------------------------------------------------------
-# Seeded synthetic inputs (the shapes and distributions of the benchmark
-# configurations; no dataset is involved).
-# ---------------------------------------------------------------------------
-
-def pack_nibbles(q: np.ndarray) -> np.ndarray:
-    """Pack uint4 values [..., 2j] (low nibble) and [..., 2j+1] (high)."""
-    q = q.astype(np.uint8)
-    return (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
-
-
-def make_nbits_weight(rng: np.random.Generator, K: int, N: int, block_size: int,
-                      zero_points: bool, scale_sigma: float = 0.02,
-                      scale_dtype=np.float32, scale_mean: float = 0.0):
-    """Packed uint4 B [N, nb, bs/2] (nibbles uniform 0..15), scales
-    |N(mean, sigma)| [N*nb], optional packed uint4 zero points (flat,
-    low nibble first, uniform 0..15)."""
-    nb = (K + block_size - 1) // block_size
-    q = rng.integers(0, 16, size=(N, nb * block_size), dtype=np.uint8)
-    q[:, K:] = 0
-    B = pack_nibbles(q.reshape(N, nb, block_size))
-    s = rng.standard_normal(N * nb) * scale_sigma + scale_mean
-    if scale_mean == 0.0:
-        s = np.abs(s)
-    scales = s.astype(scale_dtype)
-    zp = None
-    if zero_points:
-        z = rng.integers(0, 16, size=N * nb + (N * nb) % 2, dtype=np.uint8)
-        zp = pack_nibbles(z)
-    return B, scales, zp
+# Seeded synthetic inputs come from the package's workload definitions
+# (data generation only; no arithmetic of the path lives there).
+from onnx_runtime_dart_b200.workloads import make_nbits_weight, pack_nibbles  # noqa: E402,F401
