@@ -73,6 +73,7 @@ SIGNATURES = {
     "ort_cuda_h2d": (_int, [_vp, _vp, _vp, _i64]),
     "ort_cuda_d2h": (_int, [_vp, _vp, _vp, _i64]),
     "ort_cuda_matmul_nbits": (_int, [_vp, _cp, _vp, _i64, _vp, _int]),
+    "ort_cuda_matmul_nbits_noalloc": (_int, [_vp, _cp, _vp, _i64, _vp]),
     "ort_cuda_matmul": (_int, [_vp, _cp, _vp, _i64, _vp, _int]),
     "ort_cuda_gemm": (_int, [_vp, _cp, _vp, _i64, _vp, _i64, _i64, _f, _f, _vp, _int]),
     "ort_cuda_matmul_batched": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _int]),
