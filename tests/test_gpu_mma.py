@@ -1,0 +1,127 @@
+"""tcgen05 MMA modes against the oracle (prefill-sized M).
+
+Bars: MMA_F16 max|dY|/max|Y_ref| <= 2e-3 and cosine >= 0.99999 (the
+stated bf16-MMA tolerance, met with f16 operands).  MMA_BF16 (literal bf16
+operands) is held to the error bf16 rounding produces: 5e-3 / 0.99999.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.conftest import cosine, max_rel
+
+pytestmark = pytest.mark.gpu
+
+F16_TOL, F16_COS = 2e-3, 0.99999
+BF16_TOL, BF16_COS = 5e-3, 0.99999
+
+
+@pytest.fixture(scope="module")
+def sess():
+    from onnx_runtime_dart_b200 import CudaSession
+    s = CudaSession(0, mode="mma_f16")
+    yield s
+    s.close()
+
+
+def _flags(mode):
+    from onnx_runtime_dart_b200 import _lib
+    return _lib.flags_mode(_lib.MODES[mode])
+
+
+def _check(ref, y, mode):
+    tol, cs = (F16_TOL, F16_COS) if mode == "mma_f16" else (BF16_TOL, BF16_COS)
+    assert np.isfinite(y).all()
+    assert max_rel(ref, y) <= tol, max_rel(ref, y)
+    assert cosine(ref, y) >= cs
+
+
+@pytest.mark.parametrize("mode", ["mma_f16", "mma_bf16"])
+@pytest.mark.parametrize("M,K,N", [(1024, 384, 1536), (1024, 1536, 384)])
+def test_cfg2_gemm_mma(sess, mode, M, K, N):
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    c = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    sess.upload_dense("ffn", W, trans_b=True)
+    y = sess.gemm("ffn", A, c, flags=_flags(mode))
+    _check(O.gemm(A, W, c, transB=True, threads=8), y, mode)
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 64, 8), (100, 200, 300), (129, 72, 257), (300, 1000, 520)])
+def test_ragged_shapes_mma(sess, M, K, N):
+    rng = np.random.default_rng(M + K + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = rng.standard_normal((K, N)).astype(np.float32)
+    sess.upload_dense("r", W)
+    y = sess.matmul("r", A, flags=_flags("mma_f16"))
+    _check(O.matmul_kernel(A, W, threads=8), y, "mma_f16")
+
+
+@pytest.mark.parametrize("cshape", [None, (9,), (1, 9), (70, 9), (70, 1)])
+def test_gemm_epilogue_mma(sess, cshape):
+    rng = np.random.default_rng(21)
+    A = rng.standard_normal((70, 40)).astype(np.float32)
+    W = rng.standard_normal((9, 40)).astype(np.float32)
+    C = None if cshape is None else rng.standard_normal(cshape).astype(np.float32)
+    sess.upload_dense("g", W, trans_b=True)
+    y = sess.gemm("g", A, C, alpha=1.5, beta=-0.5, flags=_flags("mma_f16"))
+    _check(O.gemm(A, W, C, alpha=1.5, beta=-0.5, transB=True), y, "mma_f16")
+
+
+def test_gemm_trans_a_mma(sess):
+    rng = np.random.default_rng(22)
+    At = rng.standard_normal((48, 96)).astype(np.float32)  # [K, M]
+    W = rng.standard_normal((48, 33)).astype(np.float32)
+    sess.upload_dense("ta", W)
+    y = sess.gemm("ta", At, None, trans_a=True, flags=_flags("mma_f16"))
+    _check(O.gemm(At, W, None, transA=True), y, "mma_f16")
+
+
+def test_wide_dynamic_range_rows(sess):
+    """Rows scaled by 2^±60: f16's range normalisation keeps them exact."""
+    rng = np.random.default_rng(23)
+    A = rng.standard_normal((128, 256)).astype(np.float32)
+    A[0] *= 2.0 ** 60
+    A[1] *= 2.0 ** -60
+    W = rng.standard_normal((256, 64)).astype(np.float32)
+    sess.upload_dense("dr", W)
+    y = sess.matmul("dr", A, flags=_flags("mma_f16"))
+    ref = O.matmul_kernel(A, W)
+    for r in (0, 1, 2):
+        assert max_rel(ref[r], y[r]) <= F16_TOL
+
+
+@pytest.mark.parametrize("mode", ["mma_f16", "mma_bf16"])
+@pytest.mark.parametrize("M,K,N,bs,zp", [(256, 2048, 1024, 128, False), (256, 1024, 3072, 32, True),
+                                        (200, 4096, 520, 128, True), (128, 2048, 512, 64, True)])
+def test_nbits_prefill_mma(sess, mode, M, K, N, bs, zp):
+    rng = np.random.default_rng(K + N + bs)
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=zp, scale_dtype=np.float16)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("nb", B, s, z, k=K, n=N, block_size=bs)
+    y = sess.matmul_nbits("nb", A, flags=_flags(mode))
+    _check(O.matmul_nbits(A, B, s.astype(np.float32), z, K, N, 4, bs, threads=8), y, mode)
+
+
+def test_nbits_prefill_full_size_vs_torch(sess):
+    """Llama-3-8B down projection (14336 -> 4096) at M=2048 against an fp64
+    torch reference of the dequantised weight."""
+    import torch
+    rng = np.random.default_rng(31)
+    K, N, bs, M = 14336, 4096, 128, 2048
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True, scale_dtype=np.float16)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("big", B, s, z, k=K, n=N, block_size=bs)
+    y = sess.matmul_nbits("big", A, flags=_flags("mma_f16"))
+    dev = torch.device("cuda")
+    nb = K // bs
+    Bt = torch.from_numpy(B).to(dev).reshape(N, nb * bs // 2)
+    q = torch.stack([Bt & 0xF, Bt >> 4], -1).reshape(N, nb, bs).double()
+    zt = torch.from_numpy(z).to(dev)
+    zz = torch.stack([zt & 0xF, zt >> 4], -1).reshape(-1)[:N * nb].reshape(N, nb, 1).double()
+    st = torch.from_numpy(s.astype(np.float32)).to(dev).reshape(N, nb, 1).double()
+    W = ((q - zz) * st).reshape(N, K).float().double()
+    ref = (torch.from_numpy(A).to(dev).double() @ W.T).cpu().numpy()
+    sess.drop_weight("big")
+    _check(ref, y, "mma_f16")
