@@ -40,15 +40,19 @@ struct Weight {
   int64_t K = 0, N = 0;   // logical shape [K, N] of the full weight
   int64_t n0 = 0, nl = 0; // this rank's column range
   int64_t ns = 0;         // padded per-rank column count (all-gather unit)
-  // MatMulNBits
+  // MatMulNBits, in the device layout every kernel reads (see nbits_*):
   int bs = 0, nb = 0;
   bool has_zp = false;
-  uint8_t* B = nullptr;     // [nl][nb*bs/2] packed uint4, low nibble first
-  float* scales = nullptr;  // [nl][nb] fp32
-  uint8_t* zp = nullptr;    // packed uint4, nibble (c*nb + blk), local c
-  // TMA view of B as uint32 [nl rows][col_bytes/4] (valid when tmB_ok).
-  CUtensorMap tmB;
-  bool tmB_ok = false;
+  uint8_t* B = nullptr;      // [nl][nb*bs/2] packed uint4, nibbles of each 32-bit
+                             // word reordered (nbits_nibble below)
+  float* scales = nullptr;   // [nb][s_pitch] fp32 (transposed: block-major)
+  int64_t s_pitch = 0;       // >= nl, multiple of 4
+  uint8_t* zp = nullptr;     // [ceil(nb/2)][z_pitch] bytes: byte (b/2, n) holds
+                             // blocks 2j (low nibble) and 2j+1 of column n
+  int64_t z_pitch = 0;       // >= nl, multiple of 16
+  // TMA views for the tensor-core GEMV (valid when tc_ok)
+  CUtensorMap tmB, tmS, tmZ;
+  bool tc_ok = false;
   // dense fp32 MatMul / Gemm operand, effective [K][nl] row-major
   float* W = nullptr;
   // Lazily built MMA operand: 16-bit [nl_pad][K_pad] K-major plus the
@@ -59,6 +63,31 @@ struct Weight {
   int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
   float* scales16 = nullptr; // nbits MMA: per-(col,blk) scale * 2^-col_exp
 };
+
+// ---- device layout of a MatMulNBits weight ---------------------------------
+// Within each 32-bit word of a column's packed bytes the 8 nibbles (k offsets
+// 0..7 of that word) are stored at bit positions 0,8,16,24,4,12,20,28: k0..k3
+// sit in the low nibbles of bytes 0..3 and k4..k7 in the high nibbles, so
+// (w & 0x0F0F0F0F) and ((w >> 4) & 0x0F0F0F0F) are the int8 values of
+// k0..k3 and k4..k7 in order — the tensor-core GEMV's A operand.
+__host__ __device__ __forceinline__ int nbits_nibble_pos(int i) {
+  return (i & 3) * 8 + (i >> 2) * 4;
+}
+__host__ __device__ __forceinline__ uint32_t nbits_permute_word(uint32_t o) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) w |= ((o >> (4 * i)) & 0xFu) << nbits_nibble_pos(i);
+  return w;
+}
+// q of k offset i (0..7) within a permuted word
+__host__ __device__ __forceinline__ uint32_t nbits_q(uint32_t w, int i) {
+  return (w >> nbits_nibble_pos(i)) & 0xFu;
+}
+// zero point of column n, block b in the transposed nibble table
+__host__ __device__ __forceinline__ uint32_t nbits_zp(const uint8_t* zp, int64_t z_pitch,
+                                                      int64_t n, int64_t b) {
+  return (zp[(b >> 1) * z_pitch + n] >> ((b & 1) * 4)) & 0xFu;
+}
 
 }  // namespace ortc
 
@@ -82,11 +111,6 @@ struct ort_cuda_session {
   // grow-only kernel scratch for split-K partials (no initial value needed)
   void* kscratch = nullptr;
   size_t kscratch_bytes = 0;
-  // grow-only arrival counters, zero between calls (kernels reset the
-  // counters they use; re-zeroed after a kernel reported an error)
-  unsigned* kcnt = nullptr;
-  size_t kcnt_words = 0;
-  bool kcnt_dirty = false;
   // host-mapped error word kernels write when a bounded wait gives up
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -99,7 +123,6 @@ namespace ortc {
 int ensure_ws(ort_cuda_session* s, size_t bytes);
 int ensure_pinned(ort_cuda_session* s, size_t bytes);
 int ensure_kscratch(ort_cuda_session* s, size_t bytes);
-int ensure_kcnt(ort_cuda_session* s, size_t words);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: a 2-D
 // row-major tensor [d1][d0] with row pitch stride1 bytes, box b0 x b1.
@@ -110,13 +133,14 @@ int encode_tma_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 // ---- kernel launchers (each returns an ORT status) -----------------------
 // All pointers are device pointers; launches go to `st`.
 
-// Y[M, ldy] (columns [0, nl)) = A[M, K] . dequant(W); exact (FFMA) mode.
-int launch_nbits_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
-                      float* partials, unsigned* counters, int* err, int sm_count,
-                      cudaStream_t st, int64_t* launches);
-// Split-K scratch of the GEMV: partial floats and arrival-counter words.
-size_t gemv_partial_floats(int64_t K, int64_t nl, int64_t M);
-size_t gemv_counter_words(int64_t K, int64_t nl);
+// Decode GEMV on tensor cores, exact mode: Y[M, ldy] (columns [0, nl)) =
+// A[M, K] . dequant(W) for M <= 8 (tc_gemv_ok).  `partials` holds
+// tc_gemv_partial_floats() floats (no initial value needed).
+int prepare_nbits_tc(Weight& w);
+bool tc_gemv_ok(const Weight& w, int64_t M);
+size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count);
+int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
+                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches);
 // General CUDA-core tiled GEMM over an nbits or dense weight (any M).
 // strict=true reproduces the reference's rounding bit for bit.
 int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,
@@ -127,6 +151,8 @@ int launch_simt_batched(const float* A, const float* B, int64_t batch, int64_t m
                         int64_t n, int64_t b_batch_stride, float* Y, bool strict,
                         cudaStream_t st, int64_t* launches);
 // Upload-time device prepack helpers.
+int launch_permute_nibbles(const uint32_t* in, uint32_t* out, int64_t nwords, cudaStream_t st,
+                           int64_t* launches);
 int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,
                          int64_t* launches);
 int launch_transpose(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st,

@@ -26,10 +26,10 @@ __device__ __forceinline__ float mac(float acc, float a, float b) {
 }
 
 struct NbitsSrc {
-  const uint8_t* B;
-  const float* S;
-  const uint8_t* Z;
-  int64_t col_bytes;
+  const uint8_t* B;   // permuted-nibble packed columns
+  const float* S;     // [nb][s_pitch]
+  const uint8_t* Z;   // [ceil(nb/2)][z_pitch] or null
+  int64_t col_bytes, s_pitch, z_pitch;
   int nb, bs;
 };
 struct DenseSrc {
@@ -53,14 +53,9 @@ __device__ __forceinline__ void load_w_tile(float (&Ws)[BK][BN + 4], const Nbits
       const int kk = kw + i;
       const int blk = kk / src.bs;
       if (kk < K) {
-        const int64_t si = (int64_t)n * src.nb + blk;
-        const float scale = __ldg(src.S + si);
-        float z = 8.0f;
-        if (src.Z) {
-          const uint32_t byte = __ldg(src.Z + (si >> 1));
-          z = (float)((byte >> ((si & 1) * 4)) & 0xFu);
-        }
-        const float q = (float)((w >> (4 * i)) & 0xFu);
+        const float scale = __ldg(src.S + (int64_t)blk * src.s_pitch + n);
+        const float z = src.Z ? (float)nbits_zp(src.Z, src.z_pitch, n, blk) : 8.0f;
+        const float q = (float)nbits_q(w, i);
         v[i] = __fmul_rn(__fsub_rn(q, z), scale);
       } else {
         v[i] = 0.0f;
@@ -186,13 +181,11 @@ __global__ void strict_tail_kernel<NbitsSrc>(const float* __restrict__ A, int K,
   if (n >= col_hi) return;
   double acc = 0.0;
   for (int k = 0; k < K; k++) {
-    const int blk = k / src.bs, j = k % src.bs;
-    const int64_t si = (int64_t)n * src.nb + blk;
-    const uint8_t byte = src.B[(int64_t)n * src.col_bytes + (int64_t)blk * (src.bs / 2) + (j >> 1)];
-    const float q = (float)((j & 1) ? (byte >> 4) : (byte & 0xF));
-    float z = 8.0f;
-    if (src.Z) z = (float)((src.Z[si >> 1] >> ((si & 1) * 4)) & 0xF);
-    const float w = __fmul_rn(__fsub_rn(q, z), src.S[si]);
+    const int blk = k / src.bs;
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(src.B + (int64_t)n * src.col_bytes + ((k >> 3) << 2));
+    const float q = (float)nbits_q(word, k & 7);
+    const float z = src.Z ? (float)nbits_zp(src.Z, src.z_pitch, n, blk) : 8.0f;
+    const float w = __fmul_rn(__fsub_rn(q, z), src.S[(int64_t)blk * src.s_pitch + n]);
     acc = __dadd_rn(acc, __dmul_rn((double)A[k], (double)w));
   }
   Y[n] = (float)acc;
@@ -216,6 +209,13 @@ __global__ void strict_tail_kernel<DenseSrc>(const float* __restrict__ A, int K,
     v = __fadd_rn(v, c);
   }
   Y[n] = v;
+}
+
+__global__ void permute_nibbles_kernel(const uint32_t* __restrict__ in, uint32_t* __restrict__ out,
+                                       int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = nbits_permute_word(in[i]);
 }
 
 __global__ void half_to_float_kernel(const uint16_t* __restrict__ h, float* __restrict__ out,
@@ -283,7 +283,7 @@ int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, fl
     tail_lo = (int)(g_lo < 0 ? 0 : (g_lo > N ? N : g_lo));
   }
   if (w.kind == W_NBITS) {
-    NbitsSrc src{w.B, w.scales, w.zp, (int64_t)w.nb * w.bs / 2, w.nb, w.bs};
+    NbitsSrc src{w.B, w.scales, w.zp, (int64_t)w.nb * w.bs / 2, w.s_pitch, w.z_pitch, w.nb, w.bs};
     rc = strict ? run_simt<true>(A, M, K, tail_lo, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches)
                 : run_simt<false>(A, M, K, N, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches);
     if (rc == ORT_CUDA_OK && tail_lo < N) {
@@ -330,6 +330,17 @@ int launch_simt_batched(const float* A, const float* B, int64_t batch, int64_t m
     }
   }
   return rc;
+}
+
+int launch_permute_nibbles(const uint32_t* in, uint32_t* out, int64_t nwords, cudaStream_t st,
+                           int64_t* launches) {
+  if (nwords == 0) return ORT_CUDA_OK;
+  int64_t blocks = (nwords + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  permute_nibbles_kernel<<<(unsigned)blocks, 256, 0, st>>>(in, out, nwords);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
 }
 
 int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,

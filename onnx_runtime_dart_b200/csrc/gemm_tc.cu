@@ -253,37 +253,38 @@ __global__ void w16_dense_kernel(const float* __restrict__ W, int K, int nl,
 
 // int4 weight -> 16-bit [nl][K]: W = (q - zp) * scale (fp32, as the
 // reference rounds it), then * 2^-f_n and rounded to 16 bits.
-__global__ void nbits_col_exp_kernel(const float* __restrict__ S, int nb, int nl,
+__global__ void nbits_col_exp_kernel(const float* __restrict__ S, int64_t s_pitch, int nb, int nl,
                                      int* __restrict__ col_exp) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= nl) return;
   float mx = 0.0f;
-  for (int b = 0; b < nb; b++) mx = fmaxf(mx, fabsf(S[(int64_t)n * nb + b]));
+  for (int b = 0; b < nb; b++) mx = fmaxf(mx, fabsf(S[(int64_t)b * s_pitch + n]));
   col_exp[n] = norm_exp(15.0f * mx);
 }
 
 template <bool BF16>
 __global__ void w16_nbits_kernel(const uint8_t* __restrict__ B, const float* __restrict__ S,
-                                 const uint8_t* __restrict__ Z, int K, int nb, int bs, int nl,
-                                 const int* __restrict__ col_exp, uint16_t* __restrict__ out) {
+                                 int64_t s_pitch, const uint8_t* __restrict__ Z, int64_t z_pitch,
+                                 int K, int nb, int bs, int nl, const int* __restrict__ col_exp,
+                                 uint16_t* __restrict__ out) {
   const int64_t col_bytes = (int64_t)nb * bs / 2;
-  const int64_t total = (int64_t)nl * ((K + 1) / 2);
+  const int64_t wpc = (K + 7) / 8;  // 32-bit words per column that hold k < K
+  const int64_t total = (int64_t)nl * wpc;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / ((K + 1) / 2);
-    const int kp = (int)(i % ((K + 1) / 2));  // byte index within the column
-    const int k = kp * 2;
-    const int blk = k / bs;
-    const int64_t si = n * nb + blk;
-    const uint8_t byte = B[n * col_bytes + (int64_t)blk * (bs / 2) + ((k % bs) >> 1)];
-    float z = 8.0f;
-    if (Z) z = (float)((Z[si >> 1] >> ((si & 1) * 4)) & 0xF);
-    const float s = S[si];
+    const int64_t n = i / wpc;
+    const int k0 = (int)(i % wpc) * 8;
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(B + n * col_bytes + k0 / 2);
     const int e = BF16 ? 0 : col_exp[n];
-    const float w0 = __fmul_rn((float)(byte & 0xF) - z, s);
-    const float w1 = __fmul_rn((float)(byte >> 4) - z, s);
-    out[n * K + k] = to16<BF16>(BF16 ? w0 : scale_pow2(w0, -e));
-    if (k + 1 < K) out[n * K + k + 1] = to16<BF16>(BF16 ? w1 : scale_pow2(w1, -e));
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int k = k0 + j;
+      if (k >= K) break;
+      const int blk = k / bs;
+      const float z = Z ? (float)nbits_zp(Z, z_pitch, n, blk) : 8.0f;
+      const float w = __fmul_rn((float)nbits_q(word, j) - z, S[(int64_t)blk * s_pitch + n]);
+      out[n * K + k] = to16<BF16>(BF16 ? w : scale_pow2(w, -e));
+    }
   }
 }
 
@@ -404,18 +405,19 @@ int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
   uint16_t* W16 = (uint16_t*)((char*)s->kscratch + a_bytes);
   int* cexp = (int*)((char*)s->kscratch + a_bytes + w_bytes);
   if (!bf16) {
-    nbits_col_exp_kernel<<<(unsigned)((nl + 255) / 256), 256, 0, st>>>(w.scales, w.nb, (int)nl, cexp);
+    nbits_col_exp_kernel<<<(unsigned)((nl + 255) / 256), 256, 0, st>>>(w.scales, w.s_pitch, w.nb,
+                                                                        (int)nl, cexp);
     s->launches++;
   }
-  const int64_t total = nl * ((K + 1) / 2);
+  const int64_t total = nl * ((K + 7) / 8);
   unsigned blocks = (unsigned)((total + 255) / 256);
   if (blocks > (unsigned)s->sm_count * 16) blocks = (unsigned)s->sm_count * 16;
   if (bf16)
-    w16_nbits_kernel<true><<<blocks, 256, 0, st>>>(w.B, w.scales, w.zp, (int)K, w.nb, w.bs, (int)nl,
-                                                  cexp, W16);
+    w16_nbits_kernel<true><<<blocks, 256, 0, st>>>(w.B, w.scales, w.s_pitch, w.zp, w.z_pitch, (int)K,
+                                                  w.nb, w.bs, (int)nl, cexp, W16);
   else
-    w16_nbits_kernel<false><<<blocks, 256, 0, st>>>(w.B, w.scales, w.zp, (int)K, w.nb, w.bs,
-                                                   (int)nl, cexp, W16);
+    w16_nbits_kernel<false><<<blocks, 256, 0, st>>>(w.B, w.scales, w.s_pitch, w.zp, w.z_pitch,
+                                                   (int)K, w.nb, w.bs, (int)nl, cexp, W16);
   ORTC_CUDA(cudaGetLastError());
   s->launches++;
   return launch_gemm(s, A16, rexp, M, W16, cexp, nl, K, bf16, Y, ldy, 1.0f, 1.0f, nullptr, 0, 0, 0,

@@ -1,0 +1,724 @@
+// int4 block-quantised GEMV for decode (M <= 8) on tcgen05 tensor cores
+// (kind::i8), exact integer products.
+//
+// Replaces, for small M, the reference's per-call dequantisation of all of B
+// into an fp32 [K x N] buffer followed by matmulKernel's _gemv
+// (onnx_qlinear_ops.dart:127-154, gemm_kernel_simd.dart:183-246).  Packed B
+// streams from HBM exactly once.
+//
+// Arithmetic.  Y[m,n] = sum_b s[n,b] * sum_{k in b} a[m,k] * (q[k,n] - z[n,b]).
+// Each activation row is turned into fixed point, X = rint(a * 2^S_m) with
+// |X| <= 2^22 (S_m per row, from the row's largest magnitude), and split into
+// three balanced base-256 digits X = c2*2^16 + c1*2^8 + c0.  The tensor core
+// multiplies q (0..15) by each digit and accumulates in int32 with no
+// rounding at all; the zero point enters as z * sum_k c_t, the fp32 block
+// scale once per block on the CUDA cores, and 2^-S_m at the end.  The only
+// roundings are the fixed-point step of a (2^-23 of the row's largest
+// magnitude) and the fp32 additions of the epilogue.
+//
+// MMA orientation:
+//   D[n, j] (128 TMEM lanes = 128 weight columns; NM = 16 or 32 columns j)
+//     += Q[n, k..k+32) (A operand, int8, in TMEM) . X[j, k..k+32) (B, smem)
+//   X is block-diagonal: within a region of G quantisation blocks, block
+//   slot g owns columns j = (g*M + m)*3 + t (row m, digit t), so every block
+//   of the region accumulates into its own D columns.  One MMA covers 128
+//   columns x 32 k = 4096 weights.
+//
+// Roles (448 threads, one CTA per SM):
+//   warp 12    TMA producer: per work item (128 columns x 512 k) the packed
+//              tile (2 boxes, 128-byte swizzle), its scales and zero points,
+//              into a shared-memory ring of up to 6 stages.
+//   warps 0-7  dequantisers, 2 groups x 4 lane quarters: thread (quarter q,
+//              lane l) owns weight column n = 32q + l.  Per 32-k stage: one
+//              conflict-free 16-byte shared load and two masks and a shift per
+//              8 weights turn nibbles into int8 bytes, then tcgen05.st of 8
+//              TMEM columns.  They also build X for each chunk.
+//   warp 13    TMEM allocator; an elect.sync leader issues one MMA per stage
+//              (A from TMEM) and tcgen05.commit frees A slots, X buffers and
+//              D buffers.
+//   warps 8-11 epilogue: tcgen05.ld of D, zero points, block scales, and the
+//              chunk partial of each column.
+// Decomposition: tile-major (a CTA owns whole 128-column tiles and loops
+// over the 512-k chunks, adding chunk partials in chunk order in shared
+// memory) when the tiles spread evenly over the SMs, else split-K (CTAs own
+// one chunk; a second kernel adds the chunk partials in chunk order).  Both
+// form ((0 + p_0) + p_1) + ... from identical partials, and the partials
+// depend on K only, so results never depend on N or on which columns a GPU
+// owns: N-sharded results are bitwise equal to 1-GPU results.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace ortc {
+namespace {
+
+constexpr int kTile = 128;          // weight columns per item (MMA M)
+constexpr int kChunkK = 512;        // k per item
+constexpr int kItemStages = 16;     // 32-k stages per item, one MMA each
+constexpr int kAItems = 2;          // TMEM A ring: two items of 16 x 8 columns
+constexpr int kMaxBStages = 6;      // shared-memory ring depth (runtime <= 6)
+constexpr int kDeWarps = 8;         // dequantisers: 2 groups x 4 lane quarters
+constexpr int kEpiWarp0 = 8;        // epilogue: 2 groups of 4 warps, 8..15
+constexpr int kEpiWarps = 8;
+constexpr int kProducerWarp = 16, kMmaWarp = 17;
+constexpr int kThreadsTC = 18 * 32;
+constexpr int kMinBs = 32;          // one MMA never spans two blocks
+constexpr uint32_t kPackedBytes = kTile * kChunkK / 2;  // 32 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAItemCols = kItemStages * 8;        // 128 columns per item
+constexpr uint32_t kDCol = kAItems * kAItemCols;         // D starts at column 256
+constexpr uint32_t kDCols = kTmemCols - kDCol;          // 256 columns for D
+constexpr int kMaxBpi = kChunkK / kMinBs;               // blocks per item
+constexpr uint32_t kXBytesMax = 32 * kChunkK;           // X for NM = 32
+constexpr uint32_t kCsumBytes = kMaxBpi * 8 * 3 * 4;    // digit sums [bpi][M][3]
+constexpr uint32_t kXBufBytes = kXBytesMax + ((kCsumBytes + 1023) & ~1023u);
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr int kNonFinite = -100000;  // S_m of a row holding an inf or NaN
+
+// Compile-time shape of the X operand for M rows.
+template <int M>
+struct XShape {
+  static constexpr int G = M == 1 ? 5 : (M == 2 ? 2 : 1);     // blocks per D region
+  static constexpr int NM = (3 * M * G <= 16) ? 16 : 32;      // MMA N
+};
+
+struct TcParams {
+  const float* A;
+  float* Y;
+  float* part;   // split-K mode: [nch][M][tiles*128] chunk partials
+  int* err;
+  int64_t ldy;
+  int N, K, bs, nch, tiles;
+  int tile_major;  // 1: a CTA loops over all chunks of its tiles
+  int grid_tiles;  // tile-major: tiles t = blockIdx.x + i*grid_tiles
+  int tg;          // tile-major: tiles per group (y accumulators in smem)
+  int cpc;         // split-K: CTAs per chunk
+  int bpi, regions, has_zp, nbst;
+  int nd;          // D buffers: 2, or 1 when an item needs more than 128 columns
+  uint32_t dstride;
+  // Per 32-k stage of an item: D column offset of its region and whether it
+  // accumulates (bit st of acc_mask).  Computed on the host so the issuing
+  // thread does no integer division.
+  uint32_t op_d[kItemStages];
+  uint32_t acc_mask;
+  uint32_t stage_bytes, stage_tx, s_off, z_off, yacc_off;
+};
+
+// Calls f(tile, chunk, tile_in_group) for this CTA's work items, in the
+// order every role of the CTA follows; stops early when f returns false.
+template <typename F>
+__device__ __forceinline__ void for_each_item(const TcParams& p, F&& f) {
+  if (p.tile_major) {
+    const int span = p.grid_tiles * p.tg;
+    for (int g0 = blockIdx.x; g0 < p.tiles; g0 += span)
+      for (int c = 0; c < p.nch; c++)
+        for (int i = 0; i < p.tg; i++) {
+          const int t = g0 + i * p.grid_tiles;
+          if (t >= p.tiles) break;
+          if (!f(t, c, i)) return;
+        }
+  } else {
+    const int c = blockIdx.x % p.nch;
+    for (int t = blockIdx.x / p.nch; t < p.tiles; t += p.cpc)
+      if (!f(t, c, 0)) return;
+  }
+}
+
+// Bounded barrier among a fixed set of warps: every participating warp
+// arrives once (lane 0) and all lanes wait for the phase to complete.
+__device__ __forceinline__ bool warp_group_sync(uint64_t* bar, uint32_t& phase, int* err) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase);
+  phase ^= 1;
+  if (!ok) record_error(err, KERR_WAIT_FULL);
+  return ok;
+}
+
+__device__ __forceinline__ float pow2f(int e) {
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+// v * 2^e for |e| up to a few hundred, exact unless the result leaves the
+// normal range.
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+  while (e > 100) { v *= pow2f(100); e -= 100; }
+  while (e < -100) { v *= pow2f(-100); e += 100; }
+  return v * pow2f(e);
+}
+
+// X (int8, K-major, 128-byte swizzle): 128-k atoms of NM rows x 128 bytes,
+// 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint32_t x_addr(uint32_t base, int nm, int j, int k) {
+  const int atom = k >> 7, kin = k & 127, r = j & 7;
+  return base + atom * (nm * 128) + (j >> 3) * 1024 + r * 128 + (((kin >> 4) ^ r) << 4) +
+         (kin & 15);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
+                   const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
+  constexpr int G = XShape<M>::G, NM = XShape<M>::NM;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* Xs = smem;  // two buffers, each X then the digit sums
+  uint8_t* Bs = smem + 2 * kXBufBytes;
+  float* yacc = reinterpret_cast<float*>(smem + p.yacc_off);  // [tg][M][128]
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(
+      smem + p.yacc_off + (p.tile_major ? p.tg * M * kTile * 4 : 0));
+  uint64_t* bempty = bfull + kMaxBStages;
+  // ready[h]: item j = 2p + h may be issued (phase p): its A is written (8
+  // dequantiser warps) and its D buffer is free (4 epilogue warps, after
+  // reading item j - nd).  One barrier, so the issuer waits once per item.
+  uint64_t* ready = bempty + kMaxBStages;
+  uint64_t* aempty = ready + kAItems;      // [2] an item's A consumed (MMA commit)
+  uint64_t* dfull = aempty + kAItems;      // [2] an item's D complete (MMA commit)
+  uint64_t* xfull = dfull + 2;    // [2] X buffer written (8 dequantiser warps)
+  uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 4 epilogue warps)
+  uint64_t* fin = xempty + 2;
+  uint64_t* eready = fin + 1;     // row exponents written, X buffers zeroed
+  uint64_t* xsync = eready + 1;   // dequantisers, inside an X build
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xsync + 1);
+  int* e_s = reinterpret_cast<int*>(tmem_slot + 1);  // [8]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMaxBStages; s++) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], kDeWarps + 4);
+    }
+    for (int h = 0; h < kAItems; h++) {
+      mbar_init(&ready[h], kDeWarps + 4);
+      mbar_init(&aempty[h], 1);
+    }
+    for (int d = 0; d < 2; d++) {
+      mbar_init(&dfull[d], 1);
+      mbar_init(&xfull[d], kDeWarps);
+      mbar_init(&xempty[d], 1 + kEpiWarps);
+    }
+    mbar_init(fin, 1);
+    mbar_init(eready, kDeWarps);
+    mbar_init(xsync, kDeWarps);
+    fence_mbarrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmB);
+      prefetch_tensormap(&tmS);
+      if (p.has_zp) prefetch_tensormap(&tmZ);
+      const uint64_t pol = policy_evict_first();
+      int j = 0, armed[kMaxBStages];
+      for (int s = 0; s < kMaxBStages; s++) armed[s] = -1;
+      bool ok = true;
+      for_each_item(p, [&](int tile, int chunk, int) {
+        const int bst = j % p.nbst;
+        const uint32_t ph = (j / p.nbst) & 1;
+        if (!mbar_wait(&bempty[bst], ph ^ 1)) {
+          record_error(p.err, KERR_WAIT_EMPTY);
+          return ok = false;
+        }
+        uint8_t* st = Bs + bst * p.stage_bytes;
+        armed[bst] = (int)ph;
+        mbar_arrive_expect_tx(&bfull[bst], p.stage_tx);
+        const int first_b = chunk * p.bpi;
+        tma_load_2d_hint(st, &tmB, &bfull[bst], chunk * 256, tile * kTile, pol);
+        tma_load_2d_hint(st + 16384, &tmB, &bfull[bst], chunk * 256 + 128, tile * kTile, pol);
+        tma_load_2d(st + p.s_off, &tmS, &bfull[bst], tile * kTile, first_b);
+        if (p.has_zp) tma_load_2d(st + p.z_off, &tmZ, &bfull[bst], tile * kTile, first_b >> 1);
+        j++;
+        return true;
+      });
+      if (!ok)
+        for (int s = 0; s < p.nbst; s++)
+          if (armed[s] >= 0 && !mbar_wait(&bfull[s], (uint32_t)armed[s]))
+            record_error(p.err, KERR_WAIT_DRAIN);
+    }
+  } else if (warp == kMmaWarp) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_i8(128, NM);
+      int j = 0, cur = -1, nbuild = 0;
+      for_each_item(p, [&](int, int chunk, int) {
+        if (chunk != cur) {
+          if (cur >= 0) mma_commit(&xempty[(nbuild - 1) & 1]);  // X free once its MMAs end
+          if (!mbar_wait(&xfull[nbuild & 1], (nbuild >> 1) & 1)) {
+            record_error(p.err, KERR_WAIT_FULL);
+            return false;
+          }
+          cur = chunk;
+          nbuild++;
+        }
+        const uint32_t xb = smem_u32(Xs + ((nbuild - 1) & 1) * kXBufBytes);
+        const int d = j % p.nd;
+        const uint32_t dbase = tmem + kDCol + d * p.dstride;
+        // One wait per item: a wait on the issuing thread stalls behind the
+        // MMAs still in flight, so it is paid once per 16 MMAs.
+        const int h = j % kAItems;
+        if (!mbar_wait(&ready[h], (j / kAItems) & 1)) {
+          record_error(p.err, KERR_WAIT_FULL);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t abase = tmem + h * kAItemCols;
+        const uint64_t xd0 = smem_desc_sw128(xb);
+#pragma unroll
+        for (int st = 0; st < kItemStages; st++) {
+          // X atom (st / 4), 32-byte k step (st % 4) inside the swizzle atom
+          const uint32_t xoff = ((st >> 2) * (NM * 128) + (st & 3) * 32) >> 4;
+          mma_i8_ts(dbase + p.op_d[st], abase + st * 8, xd0 + xoff, idesc, (p.acc_mask >> st) & 1u);
+        }
+        mma_commit(&aempty[h]);
+        mma_commit(&dfull[d]);
+        j++;
+        return true;
+      });
+      mma_commit(fin);
+      if (!mbar_wait(fin, 0)) record_error(p.err, KERR_WAIT_MMA);
+    }
+    __syncwarp();
+  } else if (warp < kDeWarps) {
+    // ---------------- dequantisers (and X builds) ----------------
+    const int q = warp & 3, grp = warp >> 2;
+    const int nl = q * 32 + lane;  // column within the tile = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    // Row exponents over all of K: |rint(a * 2^S_m)| <= 2^22.
+    if (warp < M) {
+      float mx = 0.0f;
+      bool finite = true;
+      for (int k = lane; k < p.K; k += 32) {
+        const float a = p.A[(int64_t)warp * p.K + k];
+        finite = finite && isfinite(a);
+        mx = fmaxf(mx, fabsf(a));
+      }
+      finite = __all_sync(0xffffffffu, finite);
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      int S = 0;
+      if (!finite) {
+        S = kNonFinite;
+      } else if (mx > 0.0f) {
+        int ex;
+        frexpf(mx, &ex);  // mx < 2^ex
+        S = 22 - ex;
+      }
+      if (lane == 0) e_s[warp] = S;
+    }
+    // Zero both X buffers once: the non-zero pattern is the same for every
+    // chunk, so each build rewrites only those entries.
+    for (int i = threadIdx.x; i < 2 * (int)kXBufBytes / 16; i += kDeWarps * 32)
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
+                   : "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(eready);
+    bool ok = mbar_wait(eready, 0);
+    if (!ok) record_error(p.err, KERR_WAIT_FULL);
+    uint32_t xph = 0;
+
+    int j = 0, cur = -1, nbuild = 0;
+    for_each_item(p, [&](int, int chunk, int) {
+      if (!ok) return false;
+      if (chunk != cur) {
+        // X and the digit sums of this chunk, into buffer nbuild & 1.
+        const int xbuf = nbuild & 1;
+        if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
+          record_error(p.err, KERR_WAIT_EMPTY);
+          return ok = false;
+        }
+        uint8_t* xbase = Xs + xbuf * kXBufBytes;
+        int* csum = reinterpret_cast<int*>(xbase + kXBytesMax);  // [bpi][M][3]
+        for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
+        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        const uint32_t xb = smem_u32(xbase);
+        const int k0 = chunk * kChunkK;
+        for (int u = threadIdx.x; u < M * (kChunkK / 4); u += kDeWarps * 32) {
+          const int m = u / (kChunkK / 4), k = (u % (kChunkK / 4)) * 4;
+          const int bl = k / p.bs, slot = bl % G, S = e_s[m];
+          uint32_t w0 = 0, w1 = 0, w2 = 0;
+          int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+          for (int v = 0; v < 4; v++) {
+            const int kk = k0 + k + v;
+            int X = 0;
+            if (kk < p.K && S != kNonFinite)
+              X = __float2int_rn(scale_pow2(p.A[(int64_t)m * p.K + kk], S));
+            // balanced base-256 digits: X = c2*65536 + c1*256 + c0, each in [-128, 127]
+            const int c0 = ((X + 128) & 255) - 128;
+            const int X1 = (X - c0) >> 8;
+            const int c1 = ((X1 + 128) & 255) - 128;
+            const int c2 = (X1 - c1) >> 8;
+            w0 |= (uint32_t)(c0 & 255) << (8 * v);
+            w1 |= (uint32_t)(c1 & 255) << (8 * v);
+            w2 |= (uint32_t)(c2 & 255) << (8 * v);
+            s0 += c0;
+            s1 += c1;
+            s2 += c2;
+          }
+          const int jr = (slot * M + m) * 3;
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
+                       : "memory");
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
+                       : "memory");
+          int* cs = csum + (bl * M + m) * 3;
+          atomicAdd(cs + 0, s0);
+          atomicAdd(cs + 1, s1);
+          atomicAdd(cs + 2, s2);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xfull[xbuf]);
+        cur = chunk;
+        nbuild++;
+      }
+      const int bst = j % p.nbst;
+      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1)) {
+        record_error(p.err, KERR_WAIT_FULL);
+        return ok = false;
+      }
+      const uint32_t sB = smem_u32(Bs + bst * p.stage_bytes);
+      const int h = j % kAItems;
+      if (!mbar_wait(&aempty[h], ((j / kAItems) & 1) ^ 1)) {
+        record_error(p.err, KERR_WAIT_EMPTY);
+        return ok = false;
+      }
+      tc_fence_after();
+      const uint32_t abase = tmem + lane_addr + h * kAItemCols;
+#pragma unroll
+      for (int i = 0; i < kItemStages / 2; i++) {
+        const int s = 2 * i + grp;
+        // 16 bytes = 32 k of column nl: words hold k 0-7, 8-15, 16-23, 24-31;
+        // low nibbles of a word's bytes are its first 4 k, high nibbles the next 4.
+        const uint4 w4 = lds128(sB + (s >> 3) * 16384 + nl * 128 + (((s & 7) ^ (nl & 7)) << 4));
+        const uint4 lo = make_uint4(w4.x & 0x0F0F0F0Fu, (w4.x >> 4) & 0x0F0F0F0Fu,
+                                    w4.y & 0x0F0F0F0Fu, (w4.y >> 4) & 0x0F0F0F0Fu);
+        const uint4 hi = make_uint4(w4.z & 0x0F0F0F0Fu, (w4.z >> 4) & 0x0F0F0F0Fu,
+                                    w4.w & 0x0F0F0F0Fu, (w4.w >> 4) & 0x0F0F0F0Fu);
+        tmem_st8(abase + s * 8, lo, hi);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[h]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bempty[bst]);
+      j++;
+      return true;
+    });
+  } else if (warp < kEpiWarp0 + kEpiWarps) {
+    // ---------------- epilogue ----------------
+    // Two groups share the items.  Tile-major: a tile's items always go to
+    // the group of its tile-in-group parity, so its chunk sums in shared
+    // memory stay in chunk order; split-K: items alternate.
+    const int q = warp & 3, egrp = (warp - kEpiWarp0) >> 2;
+    const int nl = q * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    // the first nd items find their D buffers free
+    if (lane == 0 && egrp == 0)
+      for (int e = 0; e < p.nd; e++) mbar_arrive(&ready[e]);
+    bool ok = mbar_wait(eready, 0);
+    if (!ok) record_error(p.err, KERR_WAIT_FULL);
+    int S_m[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) S_m[m] = e_s[m];
+    int j = 0, cur = -1, nbuild = 0;
+    for_each_item(p, [&](int tile, int chunk, int tig) {
+      if (!ok) return false;
+      if (chunk != cur) {
+        if (cur >= 0) {  // done with the previous buffer's digit sums
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&xempty[(nbuild - 1) & 1]);
+        }
+        if (!mbar_wait(&xfull[nbuild & 1], (nbuild >> 1) & 1)) {
+          record_error(p.err, KERR_WAIT_FULL);
+          return ok = false;
+        }
+        cur = chunk;
+        nbuild++;
+      }
+      if (((p.tile_major ? tig : j) & 1) != egrp) {
+        j++;
+        return true;
+      }
+      const int* csum =
+          reinterpret_cast<const int*>(Xs + ((nbuild - 1) & 1) * kXBufBytes + kXBytesMax);
+      const int bst = j % p.nbst, d = j % p.nd;
+      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) || !mbar_wait(&dfull[d], (j / p.nd) & 1)) {
+        record_error(p.err, KERR_WAIT_MMA);
+        return ok = false;
+      }
+      tc_fence_after();
+      float y[M];
+#pragma unroll
+      for (int m = 0; m < M; m++) y[m] = 0.0f;
+      const uint8_t* stg = Bs + bst * p.stage_bytes;
+      const float* stile = reinterpret_cast<const float*>(stg + p.s_off);
+      const int first_b = chunk * p.bpi;
+      const uint32_t dcol = tmem + lane_addr + kDCol + d * p.dstride;
+      for (int rg = 0; rg < p.regions; rg++) {
+        uint32_t v[NM];
+        if constexpr (NM == 16)
+          tmem_ld16(dcol + rg * NM, v);
+        else
+          tmem_ld32(dcol + rg * NM, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int slot = 0; slot < G; slot++) {
+          const int b = rg * G + slot;
+          if (b < p.bpi) {
+            int z = 8;
+            if (p.has_zp) {
+              const int bg = first_b + b;
+              const uint32_t zb = stg[p.z_off + ((bg >> 1) - (first_b >> 1)) * kTile + nl];
+              z = (bg & 1) ? (int)(zb >> 4) : (int)(zb & 0xF);
+            }
+            const float sc = stile[b * kTile + nl];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+              const int c = (slot * M + m) * 3;
+              const int* cs = csum + (b * M + m) * 3;
+              const int d0 = (int)v[c] - z * cs[0];
+              const int d1 = (int)v[c + 1] - z * cs[1];
+              const int d2 = (int)v[c + 2] - z * cs[2];
+              const float val = ((float)d2 * 65536.0f + (float)d1 * 256.0f) + (float)d0;
+              y[m] = fmaf(sc, val, y[m]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&ready[(j + p.nd) % kAItems]);  // D buffer d free for item j + nd
+        mbar_arrive(&bempty[bst]);
+      }
+      j++;
+      float part[M];
+#pragma unroll
+      for (int m = 0; m < M; m++)
+        part[m] = S_m[m] == kNonFinite ? __int_as_float(0x7fc00000) : scale_pow2(y[m], -S_m[m]);
+      const int n = tile * kTile + nl;
+      if (p.tile_major) {
+        // chunk partials summed in chunk order: ((0 + p0) + p1) + ...
+        float* ya = yacc + (size_t)tig * M * kTile;
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+          const float acc = chunk == 0 ? 0.0f + part[m] : ya[m * kTile + nl] + part[m];
+          ya[m * kTile + nl] = acc;
+          if (chunk == p.nch - 1 && n < p.N) p.Y[m * p.ldy + n] = acc;
+        }
+      } else {
+        const int64_t npad = (int64_t)p.tiles * kTile;
+#pragma unroll
+        for (int m = 0; m < M; m++) p.part[((int64_t)chunk * M + m) * npad + n] = part[m];
+      }
+      return true;
+    });
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Split-K: Y[m, n] = ((0 + part[0]) + part[1]) + ... in chunk order, the same
+// sum the tile-major path forms, so both give identical bits.
+__global__ void gemv_tc_reduce_kernel(const float* __restrict__ part, float* __restrict__ Y,
+                                      int64_t ldy, int M, int N, int nch, int64_t npad) {
+  const int64_t total = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / N), n = (int)(i % N);
+    float acc = 0.0f;
+    for (int c = 0; c < nch; c++) acc = acc + part[((int64_t)c * M + m) * npad + n];
+    Y[m * ldy + n] = acc;
+  }
+}
+
+// Work decomposition.  Tile-major when the tiles spread evenly over the SMs
+// (at least one per SM, at least 90% balance); split-K otherwise.  Both sum
+// the chunk partials in chunk order, so the choice never changes a bit.
+struct Plan {
+  bool tile_major;
+  int nch, tiles, grid, cpc, tg;
+  size_t partial_floats;
+};
+
+Plan make_plan(int64_t K, int64_t nl, int64_t M, int sm_count) {
+  Plan pl;
+  pl.nch = (int)((K + kChunkK - 1) / kChunkK);
+  pl.tiles = (int)((nl + kTile - 1) / kTile);
+  const int gt = std::min(pl.tiles, sm_count);
+  const double per = (double)pl.tiles / gt;
+  const double eff = per / std::ceil(per);
+  pl.tile_major = pl.nch == 1 || pl.nch > sm_count || (pl.tiles >= sm_count && eff >= 0.9);
+  if (pl.tile_major) {
+    pl.grid = gt;
+    pl.cpc = 0;
+    pl.tg = std::max<int>(1, (int)(32 / M));
+    pl.partial_floats = 0;
+  } else {
+    pl.cpc = std::min(pl.tiles, sm_count / pl.nch);
+    pl.grid = pl.cpc * pl.nch;
+    pl.tg = 1;
+    pl.partial_floats = (size_t)pl.nch * M * pl.tiles * kTile;
+  }
+  return pl;
+}
+
+// TMEM layout of D for one item: regions of G blocks, NM columns each.  Two
+// D buffers when one fits in 128 columns.
+struct DPlan {
+  int regions, nm, nd;  // nd = 0: does not fit
+};
+
+DPlan d_plan(int64_t M, int bs) {
+  const int G = M == 1 ? 5 : (M == 2 ? 2 : 1);
+  DPlan d;
+  d.nm = (3 * M * G <= 16) ? 16 : 32;
+  d.regions = (kChunkK / bs + G - 1) / G;
+  const int per = d.regions * d.nm;
+  d.nd = per <= (int)kDCols / 2 ? 2 : (per <= (int)kDCols ? 1 : 0);
+  return d;
+}
+
+template <int M>
+int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
+  const DPlan dp = d_plan(M, w.bs);
+  p.regions = dp.regions;
+  p.nd = dp.nd;
+  p.dstride = p.nd == 2 ? kDCols / 2 : 0;
+  // stage st covers k [32 st, 32 st + 32) of the item: block 32 st / bs,
+  // region block / G; the first stage of a region starts its accumulator
+  constexpr int G = XShape<M>::G;
+  p.acc_mask = 0;
+  for (int st = 0; st < kItemStages; st++) {
+    const int blk = st * 32 / w.bs, rg = blk / G;
+    p.op_d[st] = (uint32_t)(rg * dp.nm);
+    if ((st * 32) % (G * w.bs) != 0) p.acc_mask |= 1u << st;
+  }
+  const uint32_t yacc_bytes = pl.tile_major ? (uint32_t)(p.tg * M * kTile * 4) : 0;
+  const size_t fixed = 1024 + 2 * kXBufBytes + yacc_bytes + 1024;
+  int nbst = (int)((kSmemLimit - fixed) / p.stage_bytes);
+  if (nbst > kMaxBStages) nbst = kMaxBStages;
+  if (nbst < 2) return fail(ORT_CUDA_ERR_UNSUPPORTED, "tc gemv: shared memory too small");
+  p.nbst = nbst;
+  p.yacc_off = 2 * kXBufBytes + nbst * p.stage_bytes;
+  const size_t smem = fixed + (size_t)nbst * p.stage_bytes;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemLimit));
+    configured |= 1ull << (dev & 63);
+  }
+  gemv_tc_kernel<M><<<pl.grid, kThreadsTC, smem, st>>>(w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p);
+  ORTC_CUDA(cudaGetLastError());
+  return ORT_CUDA_OK;
+}
+
+}  // namespace
+
+// TMA views of a MatMulNBits weight for the tensor-core GEMV.
+int prepare_nbits_tc(Weight& w) {
+  w.tc_ok = false;
+  const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
+  if (w.bs < kMinBs || w.bs > kChunkK || col_bytes % 16 != 0 || w.nl == 0) return ORT_CUDA_OK;
+  const int bpi = kChunkK / w.bs;
+  int rc = encode_tma_2d(&w.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes,
+                         (uint64_t)w.nl, (uint64_t)col_bytes, 128, kTile,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tma_2d(&w.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales, (uint64_t)w.nl,
+                     (uint64_t)w.nb, (uint64_t)w.s_pitch * 4, kTile, bpi,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (w.has_zp) {
+    rc = encode_tma_2d(&w.tmZ, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.zp, (uint64_t)w.nl,
+                       (uint64_t)((w.nb + 1) / 2), (uint64_t)w.z_pitch, kTile,
+                       bpi >= 2 ? bpi / 2 : 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  w.tc_ok = true;
+  return ORT_CUDA_OK;
+}
+
+// The tensor-core GEMV takes M <= 8 when one item's D columns fit in TMEM
+// beside the A ring (384 columns).
+bool tc_gemv_ok(const Weight& w, int64_t M) {
+  if (!w.tc_ok || M < 1 || M > 8) return false;
+  return d_plan(M, w.bs).nd > 0;
+}
+
+size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count) {
+  return make_plan(K, nl, M, sm_count).partial_floats;
+}
+
+int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
+                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches) {
+  if (w.nl == 0) return ORT_CUDA_OK;
+  const Plan pl = make_plan(w.K, w.nl, M, sm_count);
+  TcParams p;
+  p.A = A;
+  p.Y = Y;
+  p.err = err;
+  p.ldy = ldy;
+  p.N = (int)w.nl;
+  p.K = (int)w.K;
+  p.bs = w.bs;
+  p.nch = pl.nch;
+  p.tiles = pl.tiles;
+  p.tile_major = pl.tile_major ? 1 : 0;
+  p.grid_tiles = pl.grid;
+  p.tg = pl.tg;
+  p.cpc = pl.cpc;
+  p.part = pl.tile_major ? nullptr : partials;
+  p.bpi = kChunkK / w.bs;
+  p.has_zp = w.has_zp ? 1 : 0;
+  const int z_rows = p.bpi >= 2 ? p.bpi / 2 : 1;
+  p.s_off = kPackedBytes;
+  p.z_off = kPackedBytes + (uint32_t)p.bpi * kTile * 4;
+  const uint32_t zbytes = p.has_zp ? (uint32_t)z_rows * kTile : 0;
+  p.stage_bytes = (p.z_off + zbytes + 1023) & ~1023u;
+  p.stage_tx = kPackedBytes + (uint32_t)p.bpi * kTile * 4 + zbytes;
+  int rc;
+  switch (M) {
+    case 1: rc = launch_m<1>(w, p, pl, st); break;
+    case 2: rc = launch_m<2>(w, p, pl, st); break;
+    case 3: rc = launch_m<3>(w, p, pl, st); break;
+    case 4: rc = launch_m<4>(w, p, pl, st); break;
+    case 5: rc = launch_m<5>(w, p, pl, st); break;
+    case 6: rc = launch_m<6>(w, p, pl, st); break;
+    case 7: rc = launch_m<7>(w, p, pl, st); break;
+    case 8: rc = launch_m<8>(w, p, pl, st); break;
+    default: return fail(ORT_CUDA_ERR_INVALID_ARG, "tc gemv: M out of range");
+  }
+  if (rc) return rc;
+  (*launches)++;
+  if (!pl.tile_major) {
+    const int64_t total = M * w.nl;
+    const unsigned blocks =
+        (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count * 8);
+    gemv_tc_reduce_kernel<<<blocks, 256, 0, st>>>(partials, Y, ldy, (int)M, (int)w.nl, pl.nch,
+                                                  (int64_t)pl.tiles * kTile);
+    ORTC_CUDA(cudaGetLastError());
+    (*launches)++;
+  }
+  return ORT_CUDA_OK;
+}
+
+}  // namespace ortc

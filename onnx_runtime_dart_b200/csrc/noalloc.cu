@@ -6,14 +6,14 @@
 // or a latency-critical path where cudaMalloc's implicit device
 // synchronisation is not acceptable.  ort_cuda_matmul_nbits may grow the
 // session's split-K scratch with cudaMalloc; this entry point never does.
-// It runs the same decode GEMV kernel with its scratch (split-K partial
-// sums and arrival counters) in the two file-scope arrays below, which
-// every GPU that loads this library holds until the process exits.
+// It runs the same decode GEMV kernels with their scratch (the split-K
+// partial sums) in the file-scope array below, which every GPU that loads
+// this library holds until the process exits.
 //
-// Host code must not use the arrays' names as device addresses (on the host
-// they are stand-ins); the device addresses come from
-// cudaGetSymbolAddress, taken once per device with that device current, on
-// the first call of the entry point on that device.
+// Host code must not use the array's name as a device address (on the host
+// it is a stand-in); the device address comes from cudaGetSymbolAddress,
+// taken once per device with that device current, on the first call of the
+// entry point on that device.
 #include <mutex>
 
 #include "common.cuh"
@@ -21,22 +21,19 @@
 namespace ortc {
 namespace {
 
-// 4 MiB of partial sums and 256 KiB of arrival counters per GPU.
+// 4 MiB of partial sums per GPU.
 constexpr size_t kNoAllocPartialFloats = size_t(1) << 20;
-constexpr size_t kNoAllocCounterWords = size_t(1) << 16;
 
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartialFloats];
-static __device__ __align__(256) unsigned g_noalloc_counters[kNoAllocCounterWords];
 
 struct Slot {
   float* partials = nullptr;
-  unsigned* counters = nullptr;
   bool ready = false;
 };
 std::mutex g_mu;
 Slot g_slots[64];
 
-// Device addresses of the two arrays on `device` (which must be current).
+// Device address of the array on `device` (which must be current).
 int slot_for(int device, Slot** out) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (device < 0 || device >= 64) return fail(ORT_CUDA_ERR_INVALID_ARG, "device index >= 64");
@@ -46,9 +43,6 @@ int slot_for(int device, Slot** out) {
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(partials)");
     sl.partials = static_cast<float*>(p);
-    e = cudaGetSymbolAddress(&p, g_noalloc_counters);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(counters)");
-    sl.counters = static_cast<unsigned*>(p);
     sl.ready = true;
   }
   *out = &sl;
@@ -73,30 +67,23 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
              "no-allocation MatMulNBits runs on single-GPU sessions only");
   ORTC_CHECK(M >= 1 && M <= 4, ORT_CUDA_ERR_INVALID_ARG,
              "no-allocation MatMulNBits takes 1 <= M <= 4, got M=" + std::to_string(M));
-  ORTC_CHECK(w.tmB_ok && w.K % 32 == 0, ORT_CUDA_ERR_UNSUPPORTED,
-             "no-allocation MatMulNBits needs K % 32 == 0");
-  ORTC_CHECK(((uintptr_t)A & 15) == 0, ORT_CUDA_ERR_INVALID_ARG, "A must be 16-byte aligned");
-  const size_t pf = gemv_partial_floats(w.K, w.nl, M);
-  const size_t cw = gemv_counter_words(w.K, w.nl);
-  ORTC_CHECK(pf <= kNoAllocPartialFloats && cw <= kNoAllocCounterWords, ORT_CUDA_ERR_INVALID_ARG,
+  ORTC_CHECK(tc_gemv_ok(w, M), ORT_CUDA_ERR_UNSUPPORTED,
+             "no-allocation MatMulNBits needs 32 <= block_size <= 512");
+  const size_t pf = tc_gemv_partial_floats(w.K, w.nl, M, s->sm_count);
+  ORTC_CHECK(pf <= kNoAllocPartialFloats, ORT_CUDA_ERR_INVALID_ARG,
              "no-allocation MatMulNBits: this shape needs " + std::to_string(pf) +
-                 " partial floats and " + std::to_string(cw) +
-                 " counters; the static scratch holds " + std::to_string(kNoAllocPartialFloats) +
-                 " and " + std::to_string(kNoAllocCounterWords));
+                 " partial floats; the static scratch holds " +
+                 std::to_string(kNoAllocPartialFloats));
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != s->device) ORTC_CUDA(cudaSetDevice(s->device));
   Slot* sl = nullptr;
+  // The array keeps the previous call's contents; nothing in it needs a
+  // starting value (every partial is written before it is read).
   int rc = slot_for(s->device, &sl);
-  if (rc == ORT_CUDA_OK && cw > 0) {
-    // The arrays keep the previous call's contents: the counters must
-    // start at zero.  (cudaMemsetAsync allocates nothing.)
-    cudaError_t e = cudaMemsetAsync(sl->counters, 0, cw * sizeof(unsigned), s->stream);
-    if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemsetAsync(counters)");
-  }
   if (rc == ORT_CUDA_OK)
-    rc = launch_nbits_gemv(w, A, M, Y, w.nl, sl->partials, sl->counters, s->err_dev,
-                           s->sm_count, s->stream, &s->launches);
+    rc = launch_tc_gemv(w, A, M, Y, w.nl, sl->partials, s->err_dev, s->sm_count, s->stream,
+                        &s->launches);
   if (prev >= 0 && prev != s->device) cudaSetDevice(prev);
   return rc;
 }

@@ -73,24 +73,6 @@ int ensure_kscratch(ort_cuda_session* s, size_t bytes) {
   return ORT_CUDA_OK;
 }
 
-int ensure_kcnt(ort_cuda_session* s, size_t words) {
-  if (words <= s->kcnt_words && !s->kcnt_dirty) return ORT_CUDA_OK;
-  if (words > s->kcnt_words) {
-    size_t want = words + words / 4 + 4096;
-    if (s->kcnt) {
-      ORTC_CUDA(cudaStreamSynchronize(s->stream));
-      ORTC_CUDA(cudaFree(s->kcnt));
-      s->kcnt = nullptr;
-      s->kcnt_words = 0;
-    }
-    ORTC_CUDA(cudaMalloc(&s->kcnt, want * 4));
-    s->kcnt_words = want;
-  }
-  ORTC_CUDA(cudaMemsetAsync(s->kcnt, 0, s->kcnt_words * 4, s->stream));
-  s->kcnt_dirty = false;
-  return ORT_CUDA_OK;
-}
-
 namespace {
 
 struct DeviceGuard {
@@ -147,13 +129,12 @@ void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_
 }
 
 // A kernel whose bounded wait gave up wrote a code into the host-mapped
-// error word; report it once and mark the kernel scratch for re-zeroing.
+// error word; report it once.
 int check_kernel_error(ort_cuda_session* s) {
   volatile int* e = s->err_host;
   if (!e || *e == 0) return ORT_CUDA_OK;
   const int code = *e;
   *e = 0;
-  s->kcnt_dirty = true;
   return fail(ORT_CUDA_ERR_TIMEOUT,
               "a kernel wait exceeded its bound (code " + std::to_string(code) +
                   "); the kernel stopped and returned");
@@ -389,7 +370,6 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   s->allocs.clear();
   if (s->ws) cudaFree(s->ws);
   if (s->kscratch) cudaFree(s->kscratch);
-  if (s->kcnt) cudaFree(s->kcnt);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
   if (s->nccl) {
@@ -467,41 +447,78 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
   };
   cudaError_t e;
   if (nl > 0) {
+    // Packed B: this rank's columns are contiguous; upload, then reorder
+    // the nibbles of every 32-bit word into the device layout.
+    uint8_t* tmpB = nullptr;
+    e = cudaMalloc(&tmpB, (size_t)(nl * col_bytes));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(B staging)"));
     e = cudaMalloc(&w.B, (size_t)(nl * col_bytes));
-    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(B)"));
-    e = cudaMemcpyAsync(w.B, B + w.n0 * col_bytes, (size_t)(nl * col_bytes),
-                        cudaMemcpyHostToDevice, s->stream);
-    if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy B"));
-    e = cudaMalloc(&w.scales, (size_t)(nl * nb * 4));
-    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(scales)"));
-    if (f16) {
-      uint16_t* tmp = nullptr;
-      e = cudaMalloc(&tmp, (size_t)(nl * nb * 2));
-      if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(scales16)"));
-      e = cudaMemcpyAsync(tmp, (const uint16_t*)scales + w.n0 * nb, (size_t)(nl * nb * 2),
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(tmpB, B + w.n0 * col_bytes, (size_t)(nl * col_bytes),
                           cudaMemcpyHostToDevice, s->stream);
-      int rc = e == cudaSuccess ? launch_half_to_float(tmp, w.scales, nl * nb, s->stream, &s->launches)
-                                : cuda_fail(e, "copy scales");
-      cudaStreamSynchronize(s->stream);
-      cudaFree(tmp);
-      if (rc) return cleanup(rc);
+    int rc = e == cudaSuccess ? launch_permute_nibbles((const uint32_t*)tmpB, (uint32_t*)w.B,
+                                                       nl * col_bytes / 4, s->stream, &s->launches)
+                              : cuda_fail(e, "copy B");
+    cudaStreamSynchronize(s->stream);
+    cudaFree(tmpB);
+    if (rc) return cleanup(rc);
+    // Scales: fp32 (fp16 widened bit-exactly on the device), transposed to
+    // block-major [nb][s_pitch].
+    w.s_pitch = (nl + 3) / 4 * 4;
+    float* tmpS = nullptr;
+    e = cudaMalloc(&tmpS, (size_t)(nl * nb * 4));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(scale staging)"));
+    e = cudaMalloc(&w.scales, (size_t)(nb * w.s_pitch * 4));
+    if (e == cudaSuccess) e = cudaMemsetAsync(w.scales, 0, (size_t)(nb * w.s_pitch * 4), s->stream);
+    if (e == cudaSuccess) {
+      if (f16) {
+        uint16_t* tmp16 = nullptr;
+        e = cudaMalloc(&tmp16, (size_t)(nl * nb * 2));
+        if (e == cudaSuccess)
+          e = cudaMemcpyAsync(tmp16, (const uint16_t*)scales + w.n0 * nb, (size_t)(nl * nb * 2),
+                              cudaMemcpyHostToDevice, s->stream);
+        rc = e == cudaSuccess ? launch_half_to_float(tmp16, tmpS, nl * nb, s->stream, &s->launches)
+                              : cuda_fail(e, "copy scales");
+        cudaStreamSynchronize(s->stream);
+        if (tmp16) cudaFree(tmp16);
+      } else {
+        e = cudaMemcpyAsync(tmpS, (const float*)scales + w.n0 * nb, (size_t)(nl * nb * 4),
+                            cudaMemcpyHostToDevice, s->stream);
+        rc = e == cudaSuccess ? ORT_CUDA_OK : cuda_fail(e, "copy scales");
+      }
     } else {
-      e = cudaMemcpyAsync(w.scales, (const float*)scales + w.n0 * nb, (size_t)(nl * nb * 4),
-                          cudaMemcpyHostToDevice, s->stream);
-      if (e != cudaSuccess) return cleanup(cuda_fail(e, "copy scales"));
+      rc = cuda_fail(e, "cudaMalloc(scales)");
     }
+    // [nl][nb] -> [nb][s_pitch]: transpose into a padded pitch via a dense
+    // [nb][nl] temporary then a pitched copy.
+    float* tmpT = nullptr;
+    if (!rc) {
+      e = cudaMalloc(&tmpT, (size_t)(nl * nb * 4));
+      rc = e == cudaSuccess ? launch_transpose(tmpS, tmpT, nl, nb, s->stream, &s->launches)
+                            : cuda_fail(e, "cudaMalloc(scale transpose)");
+    }
+    if (!rc) {
+      e = cudaMemcpy2DAsync(w.scales, (size_t)(w.s_pitch * 4), tmpT, (size_t)(nl * 4),
+                            (size_t)(nl * 4), (size_t)nb, cudaMemcpyDeviceToDevice, s->stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "pitch scales");
+    }
+    cudaStreamSynchronize(s->stream);
+    cudaFree(tmpS);
+    if (tmpT) cudaFree(tmpT);
+    if (rc) return cleanup(rc);
     if (zp) {
-      // Re-index zero points to the local flat layout: nibble (c*nb + blk)
-      // of this rank's column c (the reference's flat indexing,
-      // onnx_qlinear_ops.dart:135-137), from either input layout.
-      const int64_t nz = nl * nb;
-      std::vector<uint8_t> z((size_t)((nz + 1) / 2), 0);
+      // Zero points from either input layout (the reference's flat nibble
+      // n*nb + blk, onnx_qlinear_ops.dart:135-137, or ORT's per-column
+      // padding) into the transposed table [ceil(nb/2)][z_pitch].
+      w.z_pitch = (nl + 15) / 16 * 16;
+      const int64_t zrows = (nb + 1) / 2;
+      std::vector<uint8_t> z((size_t)(zrows * w.z_pitch), 0);
       const bool per_col = (flags & ORT_CUDA_ZP_PER_COLUMN) != 0;
       const int64_t col_zbytes = (nb + 1) / 2;
       for (int64_t c = 0; c < nl; c++) {
+        const int64_t gc = w.n0 + c;
         for (int64_t b = 0; b < nb; b++) {
           uint8_t v;
-          const int64_t gc = w.n0 + c;
           if (per_col) {
             const uint8_t byte = zp[gc * col_zbytes + (b >> 1)];
             v = (b & 1) ? (byte >> 4) : (byte & 0xF);
@@ -510,8 +527,7 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
             const uint8_t byte = zp[zi >> 1];
             v = (zi & 1) ? (byte >> 4) : (byte & 0xF);
           }
-          const int64_t li = c * nb + b;
-          z[(size_t)(li >> 1)] |= (uint8_t)(v << ((li & 1) * 4));
+          z[(size_t)((b >> 1) * w.z_pitch + c)] |= (uint8_t)(v << ((b & 1) * 4));
         }
       }
       e = cudaMalloc(&w.zp, z.size());
@@ -521,13 +537,8 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
     }
     e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "upload sync"));
-    if (K % 32 == 0 && col_bytes % 16 == 0) {
-      // TMA view for the decode GEMV: uint32 [nl][col_bytes/4], 32 x 512 B boxes.
-      int rc = encode_tma_2d(&w.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT32, w.B, (uint64_t)(col_bytes / 4),
-                             (uint64_t)nl, (uint64_t)col_bytes, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
-      if (rc) return cleanup(rc);
-      w.tmB_ok = true;
-    }
+    rc = prepare_nbits_tc(w);
+    if (rc) return cleanup(rc);
   }
   auto it = s->weights.find(name);
   if (it != s->weights.end()) {
@@ -735,8 +746,6 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
   return ORT_CUDA_OK;
 }
 
-bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
-
 }  // namespace
 
 extern "C" {
@@ -761,13 +770,11 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if (mode == ORT_CUDA_MODE_STRICT)
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
-                  const bool gemv_ok = M <= 4 && w.tmB_ok && (w.K % 32) == 0 && aligned16(dA);
-                  if (gemv_ok) {
-                    int rc = ensure_kscratch(s, gemv_partial_floats(w.K, w.nl, M) * 4);
-                    if (!rc) rc = ensure_kcnt(s, gemv_counter_words(w.K, w.nl));
+                  if (tc_gemv_ok(w, M)) {
+                    int rc = ensure_kscratch(s, tc_gemv_partial_floats(w.K, w.nl, M, s->sm_count) * 4);
                     if (rc) return rc;
-                    return launch_nbits_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->kcnt,
-                                             s->err_dev, s->sm_count, s->stream, &s->launches);
+                    return launch_tc_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
+                                          s->sm_count, s->stream, &s->launches);
                   }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K))

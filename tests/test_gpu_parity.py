@@ -374,8 +374,15 @@ def test_empty_m(sess):
 
 def test_launch_counter_counts_own_kernels(sess):
     rng = np.random.default_rng(15)
-    B, s, z = O.make_nbits_weight(rng, 1024, 256, 32, zero_points=False)
-    sess.upload_nbits("lc", B, s, z, k=1024, n=256, block_size=32)
+    # one 512-k chunk: a single GEMV launch
+    B, s, z = O.make_nbits_weight(rng, 512, 256, 32, zero_points=False)
+    sess.upload_nbits("lc", B, s, z, k=512, n=256, block_size=32)
     before = sess.launch_count()
-    sess.matmul_nbits("lc", rng.standard_normal((1, 1024)).astype(np.float32))
+    sess.matmul_nbits("lc", rng.standard_normal((1, 512)).astype(np.float32))
     assert sess.launch_count() == before + 1
+    # two chunks over two column tiles: split-K GEMV plus the chunk-order reduction
+    B, s, z = O.make_nbits_weight(rng, 1024, 256, 32, zero_points=False)
+    sess.upload_nbits("lc2", B, s, z, k=1024, n=256, block_size=32)
+    before = sess.launch_count()
+    sess.matmul_nbits("lc2", rng.standard_normal((1, 1024)).astype(np.float32))
+    assert sess.launch_count() == before + 2
