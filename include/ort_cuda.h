@@ -177,19 +177,18 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
  * device memory owned by another runtime's allocator, or a latency path
  * where cudaMalloc's implicit device synchronisation is not acceptable.
  * ort_cuda_matmul_nbits may grow session scratch with cudaMalloc; this
- * call runs the same exact-mode decode GEMV with its split-K scratch in
- * static device arrays of this library: 4 MiB of partial sums plus 256 KiB
- * of arrival counters, held by every GPU that loads the library until the
- * process exits.  Shapes whose scratch would exceed that are rejected with
- * ORT_CUDA_ERR_INVALID_ARG (e.g. M=1 fits a 4096 x 128256 weight).
- *   A, Y   DEVICE pointers ([M,K] and [M,N] fp32; A 16-byte aligned);
- *          the call is stream-ordered on the session stream
- *   M      1..4; K % 32 == 0; single-GPU sessions only
- * The first call on a device looks up the arrays' device addresses
+ * call runs the same exact-mode decode GEMV with its split-K scratch in a
+ * static device array of this library: 4 MiB of partial sums, held by every
+ * GPU that loads the library until the process exits.  Shapes whose
+ * scratch would exceed that are rejected with ORT_CUDA_ERR_INVALID_ARG
+ * (only few-column, very long-K weights need split-K scratch at all).
+ *   A, Y   DEVICE pointers ([M,K] and [M,N] fp32); the call is
+ *          stream-ordered on the session stream
+ *   M      1..4; 32 <= block_size <= 512; single-GPU sessions only
+ * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls share the arrays, so calls that overlap on the GPU (other
- * streams, other sessions on the same device) race; the counters are
- * cleared at the start of every call. */
+ * All calls share the array, so calls that overlap on the GPU (other
+ * streams, other sessions on the same device) race. */
 ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, const char* name,
                                                const float* A, int64_t M, float* Y);
 

@@ -3,7 +3,7 @@
 Some hosts cannot call cudaMalloc once they are running (a device-memory
 budget fixed at start-up, memory owned by another runtime's allocator, or a
 latency path that cannot take cudaMalloc's implicit device synchronisation).
-This entry point keeps its split-K scratch in static device arrays of the
+This entry point keeps its split-K scratch in a static device array of the
 library.  The test calls it through the C ABI on device buffers and checks
 it against the regular entry point on two calls in a row; the file is named
 to be collected last.
@@ -21,10 +21,10 @@ TOL = 1e-5  # exact-mode bar used by every GPU parity test
 
 
 @pytest.mark.parametrize("K,N,bs,zp,M", [
-    (4096, 3000, 128, True, 1),     # 4 k-chunks: partials + counters used
-    (14336, 1024, 128, True, 4),    # 14 k-chunks, M = 4
-    (1024, 777, 32, False, 2),      # single chunk: no scratch needed
-    (2048, 128256 // 2, 128, True, 1),
+    (4096, 3000, 128, True, 1),     # split-K: chunk partials in the static array
+    (14336, 1024, 128, True, 4),    # 28 chunks, M = 4
+    (512, 777, 32, False, 2),       # single chunk: no scratch needed
+    (2048, 128256 // 2, 128, True, 1),  # many tiles: no scratch needed
 ])
 def test_noalloc_matches_regular_entry_point(K, N, bs, zp, M):
     from onnx_runtime_dart_b200 import CudaSession, DeviceTensor, _lib
@@ -42,7 +42,8 @@ def test_noalloc_matches_regular_entry_point(K, N, bs, zp, M):
             rc = L.ort_cuda_matmul_nbits_noalloc(s.handle, b"w", A.ptr, M, Y.ptr)
             assert rc == 0, _lib.last_error()
             s.sync()
-            assert s.launch_count() == before + 1
+            # one GEMV launch, plus the chunk-sum launch for split-K shapes
+            assert s.launch_count() in (before + 1, before + 2)
             assert max_rel(ref, Y.numpy()) <= TOL
 
 
@@ -51,7 +52,7 @@ def test_noalloc_rejects_what_it_cannot_hold():
     from onnx_runtime_dart_b200.workloads import make_nbits_weight
     L = _lib.load()
     rng = np.random.default_rng(3)
-    K, N = 4096, 128256  # M=4 needs 4*4*128256 partial floats > 2^20
+    K, N = 40960, 4096  # split-K, M=4: 80 chunks x 4 x 4096 partial floats > 2^20
     B, sc, z = make_nbits_weight(rng, K, N, 128, zero_points=False, scale_dtype=np.float16)
     with CudaSession(0) as s:
         s.upload_nbits("big", B, sc, z, k=K, n=N, block_size=128)
