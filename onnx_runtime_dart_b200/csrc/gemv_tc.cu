@@ -74,7 +74,8 @@ constexpr uint32_t kDCols = kTmemCols - kDCol;          // 256 columns for D
 constexpr int kMaxBpi = kChunkK / kMinBs;               // blocks per item
 constexpr uint32_t kXBytesMax = 32 * kChunkK;           // X for NM = 32
 constexpr uint32_t kCsumBytes = kMaxBpi * 8 * 3 * 4;    // digit sums [bpi][M][3]
-constexpr uint32_t kXBufBytes = kXBytesMax + ((kCsumBytes + 1023) & ~1023u);
+// X buffer: X, digit sums, row max bits [8], row exponents [8]
+constexpr uint32_t kXBufBytes = kXBytesMax + ((kCsumBytes + 64 + 1023) & ~1023u);
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr int kNonFinite = -100000;  // S_m of a row holding an inf or NaN
 
@@ -97,6 +98,7 @@ struct TcParams {
   int tg;          // tile-major: tiles per group (y accumulators in smem)
   int cpc;         // split-K: CTAs per chunk
   int bpi, regions, has_zp, nbst;
+  int a_vec;       // A 16-byte aligned and K % 4 == 0: 16-byte activation loads
   int nd;          // D buffers: 2, or 1 when an item needs more than 128 columns
   uint32_t dstride;
   // Per 32-k stage of an item: D column offset of its region and whether it
@@ -180,10 +182,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* xfull = dfull + 2;    // [2] X buffer written (8 dequantiser warps)
   uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 4 epilogue warps)
   uint64_t* fin = xempty + 2;
-  uint64_t* eready = fin + 1;     // row exponents written, X buffers zeroed
-  uint64_t* xsync = eready + 1;   // dequantisers, inside an X build
+  uint64_t* xsync = fin + 1;      // dequantisers, inside an X build
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xsync + 1);
-  int* e_s = reinterpret_cast<int*>(tmem_slot + 1);  // [8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -202,7 +202,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&xempty[d], 1 + kEpiWarps);
     }
     mbar_init(fin, 1);
-    mbar_init(eready, kDeWarps);
     mbar_init(xsync, kDeWarps);
     fence_mbarrier_init();
   }
@@ -214,6 +213,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The next kernel in the stream may start its prologue and weight stream
+  // as our CTAs retire; it waits for our completion before touching
+  // activations or outputs (griddep_wait).
+  griddep_launch_dependents();
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -294,43 +297,22 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int q = warp & 3, grp = warp >> 2;
     const int nl = q * 32 + lane;  // column within the tile = TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    // Row exponents over all of K: |rint(a * 2^S_m)| <= 2^22.
-    if (warp < M) {
-      float mx = 0.0f;
-      bool finite = true;
-      for (int k = lane; k < p.K; k += 32) {
-        const float a = p.A[(int64_t)warp * p.K + k];
-        finite = finite && isfinite(a);
-        mx = fmaxf(mx, fabsf(a));
-      }
-      finite = __all_sync(0xffffffffu, finite);
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      int S = 0;
-      if (!finite) {
-        S = kNonFinite;
-      } else if (mx > 0.0f) {
-        int ex;
-        frexpf(mx, &ex);  // mx < 2^ex
-        S = 22 - ex;
-      }
-      if (lane == 0) e_s[warp] = S;
-    }
     // Zero both X buffers once: the non-zero pattern is the same for every
     // chunk, so each build rewrites only those entries.
     for (int i = threadIdx.x; i < 2 * (int)kXBufBytes / 16; i += kDeWarps * 32)
       asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
                    : "memory");
-    __syncwarp();
-    if (lane == 0) mbar_arrive(eready);
-    bool ok = mbar_wait(eready, 0);
-    if (!ok) record_error(p.err, KERR_WAIT_FULL);
     uint32_t xph = 0;
+    bool ok = warp_group_sync(xsync, xph, p.err);
+    griddep_wait();  // activations come from the previous kernel in the stream
 
+    constexpr int kU = kChunkK / 4;                          // 4-k units per row
+    constexpr int kPer = (M * kU + kDeWarps * 32 - 1) / (kDeWarps * 32);
     int j = 0, cur = -1, nbuild = 0;
     for_each_item(p, [&](int, int chunk, int) {
       if (!ok) return false;
       if (chunk != cur) {
-        // X and the digit sums of this chunk, into buffer nbuild & 1.
+        // X, digit sums and row exponents of this chunk, into buffer nbuild & 1.
         const int xbuf = nbuild & 1;
         if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
           record_error(p.err, KERR_WAIT_EMPTY);
@@ -338,21 +320,63 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         uint8_t* xbase = Xs + xbuf * kXBufBytes;
         int* csum = reinterpret_cast<int*>(xbase + kXBytesMax);  // [bpi][M][3]
+        unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXBytesMax + kCsumBytes);  // [8]
+        int* rexp = reinterpret_cast<int*>(rmax + 8);                                  // [8]
         for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
+        if (threadIdx.x < 8) rmax[threadIdx.x] = 0;
+        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        // Activations of the chunk, unit u = 4 consecutive k of row u / kU.
+        // A warp's 32 units lie in one row.
+        const int k0 = chunk * kChunkK;
+        float4 av[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; i++) {
+          const int u = threadIdx.x + i * kDeWarps * 32;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (u < M * kU) {
+            const int m = u / kU, k = k0 + (u % kU) * 4;
+            const float* src = p.A + (int64_t)m * p.K + k;
+            if (p.a_vec && k + 3 < p.K) {
+              a = __ldg(reinterpret_cast<const float4*>(src));
+            } else {
+              if (k < p.K) a.x = src[0];
+              if (k + 1 < p.K) a.y = src[1];
+              if (k + 2 < p.K) a.z = src[2];
+              if (k + 3 < p.K) a.w = src[3];
+            }
+            // largest magnitude as bits; inf and NaN compare above 0x7f7fffff
+            const unsigned mb = max(max(__float_as_uint(a.x) & 0x7fffffffu, __float_as_uint(a.y) & 0x7fffffffu),
+                                    max(__float_as_uint(a.z) & 0x7fffffffu, __float_as_uint(a.w) & 0x7fffffffu));
+            const unsigned wm = __reduce_max_sync(0xffffffffu, mb);
+            if (lane == 0) atomicMax(&rmax[m], wm);
+          }
+          av[i] = a;
+        }
         if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
         const uint32_t xb = smem_u32(xbase);
-        const int k0 = chunk * kChunkK;
-        for (int u = threadIdx.x; u < M * (kChunkK / 4); u += kDeWarps * 32) {
-          const int m = u / (kChunkK / 4), k = (u % (kChunkK / 4)) * 4;
-          const int bl = k / p.bs, slot = bl % G, S = e_s[m];
+#pragma unroll
+        for (int i = 0; i < kPer; i++) {
+          const int u = threadIdx.x + i * kDeWarps * 32;
+          if (u >= M * kU) continue;
+          const int m = u / kU, k = (u % kU) * 4;
+          const int bl = k / p.bs, slot = bl % G;
+          // chunk exponent: |rint(a * 2^S)| <= 2^22 for every a of the row
+          const unsigned mb = rmax[m];
+          int S = 0;
+          if (mb > 0x7f7fffffu) {
+            S = kNonFinite;
+          } else if (mb != 0) {
+            int ex;
+            frexpf(__uint_as_float(mb), &ex);  // max < 2^ex
+            S = 22 - ex;
+          }
+          if ((u % kU) == 0) rexp[m] = S;
+          const float vals[4] = {av[i].x, av[i].y, av[i].z, av[i].w};
           uint32_t w0 = 0, w1 = 0, w2 = 0;
           int s0 = 0, s1 = 0, s2 = 0;
 #pragma unroll
           for (int v = 0; v < 4; v++) {
-            const int kk = k0 + k + v;
-            int X = 0;
-            if (kk < p.K && S != kNonFinite)
-              X = __float2int_rn(scale_pow2(p.A[(int64_t)m * p.K + kk], S));
+            const int X = S == kNonFinite ? 0 : __float2int_rn(scale_pow2(vals[v], S));
             // balanced base-256 digits: X = c2*65536 + c1*256 + c0, each in [-128, 127]
             const int c0 = ((X + 128) & 255) - 128;
             const int X1 = (X - c0) >> 8;
@@ -427,11 +451,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // the first nd items find their D buffers free
     if (lane == 0 && egrp == 0)
       for (int e = 0; e < p.nd; e++) mbar_arrive(&ready[e]);
-    bool ok = mbar_wait(eready, 0);
-    if (!ok) record_error(p.err, KERR_WAIT_FULL);
+    griddep_wait();  // outputs and split-K scratch may still be in use upstream
+    bool ok = true;
     int S_m[M];
-#pragma unroll
-    for (int m = 0; m < M; m++) S_m[m] = e_s[m];
     int j = 0, cur = -1, nbuild = 0;
     for_each_item(p, [&](int tile, int chunk, int tig) {
       if (!ok) return false;
@@ -444,6 +466,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           record_error(p.err, KERR_WAIT_FULL);
           return ok = false;
         }
+        const int* rexp = reinterpret_cast<const int*>(Xs + (nbuild & 1) * kXBufBytes +
+                                                       kXBytesMax + kCsumBytes + 32);
+#pragma unroll
+        for (int m = 0; m < M; m++) S_m[m] = rexp[m];
         cur = chunk;
         nbuild++;
       }
@@ -535,15 +561,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // Split-K: Y[m, n] = ((0 + part[0]) + part[1]) + ... in chunk order, the same
-// sum the tile-major path forms, so both give identical bits.
-__global__ void gemv_tc_reduce_kernel(const float* __restrict__ part, float* __restrict__ Y,
-                                      int64_t ldy, int M, int N, int nch, int64_t npad) {
+// sum the tile-major path forms, so both give identical bits.  Launched as a
+// programmatic dependent of the GEMV: its small CTAs become resident beside
+// the GEMV's and wait in griddepcontrol.wait, so no launch gap follows.
+__global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __restrict__ part,
+                                                           float* __restrict__ Y, int64_t ldy,
+                                                           int M, int N, int nch, int64_t npad) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int64_t total = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int m = (int)(i / N), n = (int)(i % N);
+    const float* src = part + (int64_t)m * npad + n;
+    const int64_t cs = (int64_t)M * npad;
     float acc = 0.0f;
-    for (int c = 0; c < nch; c++) acc = acc + part[((int64_t)c * M + m) * npad + n];
+    int c = 0;
+    for (; c + 4 <= nch; c += 4) {  // four loads in flight, added in chunk order
+      const float p0 = src[(c + 0) * cs], p1 = src[(c + 1) * cs];
+      const float p2 = src[(c + 2) * cs], p3 = src[(c + 3) * cs];
+      acc = acc + p0;
+      acc = acc + p1;
+      acc = acc + p2;
+      acc = acc + p3;
+    }
+    for (; c < nch; c++) acc = acc + src[c * cs];
     Y[m * ldy + n] = acc;
   }
 }
@@ -626,8 +668,20 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
                                    (int)kSmemLimit));
     configured |= 1ull << (dev & 63);
   }
-  gemv_tc_kernel<M><<<pl.grid, kThreadsTC, smem, st>>>(w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p);
-  ORTC_CUDA(cudaGetLastError());
+  // Programmatic dependent launch: this kernel's prologue and weight stream
+  // may overlap the previous kernel's tail; it reads activations and writes
+  // outputs only after griddepcontrol.wait.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.grid);
+  cfg.blockDim = dim3(kThreadsTC);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p));
   return ORT_CUDA_OK;
 }
 
@@ -687,6 +741,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   p.tg = pl.tg;
   p.cpc = pl.cpc;
   p.part = pl.tile_major ? nullptr : partials;
+  p.a_vec = ((reinterpret_cast<uintptr_t>(A) & 15) == 0 && w.K % 4 == 0) ? 1 : 0;
   p.bpi = kChunkK / w.bs;
   p.has_zp = w.has_zp ? 1 : 0;
   const int z_rows = p.bpi >= 2 ? p.bpi / 2 : 1;
@@ -711,11 +766,17 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   (*launches)++;
   if (!pl.tile_major) {
     const int64_t total = M * w.nl;
-    const unsigned blocks =
-        (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count * 8);
-    gemv_tc_reduce_kernel<<<blocks, 256, 0, st>>>(partials, Y, ldy, (int)M, (int)w.nl, pl.nch,
-                                                  (int64_t)pl.tiles * kTile);
-    ORTC_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>((total + 127) / 128, (int64_t)sm_count * 4));
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_reduce_kernel, (const float*)partials, Y, ldy,
+                                 (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile));
     (*launches)++;
   }
   return ORT_CUDA_OK;

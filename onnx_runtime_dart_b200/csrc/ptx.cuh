@@ -147,6 +147,15 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr) {
 
 // Records an error code in the host-mapped error word (a plain store: any
 // non-zero value reports the failure; atomics over PCIe are not assumed).
+// Programmatic dependent launch.  griddep_wait blocks until the previous
+// kernel in the stream has completed and its memory is visible (a no-op
+// when this kernel was launched without the attribute);
+// griddep_launch_dependents lets the next kernel start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) *reinterpret_cast<volatile int*>(err) = code;
 }

@@ -189,6 +189,26 @@ def test_zero_point_per_column_odd_nb(sess):
     assert max_rel(ref, sess.matmul_nbits("pc", A)) <= EXACT_TOL
 
 
+def test_split_k_repeat_bitwise(sess):
+    """Split-K decode GEMVs write chunk partials that a dependent kernel,
+    launched to overlap the GEMV's tail, adds in chunk order.  Repeated and
+    interleaved calls on two split-K weights sharing the session scratch
+    must reproduce their first results bit for bit."""
+    rng = np.random.default_rng(21)
+    shapes = {"sk1": (4096, 3000, 128, 1), "sk2": (14336, 1024, 128, 4)}
+    A, first = {}, {}
+    for name, (K, N, bs, M) in shapes.items():
+        B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True)
+        sess.upload_nbits(name, B, s, z, k=K, n=N, block_size=bs)
+        A[name] = rng.standard_normal((M, K)).astype(np.float32)
+        first[name] = sess.matmul_nbits(name, A[name])
+        ref = O.matmul_nbits(A[name], B, s, z, K, N, 4, bs, threads=8)
+        assert max_rel(ref, first[name]) <= EXACT_TOL
+    for _ in range(3):
+        for name in shapes:
+            assert np.array_equal(sess.matmul_nbits(name, A[name]), first[name])
+
+
 def test_shard_columns_bitwise_invariant(sess):
     """A column's result does not depend on which other columns are computed
     with it -- the property N-sharding relies on (parallel_pool_test.dart's
