@@ -7,14 +7,15 @@
 // streams from HBM exactly once.
 //
 // Arithmetic.  Y[m,n] = sum_b s[n,b] * sum_{k in b} a[m,k] * (q[k,n] - z[n,b]).
-// Each activation row is turned into fixed point, X = rint(a * 2^S_m) with
-// |X| <= 2^22 (S_m per row, from the row's largest magnitude), and split into
-// three balanced base-256 digits X = c2*2^16 + c1*2^8 + c0.  The tensor core
-// multiplies q (0..15) by each digit and accumulates in int32 with no
-// rounding at all; the zero point enters as z * sum_k c_t, the fp32 block
-// scale once per block on the CUDA cores, and 2^-S_m at the end.  The only
-// roundings are the fixed-point step of a (2^-23 of the row's largest
-// magnitude) and the fp32 additions of the epilogue.
+// Each activation row is turned into fixed point per 512-k chunk,
+// X = rint(a * 2^S) with |X| <= 2^22 (S from the row's largest magnitude in
+// the chunk), and split into three balanced base-256 digits
+// X = c2*2^16 + c1*2^8 + c0.  The tensor core multiplies q (0..15) by each
+// digit and accumulates in int32 with no rounding at all.  Per block, the
+// epilogue forms D - z * sum(X) (the X build supplies sum(X) per block and
+// row), then applies the fp32 block scale, and 2^-S at the end.  The only
+// roundings are the fixed-point step of a (2^-23 of the chunk row's largest
+// magnitude) and the fp32 operations of the epilogue.
 //
 // MMA orientation:
 //   D[n, j] (128 TMEM lanes = 128 weight columns; NM = 16 or 32 columns j)
@@ -24,20 +25,24 @@
 //   of the region accumulates into its own D columns.  One MMA covers 128
 //   columns x 32 k = 4096 weights.
 //
-// Roles (448 threads, one CTA per SM):
-//   warp 12    TMA producer: per work item (128 columns x 512 k) the packed
+// Roles (576 threads, one CTA per SM):
+//   warp 16    TMA producer: per work item (128 columns x 512 k) the packed
 //              tile (2 boxes, 128-byte swizzle), its scales and zero points,
 //              into a shared-memory ring of up to 6 stages.
 //   warps 0-7  dequantisers, 2 groups x 4 lane quarters: thread (quarter q,
 //              lane l) owns weight column n = 32q + l.  Per 32-k stage: one
-//              conflict-free 16-byte shared load and two masks and a shift per
-//              8 weights turn nibbles into int8 bytes, then tcgen05.st of 8
-//              TMEM columns.  They also build X for each chunk.
-//   warp 13    TMEM allocator; an elect.sync leader issues one MMA per stage
-//              (A from TMEM) and tcgen05.commit frees A slots, X buffers and
-//              D buffers.
-//   warps 8-11 epilogue: tcgen05.ld of D, zero points, block scales, and the
-//              chunk partial of each column.
+//              conflict-free 16-byte shared load and one mask (and a shift)
+//              per 4 weights turn nibbles into bytes, then tcgen05.st of 8
+//              TMEM columns.  They also build X per chunk.  This role is
+//              instruction-bound: keep its per-weight work minimal.
+//   warp 17    TMEM allocator; an elect.sync leader waits once per item and
+//              issues its 16 MMAs (A from TMEM, stage table precomputed on
+//              the host); tcgen05.commit frees A, X and D buffers.
+//   warps 8-15 epilogue, 2 groups of 4 taking alternate items (tile-major:
+//              alternate tiles): tcgen05.ld of D, zero points, block scales,
+//              and the chunk partial of each column.
+// Synchronisation is batched per item because an mbarrier wait costs about
+// 200 cycles even when its phase has completed.
 // Decomposition: tile-major (a CTA owns whole 128-column tiles and loops
 // over the 512-k chunks, adding chunk partials in chunk order in shared
 // memory) when the tiles spread evenly over the SMs, else split-K (CTAs own
@@ -73,11 +78,13 @@ constexpr uint32_t kDCol = kAItems * kAItemCols;         // D starts at column 2
 constexpr uint32_t kDCols = kTmemCols - kDCol;          // 256 columns for D
 constexpr int kMaxBpi = kChunkK / kMinBs;               // blocks per item
 constexpr uint32_t kXBytesMax = 32 * kChunkK;           // X for NM = 32
-constexpr uint32_t kCsumBytes = kMaxBpi * 8 * 3 * 4;    // digit sums [bpi][M][3]
-// X buffer: X, digit sums, row max bits [8], row exponents [8]
-constexpr uint32_t kXBufBytes = kXBytesMax + ((kCsumBytes + 64 + 1023) & ~1023u);
+// X buffer: X, then the rows' largest-magnitude bits [8] and exponents [8],
+// the blocks' digit sums [bpi][M][3] (int) and their fp32 totals [bpi][M].
+constexpr uint32_t kXRmax = kXBytesMax, kXRexp = kXBytesMax + 32, kXCsum = kXBytesMax + 64;
+constexpr uint32_t kXXsum = kXCsum + kMaxBpi * 8 * 3 * 4;
+constexpr uint32_t kXBufBytes = (kXXsum + kMaxBpi * 8 * 4 + 1023) & ~1023u;
 constexpr size_t kSmemLimit = 227 * 1024;
-constexpr int kNonFinite = -100000;  // S_m of a row holding an inf or NaN
+constexpr int kNonFinite = -100000;  // exponent of a chunk row holding an inf or NaN
 
 // Compile-time shape of the X operand for M rows.
 template <int M>
@@ -97,7 +104,7 @@ struct TcParams {
   int grid_tiles;  // tile-major: tiles t = blockIdx.x + i*grid_tiles
   int tg;          // tile-major: tiles per group (y accumulators in smem)
   int cpc;         // split-K: CTAs per chunk
-  int bpi, regions, has_zp, nbst;
+  int bpi, regions, has_zp, z_rows, nbst;
   int a_vec;       // A 16-byte aligned and K % 4 == 0: 16-byte activation loads
   int nd;          // D buffers: 2, or 1 when an item needs more than 128 columns
   uint32_t dstride;
@@ -319,11 +326,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           return ok = false;
         }
         uint8_t* xbase = Xs + xbuf * kXBufBytes;
-        int* csum = reinterpret_cast<int*>(xbase + kXBytesMax);  // [bpi][M][3]
-        unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXBytesMax + kCsumBytes);  // [8]
-        int* rexp = reinterpret_cast<int*>(rmax + 8);                                  // [8]
-        for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
+        unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXRmax);  // [8]
+        int* rexp = reinterpret_cast<int*>(xbase + kXRexp);            // [8]
+        int* csum = reinterpret_cast<int*>(xbase + kXCsum);            // [bpi][M][3]
+        float* xsum = reinterpret_cast<float*>(xbase + kXXsum);        // [bpi][M]
         if (threadIdx.x < 8) rmax[threadIdx.x] = 0;
+        for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
         if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
         // Activations of the chunk, unit u = 4 consecutive k of row u / kU.
         // A warp's 32 units lie in one row.
@@ -395,11 +403,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                        : "memory");
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
                        : "memory");
-          int* cs = csum + (bl * M + m) * 3;
-          atomicAdd(cs + 0, s0);
-          atomicAdd(cs + 1, s1);
-          atomicAdd(cs + 2, s2);
+          // digit sums of the block: lanes of one block form an aligned run of
+          // min(32, bs / 4) units; add across it, one atomic per run and digit
+          for (int off = 1; off < p.bs / 4 && off < 32; off <<= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+          }
+          if ((lane & (min(32, p.bs / 4) - 1)) == 0) {
+            int* cs = csum + (bl * M + m) * 3;
+            atomicAdd(cs + 0, s0);
+            atomicAdd(cs + 1, s1);
+            atomicAdd(cs + 2, s2);
+          }
         }
+        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        // each block's sum of X per row, for the zero-point term z * sum X
+        for (int i = threadIdx.x; i < p.bpi * M; i += kDeWarps * 32)
+          xsum[i] = ((float)csum[i * 3 + 2] * 65536.0f + (float)csum[i * 3 + 1] * 256.0f) +
+                    (float)csum[i * 3];
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&xfull[xbuf]);
@@ -466,8 +488,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           record_error(p.err, KERR_WAIT_FULL);
           return ok = false;
         }
-        const int* rexp = reinterpret_cast<const int*>(Xs + (nbuild & 1) * kXBufBytes +
-                                                       kXBytesMax + kCsumBytes + 32);
+        const int* rexp = reinterpret_cast<const int*>(Xs + (nbuild & 1) * kXBufBytes + kXRexp);
 #pragma unroll
         for (int m = 0; m < M; m++) S_m[m] = rexp[m];
         cur = chunk;
@@ -477,8 +498,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         j++;
         return true;
       }
-      const int* csum =
-          reinterpret_cast<const int*>(Xs + ((nbuild - 1) & 1) * kXBufBytes + kXBytesMax);
       const int bst = j % p.nbst, d = j % p.nd;
       if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) || !mbar_wait(&dfull[d], (j / p.nd) & 1)) {
         record_error(p.err, KERR_WAIT_MMA);
@@ -490,7 +509,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int m = 0; m < M; m++) y[m] = 0.0f;
       const uint8_t* stg = Bs + bst * p.stage_bytes;
       const float* stile = reinterpret_cast<const float*>(stg + p.s_off);
-      const int first_b = chunk * p.bpi;
+      const float* xsum =
+          reinterpret_cast<const float*>(Xs + ((nbuild - 1) & 1) * kXBufBytes + kXXsum);
+      // zero points of the item's blocks for column nl: block b is nibble
+      // b + (first block odd) of zbits (the tile's rows hold block pairs)
+      uint64_t zbits = 0x8888888888888888ull;
+      int zsh = 0;
+      if (p.has_zp) {
+        zbits = 0;
+        for (int r = 0; r < p.z_rows; r++)
+          zbits |= (uint64_t)stg[p.z_off + r * kTile + nl] << (8 * r);
+        zsh = ((chunk * p.bpi) & 1) * 4;
+      }
       const uint32_t dcol = tmem + lane_addr + kDCol + d * p.dstride;
       for (int rg = 0; rg < p.regions; rg++) {
         uint32_t v[NM];
@@ -503,22 +533,16 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int slot = 0; slot < G; slot++) {
           const int b = rg * G + slot;
           if (b < p.bpi) {
-            int z = 8;
-            if (p.has_zp) {
-              const int bg = first_b + b;
-              const uint32_t zb = stg[p.z_off + ((bg >> 1) - (first_b >> 1)) * kTile + nl];
-              z = (bg & 1) ? (int)(zb >> 4) : (int)(zb & 0xF);
-            }
             const float sc = stile[b * kTile + nl];
+            const float zf = (float)((uint32_t)(zbits >> (4 * b + zsh)) & 0xFu);
 #pragma unroll
             for (int m = 0; m < M; m++) {
+              // D_t = sum q * c_t over the block (exact int32); the block's
+              // sum (q - z) * X is D - z * sum X
               const int c = (slot * M + m) * 3;
-              const int* cs = csum + (b * M + m) * 3;
-              const int d0 = (int)v[c] - z * cs[0];
-              const int d1 = (int)v[c + 1] - z * cs[1];
-              const int d2 = (int)v[c + 2] - z * cs[2];
-              const float val = ((float)d2 * 65536.0f + (float)d1 * 256.0f) + (float)d0;
-              y[m] = fmaf(sc, val, y[m]);
+              const float dq = ((float)(int)v[c + 2] * 65536.0f + (float)(int)v[c + 1] * 256.0f) +
+                               (float)(int)v[c];
+              y[m] = fmaf(sc, fmaf(-zf, xsum[b * M + m], dq), y[m]);
             }
           }
         }
@@ -745,6 +769,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   p.bpi = kChunkK / w.bs;
   p.has_zp = w.has_zp ? 1 : 0;
   const int z_rows = p.bpi >= 2 ? p.bpi / 2 : 1;
+  p.z_rows = z_rows;
   p.s_off = kPackedBytes;
   p.z_off = kPackedBytes + (uint32_t)p.bpi * kTile * 4;
   const uint32_t zbytes = p.has_zp ? (uint32_t)z_rows * kTile : 0;
