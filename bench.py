@@ -14,6 +14,9 @@ all-gathered over NCCL inside each op (strong scaling: total work fixed).
 zero points + 4*M*K (A) + 4*M*N_local (Y), summed over ranks.
 `e2e` = the same metric through the C ABI with host buffers (pinned), the
 host<->device copies inside the timed region.
+`prefill` = the metric's second half: the same five projections at M=2048
+in the fp16 tensor-core mode (the mode held to 2e-3 max-relative error),
+2*M*K*N flops per op over device time, TFLOP/s, whole job.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -37,6 +40,8 @@ METRIC = "MatMulNBits eff. HBM GB/s (M=1) and TFLOP/s (M=2048) at 1/2/4/8 B200"
 BS = 128
 SEED = 5
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+PREFILL_M = 2048
 
 
 def parse():
@@ -58,6 +63,14 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), "measured (burst bf16 GEMM)"
+    return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -263,6 +276,41 @@ def main():
     ms_step = e0.elapsed_time(e1) / args.steps
     big_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
 
+    # ---- prefill: M=2048 in the fp16 tensor-core mode ---------------------
+    from onnx_runtime_dart_b200 import _lib
+    pf_flags = _lib.flags_mode(_lib.MODES["mma_f16"])
+    Ap = {K: torch.randn(PREFILL_M, K, device=dev, generator=gen) for K in A}
+    Yp = {p.name: torch.empty(PREFILL_M, p.N, device=dev) for p in projs}
+
+    def step_prefill(ev=None):
+        for p in projs:
+            if ev is not None and p.name == big.name:
+                ev[0].record(stream)
+            sess.matmul_nbits(p.name, Ap[p.K], out=Yp[p.name], flags=pf_flags)
+            if ev is not None and p.name == big.name:
+                ev[1].record(stream)
+
+    pf_steps = max(1, min(args.steps, 10))
+    for _ in range(args.warmup):
+        step_prefill()
+    barrier()
+    pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(pf_steps)]
+    e0.record(stream)
+    for i in range(pf_steps):
+        step_prefill(pev[i])
+    e1.record(stream)
+    barrier()
+    pf_ms = e0.elapsed_time(e1) / pf_steps
+    pf_big_ms = sum(a.elapsed_time(b) for a, b in pev) / pf_steps
+    rank_flops = 0
+    for p in projs:
+        a, b = shard_range(p.N, rank, world)
+        rank_flops += 2 * PREFILL_M * p.K * (b - a)
+    ba, bb = shard_range(big.N, rank, world)
+    big_flops = 2 * PREFILL_M * big.K * (bb - ba)
+    del Ap, Yp
+
     # ---- end to end through the C ABI with host buffers -----------------
     hostA = {K: torch.randn(M, K, generator=torch.Generator().manual_seed(K)).pin_memory().numpy()
              for K in A}
@@ -283,16 +331,17 @@ def main():
     h2d = sum(4 * M * p.K for p in projs)
     d2h = sum(4 * M * p.N for p in projs)
 
-    stats = torch.tensor([ms_step, e2e_ms, big_ms], dtype=torch.float64)
-    tot = torch.tensor([rank_bytes, launches], dtype=torch.float64)
+    stats = torch.tensor([ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms], dtype=torch.float64)
+    tot = torch.tensor([rank_bytes, launches, rank_flops], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-    ms_step, e2e_ms, big_ms = stats.tolist()
-    job_bytes, launches = tot.tolist()
+    ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms = stats.tolist()
+    job_bytes, launches, job_flops = tot.tolist()
 
     if rank == 0:
         peak, peak_kind = peaks()
+        tpk, tpk_kind = tensor_peak()
         achieved = big_bytes / (big_ms * 1e-3) / 1e9
         traffic = None
         tp = os.path.join(ROOT, "profiles", "gemv_lm_head_traffic.json")
@@ -329,6 +378,15 @@ def main():
                     "ms_per_step": e2e_ms},
             "gpu_launches": int(launches),
             "clocks": clk,
+            "prefill": {
+                "value": job_flops / (pf_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "M": PREFILL_M, "mode": "mma_f16", "ms_per_step": pf_ms, "steps": pf_steps,
+                "roofline": {"bound": "tensor", "kernel": f"int4 dequant + tcgen05 GEMM ({big.name})",
+                             "achieved": big_flops / (pf_big_ms * 1e-3) / 1e12,
+                             "peak": tpk, "unit": "TFLOP/s",
+                             "frac": big_flops / (pf_big_ms * 1e-3) / 1e12 / tpk,
+                             "peak_kind": tpk_kind},
+            },
         }
         print(json.dumps(line), flush=True)
     sess.close()

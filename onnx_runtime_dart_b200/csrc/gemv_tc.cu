@@ -599,17 +599,17 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
     const int m = (int)(i / N), n = (int)(i % N);
     const float* src = part + (int64_t)m * npad + n;
     const int64_t cs = (int64_t)M * npad;
+    // all of a column's partials in flight at once (up to 32), then added in
+    // chunk order
     float acc = 0.0f;
-    int c = 0;
-    for (; c + 4 <= nch; c += 4) {  // four loads in flight, added in chunk order
-      const float p0 = src[(c + 0) * cs], p1 = src[(c + 1) * cs];
-      const float p2 = src[(c + 2) * cs], p3 = src[(c + 3) * cs];
-      acc = acc + p0;
-      acc = acc + p1;
-      acc = acc + p2;
-      acc = acc + p3;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < 32; c++) v[c] = c0 + c < nch ? __ldcg(src + (c0 + c) * cs) : 0.0f;
+#pragma unroll
+      for (int c = 0; c < 32; c++)
+        if (c0 + c < nch) acc = acc + v[c];
     }
-    for (; c < nch; c++) acc = acc + src[c * cs];
     Y[m * ldy + n] = acc;
   }
 }
