@@ -89,3 +89,22 @@ def shard_range(N: int, rank: int, world: int) -> Tuple[int, int]:
     per = ((N + world - 1) // world + 3) // 4 * 4
     a = min(N, per * rank)
     return a, min(N, a + per)
+
+
+def nbits_column_shard(B: np.ndarray, scales: np.ndarray, zp: Optional[np.ndarray], K: int,
+                       N: int, block_size: int, a: int, b: int):
+    """The MatMulNBits inputs of output columns [a, b) of a weight: packed
+    B rows, the columns' scales, and the zero points re-packed in the
+    reference's flat layout (nibble (n - a) * nb + blk, low nibble first),
+    which is what a rank of an N-sharded group holds after upload."""
+    nb = (K + block_size - 1) // block_size
+    Bs = np.ascontiguousarray(B.reshape(N, nb, block_size // 2)[a:b])
+    ss = np.ascontiguousarray(scales[a * nb:b * nb])
+    zs = None
+    if zp is not None:
+        nib = np.stack([zp & 0xF, zp >> 4], 1).ravel()[:N * nb]
+        part = nib[a * nb:b * nb]
+        if part.size % 2:
+            part = np.concatenate([part, np.zeros(1, np.uint8)])
+        zs = pack_nibbles(part)
+    return Bs, ss, zs
