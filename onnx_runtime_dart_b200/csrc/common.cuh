@@ -61,7 +61,7 @@ struct Weight {
   int w16_mode = -1;
   int64_t w16_rows = 0, w16_k = 0;
   int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
-  float* scales16 = nullptr; // nbits MMA: per-(col,blk) scale * 2^-col_exp
+  uint32_t* sz16 = nullptr;  // nbits f16 MMA: per-(blk,col) {1024 + z, scale * 2^-col_exp} as fp16
 };
 
 // ---- device layout of a MatMulNBits weight ---------------------------------
@@ -163,6 +163,13 @@ int launch_unshard(const float* g, float* Y, int64_t world, int64_t M, int64_t N
 
 // tcgen05 MMA path (16-bit operands, fp32 accumulation in TMEM).
 int mma_supported_shape(int64_t M, int64_t K);
+// Fused int4 prefill GEMM (fp16 MMA mode), csrc/gemm_nbits_tc.cu.
+bool nbits_gemm_f16_ok(const Weight& w);
+int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaStream_t st,
+                       int64_t* launches);
+int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
+                          const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
+                          int* err, int sm_count, cudaStream_t st, int64_t* launches);
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
                      int64_t ldy, int mode, cudaStream_t st);
 int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, bool transA,

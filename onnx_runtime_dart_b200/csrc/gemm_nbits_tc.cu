@@ -1,0 +1,382 @@
+// Prefill MatMulNBits on tcgen05 tensor cores with the int4 dequantisation
+// fused into the GEMM main loop (fp16 MMA mode).
+//
+//   Y[M, N] = 2^(e_m + f_n) * sum_k A16[m, k] * W16[n, k]
+//   W16[n, k] = fp16((q - z) * fp16(scale * 2^-f_n))
+//
+// replacing, for prefill-sized M, the reference's dequantisation of all of B
+// into fp32 followed by matmulKernel (onnx_qlinear_ops.dart:127-154,
+// gemm_kernel_simd.dart:27-309).  A16 is the activation converted once per
+// call to fp16 with a power-of-two row normalisation e_m; f_n normalises
+// each weight column so its largest |(q - z) * scale| lies in [2^14, 2^15).
+// Packed weights are read once per 128-row band of A straight from their
+// upload layout; no 16-bit copy of the weights is written to HBM.
+//
+// Persistent kernel, one CTA per SM, tiles of 128 (m) x 256 (n), 64-k stages:
+//   warp 0      TMA producer: A tile (128 x 64 fp16, 128-byte swizzle), the
+//               packed int4 tile (256 columns x 32 bytes) and the stage's
+//               {1024 + z, scale'} table (fp16 pairs) into a 4-stage ring
+//   warps 2-9   converters: thread n owns weight column n of the tile; per
+//               8 weights two masks, four byte permutes (nibble | 0x6400 is
+//               the fp16 value 1024 + q), four exact subtractions of
+//               1024 + z and four multiplies by the scale (one rounding),
+//               stored as the MMA's K-major 128-byte-swizzled B tile
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32
+//               accumulators); an elect.sync leader waits once per stage and
+//               issues 4 MMAs (M=128, N=256, K=16), tcgen05.commit frees the
+//               stage and the converted tile
+//   warps 10-13 epilogue: tcgen05.ld of the finished accumulator while the
+//               MMAs fill the other one, exact 2^(e_m + f_n) scaling, and
+//               coalesced stores through a per-warp shared-memory transpose
+// Every wait is bounded; on expiry the kernel records an error and returns.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace ortc {
+namespace {
+
+constexpr int PBM = 128, PBN = 256, PBK = 64;
+constexpr int kRaw = 4;                              // producer ring depth
+constexpr int kConv = 3;                             // converted B tiles
+constexpr uint32_t kABytes = PBM * PBK * 2;          // 16 KB fp16 A tile
+constexpr uint32_t kQBytes = PBN * PBK / 2;          // 8 KB packed int4 tile
+constexpr uint32_t kSZBytes = PBN * 4 * 4;           // up to 4 blocks per stage
+constexpr uint32_t kRawBytes = kABytes + kQBytes + kSZBytes;  // 28 KB
+constexpr uint32_t kCBytes = PBN * PBK * 2;          // 32 KB fp16 B tile
+constexpr int kConvWarp0 = 2, kConvWarps = 8, kEpiWarp0 = 10;
+constexpr int kThreadsP = 14 * 32;
+constexpr uint32_t kEpiFloats = 32 * 33;             // per epilogue warp
+constexpr size_t kSmemP =
+    1024 + kRaw * kRawBytes + kConv * kCBytes + 4 * kEpiFloats * 4 + 256;
+
+struct PParams {
+  float* Y;
+  int64_t ldy;
+  const int* row_exp;  // [M]
+  const int* col_exp;  // [N]
+  int* err;
+  int M, N, K;
+  int m_tiles, tiles;
+  int bps;       // quantisation blocks per 64-k stage (>= 1)
+  int bs_shift;  // log2(block size)
+  uint32_t stage_tx;
+};
+
+__device__ __forceinline__ float pow2f(int e) {
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+__device__ __forceinline__ float scale_pow2(float v, int e) {
+  while (e > 100) { v *= pow2f(100); e -= 100; }
+  while (e < -100) { v *= pow2f(-100); e += 100; }
+  return v * pow2f(e);
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+// (h - zz) * s on two fp16 lanes: the subtraction of small integers is exact,
+// the product is rounded once.
+__device__ __forceinline__ uint32_t deq2(uint32_t h, uint32_t zz, uint32_t s) {
+  uint32_t d;
+  asm("{\n\t.reg .b32 t;\n\t"
+      "sub.rn.f16x2 t, %1, %2;\n\t"
+      "mul.rn.f16x2 %0, t, %3;\n\t}"
+      : "=r"(d)
+      : "r"(h), "r"(zz), "r"(s));
+  return d;
+}
+
+__global__ void __launch_bounds__(kThreadsP, 1)
+    nbits_gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ CUtensorMap tmSZ, const PParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* raw = smem;
+  uint8_t* conv = smem + kRaw * kRawBytes;
+  float* epi = reinterpret_cast<float*>(conv + kConv * kCBytes);
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(epi + 4 * kEpiFloats);
+  uint64_t* raw_empty = raw_full + kRaw;
+  uint64_t* conv_full = raw_empty + kRaw;
+  uint64_t* conv_empty = conv_full + kConv;
+  uint64_t* tm_full = conv_empty + kConv;
+  uint64_t* tm_empty = tm_full + 2;
+  uint64_t* fin = tm_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (p.K + PBK - 1) / PBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRaw; s++) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 1);
+    }
+    for (int c = 0; c < kConv; c++) {
+      mbar_init(&conv_full[c], kConvWarps);
+      mbar_init(&conv_empty[c], 1);
+    }
+    for (int d = 0; d < 2; d++) {
+      mbar_init(&tm_full[d], 1);
+      mbar_init(&tm_empty[d], 4);
+    }
+    mbar_init(fin, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmA);
+      prefetch_tensormap(&tmQ);
+      prefetch_tensormap(&tmSZ);
+      uint32_t g = 0;
+      int armed[kRaw];
+      for (int s = 0; s < kRaw; s++) armed[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        const int m0 = (t % p.m_tiles) * PBM, n0 = (t / p.m_tiles) * PBN;
+        for (int kb = 0; kb < nk; kb++, g++) {
+          const int s = g % kRaw;
+          const uint32_t ph = (g / kRaw) & 1;
+          if (!mbar_wait(&raw_empty[s], ph ^ 1)) {
+            record_error(p.err, KERR_WAIT_EMPTY);
+            ok = false;
+            break;
+          }
+          uint8_t* st = raw + s * kRawBytes;
+          armed[s] = (int)ph;
+          mbar_arrive_expect_tx(&raw_full[s], p.stage_tx);
+          tma_load_2d(st, &tmA, &raw_full[s], kb * PBK, m0);
+          tma_load_2d(st + kABytes, &tmQ, &raw_full[s], kb * (PBK / 2), n0);
+          tma_load_2d(st + kABytes + kQBytes, &tmSZ, &raw_full[s], n0,
+                      (kb * PBK) >> p.bs_shift);
+        }
+      }
+      if (!ok)
+        for (int s = 0; s < kRaw; s++)
+          if (armed[s] >= 0 && !mbar_wait(&raw_full[s], (uint32_t)armed[s]))
+            record_error(p.err, KERR_WAIT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16(0, PBM, PBN);
+      uint32_t g = 0, tcount = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, tcount++) {
+        const int d = tcount & 1;
+        if (!mbar_wait(&tm_empty[d], ((tcount >> 1) & 1) ^ 1)) {
+          record_error(p.err, KERR_WAIT_EMPTY);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dt = tmem + d * PBN;
+        for (int kb = 0; kb < nk; kb++, g++) {
+          const int s = g % kRaw, c = g % kConv;
+          if (!mbar_wait(&conv_full[c], (g / kConv) & 1)) {
+            record_error(p.err, KERR_WAIT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(raw + s * kRawBytes);
+          const uint32_t sb = smem_u32(conv + c * kCBytes);
+#pragma unroll
+          for (int kk = 0; kk < PBK / 16; kk++)
+            mma_f16_ss(dt, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), idesc,
+                       (kb | kk) != 0);
+          mma_commit(&raw_empty[s]);
+          mma_commit(&conv_empty[c]);
+        }
+        if (ok) mma_commit(&tm_full[d]);
+      }
+      mma_commit(fin);
+      if (!mbar_wait(fin, 0)) record_error(p.err, KERR_WAIT_MMA);
+    }
+    __syncwarp();
+  } else if (warp < kConvWarp0 + kConvWarps) {
+    // ---------------- converters: thread n owns weight column n ----------
+    const int n = threadIdx.x - kConvWarp0 * 32;
+    const uint32_t rowoff = (uint32_t)((n >> 3) * 1024 + (n & 7) * 128);
+    const int sw = n & 7;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nk; kb++, g++) {
+        const int s = g % kRaw, c = g % kConv;
+        if (!mbar_wait(&raw_full[s], (g / kRaw) & 1) ||
+            !mbar_wait(&conv_empty[c], ((g / kConv) & 1) ^ 1)) {
+          record_error(p.err, KERR_WAIT_FULL);
+          ok = false;
+          break;
+        }
+        const uint8_t* st = raw + s * kRawBytes;
+        const uint32_t qa = smem_u32(st + kABytes) + n * 32;
+        const uint32_t* sz = reinterpret_cast<const uint32_t*>(st + kABytes + kQBytes);
+        const uint4 w0 = lds128(qa), w1 = lds128(qa + 16);
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t cb = smem_u32(conv + c * kCBytes) + rowoff;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          // word i holds k 8i..8i+7; its block within the stage's table
+          const uint32_t v = sz[((8 * i) >> p.bs_shift) * PBN + n];
+          const uint32_t zz = prmt(v, v, 0x1010), sc = prmt(v, v, 0x3232);
+          const uint32_t lo = words[i] & 0x0F0F0F0Fu, hi = (words[i] >> 4) & 0x0F0F0F0Fu;
+          const uint32_t r0 = deq2(prmt(lo, 0x64646464u, 0x4140), zz, sc);  // k0, k1
+          const uint32_t r1 = deq2(prmt(lo, 0x64646464u, 0x4342), zz, sc);  // k2, k3
+          const uint32_t r2 = deq2(prmt(hi, 0x64646464u, 0x4140), zz, sc);  // k4, k5
+          const uint32_t r3 = deq2(prmt(hi, 0x64646464u, 0x4342), zz, sc);  // k6, k7
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(cb + ((i ^ sw) << 4)),
+                       "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv_full[c]);
+      }
+    }
+  } else {
+    // ---------------- epilogue ---------------------------------------------
+    const int q = warp & 3;
+    float* buf = epi + (warp - kEpiWarp0) * kEpiFloats;
+    uint32_t tcount = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, tcount++) {
+      const int m0 = (t % p.m_tiles) * PBM, n0 = (t / p.m_tiles) * PBN;
+      const int d = tcount & 1;
+      if (!mbar_wait(&tm_full[d], (tcount >> 1) & 1)) {
+        record_error(p.err, KERR_WAIT_MMA);
+        break;
+      }
+      tc_fence_after();
+      const int rbase = m0 + q * 32;
+      const int my_e = rbase + lane < p.M ? p.row_exp[rbase + lane] : 0;
+      for (int c0 = 0; c0 < PBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + d * PBN + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) buf[lane * 33 + j] = __uint_as_float(r[j]);
+        __syncwarp();
+        const int n = n0 + c0 + lane;
+        const int f = n < p.N ? p.col_exp[n] : 0;
+#pragma unroll 4
+        for (int j = 0; j < 32; j++) {
+          const int e = __shfl_sync(0xffffffffu, my_e, j);
+          const int row = rbase + j;
+          if (row < p.M && n < p.N)
+            p.Y[(int64_t)row * p.ldy + n] = scale_pow2(buf[j * 33 + lane], e + f);
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[d]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// {1024 + z, scale * 2^-f_n} per (block, column) as two fp16 halves, block
+// major like the scales.
+__global__ void nbits_sz16_kernel(const float* __restrict__ S, int64_t s_pitch,
+                                  const uint8_t* __restrict__ Z, int64_t z_pitch, int nb, int nl,
+                                  const int* __restrict__ col_exp, uint32_t* __restrict__ out) {
+  const int64_t total = (int64_t)nb * nl;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i / nl), n = (int)(i % nl);
+    const float z = Z ? (float)nbits_zp(Z, z_pitch, n, b) : 8.0f;
+    const float s = scale_pow2(S[(int64_t)b * s_pitch + n], -col_exp[n]);
+    const uint32_t zh = __half_as_ushort(__float2half_rn(1024.0f + z));
+    const uint32_t sh = __half_as_ushort(__float2half_rn(s));
+    out[(int64_t)b * s_pitch + n] = zh | (sh << 16);
+  }
+}
+
+}  // namespace
+
+bool nbits_gemm_f16_ok(const Weight& w) {
+  const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
+  return w.nl > 0 && col_bytes % 16 == 0 && w.bs >= 16 && (w.bs & (w.bs - 1)) == 0;
+}
+
+int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaStream_t st,
+                       int64_t* launches) {
+  const int64_t total = (int64_t)w.nb * w.nl;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 4096);
+  nbits_sz16_kernel<<<blocks, 256, 0, st>>>(w.scales, w.s_pitch, w.has_zp ? w.zp : nullptr,
+                                            w.z_pitch, w.nb, (int)w.nl, col_exp, out);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
+                          const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
+                          int* err, int sm_count, cudaStream_t st, int64_t* launches) {
+  if (M == 0 || w.nl == 0) return ORT_CUDA_OK;
+  const int64_t K = w.K, nl = w.nl, col_bytes = (int64_t)w.nb * w.bs / 2;
+  CUtensorMap tmA, tmQ, tmSZ;
+  int rc = encode_tma_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A16, (uint64_t)K, (uint64_t)M,
+                         (uint64_t)K * 2, PBK, PBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tma_2d(&tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes, (uint64_t)nl,
+                     (uint64_t)col_bytes, PBK / 2, PBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  int bs_shift = 0;
+  while ((1 << bs_shift) < w.bs) bs_shift++;
+  const int bps = w.bs >= PBK ? 1 : PBK / w.bs;
+  rc = encode_tma_2d(&tmSZ, CU_TENSOR_MAP_DATA_TYPE_UINT32, sz16, (uint64_t)nl, (uint64_t)w.nb,
+                     (uint64_t)w.s_pitch * 4, PBN, bps, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  PParams p;
+  p.Y = Y;
+  p.ldy = ldy;
+  p.row_exp = row_exp;
+  p.col_exp = col_exp;
+  p.err = err;
+  p.M = (int)M;
+  p.N = (int)nl;
+  p.K = (int)K;
+  p.m_tiles = (int)((M + PBM - 1) / PBM);
+  p.tiles = p.m_tiles * (int)((nl + PBN - 1) / PBN);
+  p.bps = bps;
+  p.bs_shift = bs_shift;
+  p.stage_tx = kABytes + kQBytes + (uint32_t)bps * PBN * 4;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    ORTC_CUDA(cudaFuncSetAttribute(nbits_gemm_f16_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemP));
+    configured |= 1ull << (dev & 63);
+  }
+  const int grid = std::min(p.tiles, sm_count);
+  nbits_gemm_f16_kernel<<<grid, kThreadsP, kSmemP, st>>>(tmA, tmQ, tmSZ, p);
+  ORTC_CUDA(cudaGetLastError());
+  (*launches)++;
+  return ORT_CUDA_OK;
+}
+
+}  // namespace ortc

@@ -393,6 +393,29 @@ int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
   if (w.nl == 0 || M == 0) return ORT_CUDA_OK;
   const bool bf16 = mode == ORT_CUDA_MODE_MMA_BF16;
   const int64_t K = w.K, nl = w.nl;
+  if (!bf16 && nbits_gemm_f16_ok(w)) {
+    // fp16 mode: dequantisation fused into the GEMM; the per-(block, column)
+    // zero-point / scale table and the column exponents are made once per
+    // session and kept with the weight.
+    if (w.sz16 == nullptr) {
+      if (w.col_exp == nullptr) ORTC_CUDA(cudaMalloc(&w.col_exp, (size_t)nl * 4));
+      ORTC_CUDA(cudaMalloc(&w.sz16, (size_t)w.nb * w.s_pitch * 4));
+      nbits_col_exp_kernel<<<(unsigned)((nl + 255) / 256), 256, 0, st>>>(w.scales, w.s_pitch, w.nb,
+                                                                          (int)nl, w.col_exp);
+      ORTC_CUDA(cudaGetLastError());
+      s->launches++;
+      int rc = prepare_nbits_sz16(w, w.col_exp, w.sz16, st, &s->launches);
+      if (rc) return rc;
+    }
+    int rc = ensure_kscratch(s, a_scratch_bytes(M, K));
+    if (rc) return rc;
+    uint16_t* A16;
+    int* rexp;
+    rc = convert_a(s, A, M, K, false, false, 0, &A16, &rexp, st);
+    if (rc) return rc;
+    return launch_nbits_gemm_f16(w, A16, rexp, M, w.sz16, w.col_exp, Y, ldy, s->err_dev,
+                                 s->sm_count, st, &s->launches);
+  }
   const size_t a_bytes = a_scratch_bytes(M, K);
   const size_t w_bytes = al256((size_t)(nl * K) * 2);
   const size_t e_bytes = al256((size_t)nl * 4);

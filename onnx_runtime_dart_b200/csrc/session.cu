@@ -98,7 +98,7 @@ bool is_pinned_host(const void* p) {
 }
 
 int free_weight(ortc::Weight& w) {
-  void* ptrs[] = {w.B, w.scales, w.zp, w.W, w.W16, w.col_exp, w.scales16};
+  void* ptrs[] = {w.B, w.scales, w.zp, w.W, w.W16, w.col_exp, w.sz16};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   w = ortc::Weight();

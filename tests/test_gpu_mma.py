@@ -104,6 +104,18 @@ def test_nbits_prefill_mma(sess, mode, M, K, N, bs, zp):
     _check(O.matmul_nbits(A, B, s.astype(np.float32), z, K, N, 4, bs, threads=8), y, mode)
 
 
+@pytest.mark.parametrize("mode", ["mma_f16", "mma_bf16"])
+def test_nbits_prefill_mma_bs16_fp32_scales(sess, mode):
+    """Four quantisation blocks per 64-k stage, fp32 scales, ragged M and N."""
+    rng = np.random.default_rng(77)
+    M, K, N, bs = 300, 1024, 777, 16
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("nb16", B, s, z, k=K, n=N, block_size=bs)
+    y = sess.matmul_nbits("nb16", A, flags=_flags(mode))
+    _check(O.matmul_nbits(A, B, s, z, K, N, 4, bs, threads=8), y, mode)
+
+
 def test_nbits_prefill_full_size_vs_torch(sess):
     """Llama-3-8B down projection (14336 -> 4096) at M=2048 against an fp64
     torch reference of the dequantised weight."""
