@@ -202,7 +202,11 @@ int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
     if (ms > timeout_ms)
       return fail(ORT_CUDA_ERR_TIMEOUT, "NCCL did not finish within " +
                                             std::to_string(timeout_ms) + " ms");
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    // an enqueue completes in microseconds: spin first, sleep only when long
+    if (ms < 2)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
@@ -214,6 +218,17 @@ int gather_y(ort_cuda_session* s, const float* local, float* gathered, float* Y,
                                  (ncclComm_t)s->nccl, s->stream);
   if (r != ncclSuccess && r != ncclInProgress)
     return fail(ORT_CUDA_ERR_NCCL, std::string("ncclAllGather: ") + nccl()->GetErrorString(r));
+  if (r == ncclInProgress) {
+    // Non-blocking communicator: the collective is on the stream only once
+    // the call has completed; nothing may follow it (on the stream or the
+    // communicator) before that.
+    const int rc = nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
+    if (rc) {
+      nccl()->CommAbort((ncclComm_t)s->nccl);
+      s->nccl = nullptr;
+      return rc;
+    }
+  }
   return launch_unshard(gathered, Y, s->world, M, Ns, N, s->stream, &s->launches);
 }
 
