@@ -111,6 +111,14 @@ struct ort_cuda_session {
   // grow-only kernel scratch for split-K partials (no initial value needed)
   void* kscratch = nullptr;
   size_t kscratch_bytes = 0;
+  // N-sharded sessions: peer-memory exchange of Y (csrc/p2p.cu).  xbuf holds
+  // 8 ready flags (one per peer, 256 bytes) then two halves of xcap floats;
+  // xpeer[r] is rank r's xbuf mapped into this process (xpeer[rank] = xbuf).
+  void* xbuf = nullptr;
+  void* xpeer[8] = {};
+  size_t xcap = 0;
+  uint64_t xepoch = 0;
+  bool p2p_ok = false;
   // host-mapped error word kernels write when a bounded wait gives up
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -123,6 +131,16 @@ namespace ortc {
 int ensure_ws(ort_cuda_session* s, size_t bytes);
 int ensure_pinned(ort_cuda_session* s, size_t bytes);
 int ensure_kscratch(ort_cuda_session* s, size_t bytes);
+// Reads and clears the kernels' error word (session.cu).
+int check_kernel_error(ort_cuda_session* s);
+// Waits for the session stream; with a communicator, bounded by the
+// session timeout (the communicator is aborted on expiry).
+int bounded_sync(ort_cuda_session* s);
+// Peer-memory all-gather of Y for N-sharded sessions (p2p.cu).
+int p2p_setup(ort_cuda_session* s);
+void p2p_teardown(ort_cuda_session* s);
+float* p2p_next_slot(ort_cuda_session* s, int64_t floats);
+int p2p_gather(ort_cuda_session* s, int64_t M, int64_t Ns, int64_t N, float* Y);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: a 2-D
 // row-major tensor [d1][d0] with row pitch stride1 bytes, box b0 x b1.

@@ -25,4 +25,8 @@ struct NcclApi {
 // Returns the resolved table, or nullptr (with the error text set).
 const NcclApi* nccl();
 
+// Polls a non-blocking communicator until its last call has completed,
+// bounded by timeout_ms (session.cu).
+int nccl_wait_ready(ncclComm_t comm, int timeout_ms);
+
 }  // namespace ortc

@@ -1,0 +1,200 @@
+// Peer-memory all-gather of Y for N-sharded sessions.
+//
+// The reference's GemmPool writes every worker's output columns straight
+// into the shared result (parallel_pool.dart:121-205); across GPUs the
+// equivalent is each rank reading the other ranks' column slices over
+// NVLink.  Every rank owns an exchange buffer (ready flags + two halves);
+// at session start the buffers are exported with CUDA IPC and the handles
+// swapped once through NCCL.  Per operation the compute kernel writes the
+// rank's [M, Ns] slice into half (epoch & 1) of its own buffer; then
+// p2p_gather_kernel posts the epoch into every peer's flag slot for this
+// rank, waits (bounded) until every peer has posted the same epoch here, and
+// reads all slices with plain peer loads into Y [M, N].  A rank's next write
+// into a half that a peer may still be reading is two epochs later, after
+// that peer has posted the intervening epoch, which it does only after its
+// own read finished: two halves are enough.  No NCCL and no multicast is on
+// the per-operation path.
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "nccl_dl.cuh"
+#include "ptx.cuh"
+
+namespace ortc {
+namespace {
+
+constexpr size_t kFlagBytes = 256;
+constexpr size_t kDefaultCapFloats = size_t(4) << 20;  // 16 MB per half
+
+struct P2PArgs {
+  const float* src[8];            // rank r's half for this epoch
+  unsigned long long* flag[8];    // rank r's flag slot for this rank
+  const unsigned long long* mine; // this rank's flags, slot r written by rank r
+  float* Y;
+  int64_t ldy;
+  int M, Ns, N, rank, world;
+  unsigned long long epoch;
+  int* err;
+};
+
+__global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    // this rank's slice (written by an earlier kernel) before the flag
+    __threadfence_system();
+    for (int r = 0; r < a.world; r++)
+      if (r != a.rank)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(a.epoch)
+                     : "memory");
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < a.world && ok; r++) {
+      if (r == a.rank) continue;
+      for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.mine + r) : "memory");
+        if (v >= a.epoch) break;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          record_error(a.err, KERR_WAIT_PEER);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int64_t total = (int64_t)a.M * a.N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / a.N), n = (int)(i % a.N);
+    const int r = n / a.Ns, j = n - r * a.Ns;
+    a.Y[m * a.ldy + n] = __ldcv(a.src[r] + (int64_t)m * a.Ns + j);
+  }
+}
+
+// Bounded completion of a non-blocking NCCL call, then of the stream.
+int nccl_finish(ort_cuda_session* s, ncclResult_t r) {
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ORT_CUDA_ERR_NCCL, std::string("NCCL: ") + nccl()->GetErrorString(r));
+  if (r == ncclInProgress) {
+    const int rc = nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
+    if (rc) return rc;
+  }
+  return bounded_sync(s);
+}
+
+// Every rank contributes `bytes` at `mine`; returns all ranks' bytes.
+int host_allgather(ort_cuda_session* s, const void* mine, size_t bytes, std::vector<char>* all) {
+  void* d = nullptr;
+  ORTC_CUDA(cudaMalloc(&d, bytes * s->world));
+  int rc = ORT_CUDA_OK;
+  cudaError_t e = cudaMemcpy((char*)d + bytes * s->rank, mine, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy");
+  if (rc == ORT_CUDA_OK)
+    rc = nccl_finish(s, nccl()->AllGather((char*)d + bytes * s->rank, d, bytes, ncclUint8,
+                                          (ncclComm_t)s->nccl, s->stream));
+  if (rc == ORT_CUDA_OK) {
+    all->resize(bytes * s->world);
+    e = cudaMemcpy(all->data(), d, bytes * s->world, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = cuda_fail(e, "cudaMemcpy");
+  }
+  cudaFree(d);
+  return rc;
+}
+
+}  // namespace
+
+int p2p_setup(ort_cuda_session* s) {
+  s->p2p_ok = false;
+  if (s->world < 2 || s->world > 8 || !s->nccl) return ORT_CUDA_OK;
+  size_t cap = kDefaultCapFloats;
+  if (const char* env = std::getenv("ORT_CUDA_P2P_FLOATS")) cap = std::strtoull(env, nullptr, 10);
+  ORTC_CUDA(cudaMalloc(&s->xbuf, kFlagBytes + 2 * cap * 4));
+  ORTC_CUDA(cudaMemset(s->xbuf, 0, kFlagBytes));
+  s->xcap = cap;
+  cudaIpcMemHandle_t h;
+  bool ok = cudaIpcGetMemHandle(&h, s->xbuf) == cudaSuccess;
+  if (!ok) std::memset(&h, 0, sizeof(h));
+  std::vector<char> handles;
+  int rc = host_allgather(s, &h, sizeof(h), &handles);
+  if (rc) return rc;
+  for (int r = 0; r < s->world; r++) {
+    if (r == s->rank) {
+      s->xpeer[r] = s->xbuf;
+      continue;
+    }
+    cudaIpcMemHandle_t hr;
+    std::memcpy(&hr, handles.data() + r * sizeof(hr), sizeof(hr));
+    void* p = nullptr;
+    if (ok && cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess)
+      s->xpeer[r] = p;
+    else
+      ok = false;
+  }
+  cudaGetLastError();  // a refused mapping only disables this path
+  // every rank must take the same path: use peer memory only if all can
+  const char mine = ok ? 1 : 0;
+  std::vector<char> oks;
+  rc = host_allgather(s, &mine, 1, &oks);
+  if (rc) return rc;
+  bool all_ok = true;
+  for (char c : oks) all_ok = all_ok && c == 1;
+  s->p2p_ok = all_ok;
+  return ORT_CUDA_OK;
+}
+
+void p2p_teardown(ort_cuda_session* s) {
+  if (s->xbuf && s->nccl) {
+    // no rank unmaps or frees before every rank's last read has finished
+    std::vector<char> all;
+    const char one = 1;
+    host_allgather(s, &one, 1, &all);
+  }
+  for (int r = 0; r < 8; r++)
+    if (s->xpeer[r] && r != s->rank) cudaIpcCloseMemHandle(s->xpeer[r]);
+  if (s->xbuf) cudaFree(s->xbuf);
+  s->xbuf = nullptr;
+  for (auto& p : s->xpeer) p = nullptr;
+  s->p2p_ok = false;
+}
+
+float* p2p_next_slot(ort_cuda_session* s, int64_t floats) {
+  if (!s->p2p_ok || (size_t)floats > s->xcap) return nullptr;
+  const uint64_t e = s->xepoch + 1;
+  return (float*)((char*)s->xbuf + kFlagBytes) + (e & 1) * s->xcap;
+}
+
+int p2p_gather(ort_cuda_session* s, int64_t M, int64_t Ns, int64_t N, float* Y) {
+  const uint64_t e = ++s->xepoch;
+  P2PArgs a;
+  for (int r = 0; r < 8; r++) {
+    a.src[r] = nullptr;
+    a.flag[r] = nullptr;
+  }
+  for (int r = 0; r < s->world; r++) {
+    a.src[r] = (const float*)((char*)s->xpeer[r] + kFlagBytes) + (e & 1) * s->xcap;
+    a.flag[r] = (unsigned long long*)s->xpeer[r] + s->rank;
+  }
+  a.mine = (const unsigned long long*)s->xbuf;
+  a.Y = Y;
+  a.ldy = N;
+  a.M = (int)M;
+  a.Ns = (int)Ns;
+  a.N = (int)N;
+  a.rank = s->rank;
+  a.world = s->world;
+  a.epoch = e;
+  a.err = s->err_dev;
+  const int64_t total = M * N;
+  const unsigned blocks =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, s->sm_count * 2));
+  p2p_gather_kernel<<<blocks, 256, 0, s->stream>>>(a);
+  ORTC_CUDA(cudaGetLastError());
+  s->launches++;
+  return ORT_CUDA_OK;
+}
+
+}  // namespace ortc

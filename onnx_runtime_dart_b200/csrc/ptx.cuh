@@ -14,6 +14,7 @@ enum KernelError : int {
   KERR_WAIT_EMPTY = 2,  // producer gave up waiting for a free stage
   KERR_WAIT_MMA = 3,    // tensor-core commit never arrived
   KERR_WAIT_DRAIN = 4,  // in-flight copies did not land before exit
+  KERR_WAIT_PEER = 5,   // a peer GPU's ready flag did not arrive
 };
 
 // Upper bound of any single wait (ns of %globaltimer).  Every legitimate

@@ -130,6 +130,8 @@ void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_
 
 // A kernel whose bounded wait gave up wrote a code into the host-mapped
 // error word; report it once.
+}  // namespace
+
 int check_kernel_error(ort_cuda_session* s) {
   volatile int* e = s->err_host;
   if (!e || *e == 0) return ORT_CUDA_OK;
@@ -209,6 +211,8 @@ int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
       std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
+
+namespace {
 
 // All-gather this rank's [M, Ns] slice (at `local`) into Y [M, N].
 int gather_y(ort_cuda_session* s, const float* local, float* gathered, float* Y, int64_t M,
@@ -372,6 +376,13 @@ ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void*
                         "): " + msg);
   }
   s->nccl = comm;
+  rc = p2p_setup(s);
+  if (rc) {
+    std::string msg = ort_cuda_last_error();
+    ort_cuda_close(s);
+    *out = nullptr;
+    return fail(rc, "peer-memory setup: " + msg);
+  }
   return ORT_CUDA_OK;
 }
 
@@ -387,6 +398,7 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->kscratch) cudaFree(s->kscratch);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
+  p2p_teardown(s);
   if (s->nccl) {
     nccl()->CommFinalize((ncclComm_t)s->nccl);
     nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
@@ -737,12 +749,16 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
     dY = (float*)(ws + L.y);
     y_pinned = is_pinned_host(Y);
   }
-  float* yloc = sharded ? (float*)(ws + L.yloc) : dY;
+  // sharded: the rank's slice goes to its peer-visible exchange half when
+  // that fits (gathered by peer loads), else to the workspace (NCCL)
+  float* xslot = sharded ? p2p_next_slot(s, M * w.ns) : nullptr;
+  float* yloc = sharded ? (xslot ? xslot : (float*)(ws + L.yloc)) : dY;
   const int64_t ldy = sharded ? w.ns : N;
   rc = compute(dA, dC, yloc, ldy);
   if (rc) return rc;
   if (sharded) {
-    rc = gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
+    rc = xslot ? p2p_gather(s, M, w.ns, N, dY)
+               : gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
     if (rc) return rc;
   }
   if (host) {
