@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline time budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time op-by-op calls instead of a CUDA graph of the timed steps")
     return ap.parse_args()
 
 
@@ -245,13 +247,26 @@ def main():
     ba, bb = shard_range(big.N, rank, world)
     big_bytes = nbits_bytes(big.K, bb - ba, BS, M, 2, True)
 
+    def record(event):
+        # inside a capture, an external event node: recorded on every replay
+        # and readable with elapsed_time, like a plain record
+        if capturing[0]:
+            from cuda.bindings import runtime as rt
+            err, = rt.cudaEventRecordWithFlags(event.cuda_event, stream.cuda_stream,
+                                               rt.cudaEventRecordExternal)
+            assert int(err) == 0, err
+        else:
+            event.record(stream)
+
+    capturing = [False]
+
     def step(ev=None):
         for p in projs:
             if ev is not None and p.name == big.name:
-                ev[0].record(stream)
+                record(ev[0])
             sess.matmul_nbits(p.name, A[p.K], out=Y[p.name])
             if ev is not None and p.name == big.name:
-                ev[1].record(stream)
+                record(ev[1])
 
     def barrier():
         torch.cuda.synchronize()
@@ -264,16 +279,37 @@ def main():
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
-    launches0 = sess.launch_count()
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gid = None
+    if not args.eager:
+        # the K timed steps recorded once (with their lm_head event pairs)
+        # and replayed with one launch; one untimed replay first
+        for a, b in kev:  # torch creates its events on first use
+            a.record(stream)
+            b.record(stream)
+        barrier()
+        sess.graph_begin()
+        capturing[0] = True
+        for i in range(args.steps):
+            step(kev[i])
+        capturing[0] = False
+        gid = sess.graph_end()
+        sess.graph_launch(gid)
+        barrier()
+    launches0 = sess.launch_count()
     e0.record(stream)
-    for i in range(args.steps):
-        step(kev[i])
+    if gid is not None:
+        sess.graph_launch(gid)
+    else:
+        for i in range(args.steps):
+            step(kev[i])
     e1.record(stream)
     barrier()
     launches = sess.launch_count() - launches0
+    if gid is not None:
+        sess.graph_drop(gid)
     clk = clocks.stop()
     ms_step = e0.elapsed_time(e1) / args.steps
     big_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
@@ -367,6 +403,8 @@ def main():
                                    "4096x4096, gate_up 4096x28672, down 14336x4096, lm_head "
                                    "4096x128256; bits 4, block 128, fp16 scales, packed zp",
                        "mode": args.mode,
+                       "launch": ("op-by-op calls" if args.eager else
+                                  "CUDA graph of the timed steps, one replay"),
                        "parallelism": f"N-sharded x{world}" + (" + NCCL all-gather of Y"
                                                               if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 387 MB of weights per step)"},

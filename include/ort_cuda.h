@@ -214,8 +214,26 @@ ORT_CUDA_API int ort_cuda_matmul_batched(ort_cuda_session* s, const float* A, co
                                          int64_t batch, int64_t m, int64_t k, int64_t n,
                                          int64_t b_batch_stride, float* Y, int flags);
 
+/* CUDA graphs of a sequence of device-pointer calls (the decode step of a
+ * model, for instance).  No counterpart in the reference, whose executor
+ * interprets the graph op by op on the CPU (onnx_graph.dart:961); here the
+ * ops of one step are recorded once and replayed with a single launch, so
+ * the host's per-op cost leaves the step.  Between graph_begin and
+ * graph_end, matmul / gemm calls on device pointers are recorded, not run;
+ * run every recorded op once before capturing (a call that would grow a
+ * buffer, use ORT_CUDA_HOST_IO or synchronise is refused with
+ * ORT_CUDA_ERR_INVALID_ARG).  Replays read and write the same device
+ * buffers as the recorded calls.  The session stream must not be the
+ * legacy default stream.  N-sharded sessions replay correctly: the
+ * peer-exchange epoch lives on the device. */
+ORT_CUDA_API int ort_cuda_graph_begin(ort_cuda_session* s);
+ORT_CUDA_API int ort_cuda_graph_end(ort_cuda_session* s, int* graph_id);
+ORT_CUDA_API int ort_cuda_graph_launch(ort_cuda_session* s, int graph_id);
+ORT_CUDA_API int ort_cuda_graph_drop(ort_cuda_session* s, int graph_id);
+
 /* Kernel launches issued by this session since it was opened (all of
- * them this library's own kernels). */
+ * them this library's own kernels; a graph launch counts the kernels it
+ * holds). */
 ORT_CUDA_API int ort_cuda_launch_count(ort_cuda_session* s, int64_t* count);
 
 #ifdef __cplusplus

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
 #include <string>
 #include <unordered_map>
 #include <unordered_set>
@@ -112,13 +113,24 @@ struct ort_cuda_session {
   void* kscratch = nullptr;
   size_t kscratch_bytes = 0;
   // N-sharded sessions: peer-memory exchange of Y (csrc/p2p.cu).  xbuf holds
-  // 8 ready flags (one per peer, 256 bytes) then two halves of xcap floats;
-  // xpeer[r] is rank r's xbuf mapped into this process (xpeer[rank] = xbuf).
+  // a 256-byte flag area (8 peer flags, epoch counter, CTA counter) then two
+  // halves of xcap floats; xpeer[r] is rank r's xbuf mapped into this
+  // process (xpeer[rank] = xbuf).
   void* xbuf = nullptr;
   void* xpeer[8] = {};
   size_t xcap = 0;
-  uint64_t xepoch = 0;
   bool p2p_ok = false;
+  bool xsel_offer = false;  // run_op offers the exchange half to the producer
+  bool xsel_taken = false;  // the producer wrote its slice there
+  // CUDA graphs captured from the session stream (ort_cuda_graph_*)
+  struct Graph {
+    cudaGraphExec_t exec;
+    int64_t launches;  // this library's kernels in the graph
+  };
+  std::map<int, Graph> graphs;
+  int next_graph = 1;
+  bool capturing = false;
+  int64_t capture_launch0 = 0;
   // host-mapped error word kernels write when a bounded wait gives up
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -130,6 +142,20 @@ namespace ortc {
 // Scratch helpers (session-owned, stream-ordered reuse).
 int ensure_ws(ort_cuda_session* s, size_t bytes);
 int ensure_pinned(ort_cuda_session* s, size_t bytes);
+// Output redirected to the half of a peer-exchange buffer that a device
+// resident epoch counter selects (half (ctr + 1) & 1, N-sharded sessions);
+// inactive when ctr is null.
+struct YSel {
+  float* half0 = nullptr;
+  int64_t cap = 0;
+  const unsigned long long* ctr = nullptr;
+};
+__device__ __forceinline__ float* ysel_base(float* Y, const YSel& s) {
+  if (!s.ctr) return Y;
+  const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(s.ctr) + 1;
+  return s.half0 + (int64_t)(e & 1) * s.cap;
+}
+
 int ensure_kscratch(ort_cuda_session* s, size_t bytes);
 // Reads and clears the kernels' error word (session.cu).
 int check_kernel_error(ort_cuda_session* s);
@@ -139,8 +165,11 @@ int bounded_sync(ort_cuda_session* s);
 // Peer-memory all-gather of Y for N-sharded sessions (p2p.cu).
 int p2p_setup(ort_cuda_session* s);
 void p2p_teardown(ort_cuda_session* s);
-float* p2p_next_slot(ort_cuda_session* s, int64_t floats);
-int p2p_gather(ort_cuda_session* s, int64_t M, int64_t Ns, int64_t N, float* Y);
+bool p2p_fits(ort_cuda_session* s, int64_t floats);
+YSel p2p_ysel(ort_cuda_session* s);
+// `local` null: the producer already wrote the slice with p2p_ysel().
+int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, int64_t N,
+               float* Y);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point: a 2-D
 // row-major tensor [d1][d0] with row pitch stride1 bytes, box b0 x b1.
@@ -158,7 +187,8 @@ int prepare_nbits_tc(Weight& w);
 bool tc_gemv_ok(const Weight& w, int64_t M);
 size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count);
 int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
-                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches);
+                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
+                   const YSel* ysel = nullptr);
 // General CUDA-core tiled GEMM over an nbits or dense weight (any M).
 // strict=true reproduces the reference's rounding bit for bit.
 int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,

@@ -356,6 +356,9 @@ int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
   const bool bf16 = mode == ORT_CUDA_MODE_MMA_BF16;
   const int64_t K = w.K, nl = w.nl;
   if (w.W16 == nullptr || w.w16_mode != mode) {
+    ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+               "the weight's first tensor-core call prepares it; run it once before "
+               "capturing a CUDA graph");
     // Prepack once per session (and per MMA mode): 16-bit [nl][K] + column exponents.
     if (w.W16) cudaFree(w.W16);
     if (w.col_exp) cudaFree(w.col_exp);
@@ -398,6 +401,9 @@ int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
     // zero-point / scale table and the column exponents are made once per
     // session and kept with the weight.
     if (w.sz16 == nullptr) {
+      ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+                 "the weight's first tensor-core call prepares it; run it once before "
+                 "capturing a CUDA graph");
       if (w.col_exp == nullptr) ORTC_CUDA(cudaMalloc(&w.col_exp, (size_t)nl * 4));
       ORTC_CUDA(cudaMalloc(&w.sz16, (size_t)w.nb * w.s_pitch * 4));
       nbits_col_exp_kernel<<<(unsigned)((nl + 255) / 256), 256, 0, st>>>(w.scales, w.s_pitch, w.nb,

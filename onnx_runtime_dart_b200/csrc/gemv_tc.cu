@@ -97,6 +97,7 @@ struct TcParams {
   const float* A;
   float* Y;
   float* part;   // split-K mode: [nch][M][tiles*128] chunk partials
+  YSel ysel;     // tile-major output redirected to a peer-exchange half
   int* err;
   int64_t ldy;
   int N, K, bs, nch, tiles;
@@ -185,7 +186,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // reading item j - nd).  One barrier, so the issuer waits once per item.
   uint64_t* ready = bempty + kMaxBStages;
   uint64_t* aempty = ready + kAItems;      // [2] an item's A consumed (MMA commit)
-  uint64_t* dfull = aempty + kAItems;      // [2] an item's D complete (MMA commit)
+  // dfull[g]: the D of epilogue group g's next item is complete (MMA
+  // commit).  One barrier per group, each waited by one group in item order,
+  // so a wait never meets a phase two steps away (which a parity wait would
+  // take for complete) even when both groups share one D buffer.
+  uint64_t* dfull = aempty + kAItems;
   uint64_t* xfull = dfull + 2;    // [2] X buffer written (8 dequantiser warps)
   uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 4 epilogue warps)
   uint64_t* fin = xempty + 2;
@@ -261,7 +266,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_i8(128, NM);
       int j = 0, cur = -1, nbuild = 0;
-      for_each_item(p, [&](int, int chunk, int) {
+      for_each_item(p, [&](int, int chunk, int tig) {
         if (chunk != cur) {
           if (cur >= 0) mma_commit(&xempty[(nbuild - 1) & 1]);  // X free once its MMAs end
           if (!mbar_wait(&xfull[nbuild & 1], (nbuild >> 1) & 1)) {
@@ -291,7 +296,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           mma_i8_ts(dbase + p.op_d[st], abase + st * 8, xd0 + xoff, idesc, (p.acc_mask >> st) & 1u);
         }
         mma_commit(&aempty[h]);
-        mma_commit(&dfull[d]);
+        mma_commit(&dfull[(p.tile_major ? tig : j) & 1]);
         j++;
         return true;
       });
@@ -476,7 +481,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     griddep_wait();  // outputs and split-K scratch may still be in use upstream
     bool ok = true;
     int S_m[M];
-    int j = 0, cur = -1, nbuild = 0;
+    int j = 0, cur = -1, nbuild = 0, mine = 0;
     for_each_item(p, [&](int tile, int chunk, int tig) {
       if (!ok) return false;
       if (chunk != cur) {
@@ -499,10 +504,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         return true;
       }
       const int bst = j % p.nbst, d = j % p.nd;
-      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) || !mbar_wait(&dfull[d], (j / p.nd) & 1)) {
+      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) || !mbar_wait(&dfull[egrp], mine & 1)) {
         record_error(p.err, KERR_WAIT_MMA);
         return ok = false;
       }
+      mine++;
       tc_fence_after();
       float y[M];
 #pragma unroll
@@ -566,7 +572,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int m = 0; m < M; m++) {
           const float acc = chunk == 0 ? 0.0f + part[m] : ya[m * kTile + nl] + part[m];
           ya[m * kTile + nl] = acc;
-          if (chunk == p.nch - 1 && n < p.N) p.Y[m * p.ldy + n] = acc;
+          if (chunk == p.nch - 1 && n < p.N) ysel_base(p.Y, p.ysel)[m * p.ldy + n] = acc;
         }
       } else {
         const int64_t npad = (int64_t)p.tiles * kTile;
@@ -589,10 +595,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 // programmatic dependent of the GEMV: its small CTAs become resident beside
 // the GEMV's and wait in griddepcontrol.wait, so no launch gap follows.
 __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __restrict__ part,
-                                                           float* __restrict__ Y, int64_t ldy,
-                                                           int M, int N, int nch, int64_t npad) {
+                                                           float* Y, int64_t ldy, int M, int N,
+                                                           int nch, int64_t npad, YSel ysel) {
   griddep_launch_dependents();
   griddep_wait();
+  Y = ysel_base(Y, ysel);
   const int64_t total = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -747,7 +754,8 @@ size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count) {
 }
 
 int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
-                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches) {
+                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
+                   const YSel* ysel) {
   if (w.nl == 0) return ORT_CUDA_OK;
   const Plan pl = make_plan(w.K, w.nl, M, sm_count);
   TcParams p;
@@ -765,6 +773,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   p.tg = pl.tg;
   p.cpc = pl.cpc;
   p.part = pl.tile_major ? nullptr : partials;
+  p.ysel = ysel ? *ysel : YSel();
   p.a_vec = ((reinterpret_cast<uintptr_t>(A) & 15) == 0 && w.K % 4 == 0) ? 1 : 0;
   p.bpi = kChunkK / w.bs;
   p.has_zp = w.has_zp ? 1 : 0;
@@ -801,7 +810,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_reduce_kernel, (const float*)partials, Y, ldy,
-                                 (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile));
+                                 (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile, p.ysel));
     (*launches)++;
   }
   return ORT_CUDA_OK;

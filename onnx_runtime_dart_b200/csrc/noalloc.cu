@@ -83,7 +83,7 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
   int rc = slot_for(s->device, &sl);
   if (rc == ORT_CUDA_OK)
     rc = launch_tc_gemv(w, A, M, Y, w.nl, sl->partials, s->err_dev, s->sm_count, s->stream,
-                        &s->launches);
+                        &s->launches, nullptr);
   if (prev >= 0 && prev != s->device) cudaSetDevice(prev);
   return rc;
 }

@@ -3,17 +3,22 @@
 // The reference's GemmPool writes every worker's output columns straight
 // into the shared result (parallel_pool.dart:121-205); across GPUs the
 // equivalent is each rank reading the other ranks' column slices over
-// NVLink.  Every rank owns an exchange buffer (ready flags + two halves);
-// at session start the buffers are exported with CUDA IPC and the handles
-// swapped once through NCCL.  Per operation the compute kernel writes the
-// rank's [M, Ns] slice into half (epoch & 1) of its own buffer; then
-// p2p_gather_kernel posts the epoch into every peer's flag slot for this
-// rank, waits (bounded) until every peer has posted the same epoch here, and
-// reads all slices with plain peer loads into Y [M, N].  A rank's next write
-// into a half that a peer may still be reading is two epochs later, after
-// that peer has posted the intervening epoch, which it does only after its
-// own read finished: two halves are enough.  No NCCL and no multicast is on
-// the per-operation path.
+// NVLink.  Every rank owns an exchange buffer (ready flags, an epoch
+// counter, two halves); at session start the buffers are exported with CUDA
+// IPC and the handles swapped once through NCCL.  Per operation, with
+// e = counter + 1 read on the device:
+//   p2p_stage_kernel    copies the rank's [M, Ns] slice into half (e & 1)
+//                       (skipped when the producing kernel wrote it there,
+//                       see YSel)
+//   p2p_gather_kernel   posts e into every peer's flag slot for this rank,
+//                       waits (bounded) until every peer has posted e here,
+//                       reads all slices with plain peer loads into Y [M, N],
+//                       and its last CTA stores counter = e.
+// A rank's next write into a half that a peer may still be reading is two
+// epochs later, after that peer has posted the intervening epoch, which it
+// does only after its own read finished: two halves are enough.  The epoch
+// lives on the device, so the sequence replays unchanged from a CUDA graph.
+// No NCCL and no multicast is on the per-operation path.
 #include <cstring>
 #include <vector>
 
@@ -25,28 +30,53 @@ namespace ortc {
 namespace {
 
 constexpr size_t kFlagBytes = 256;
+constexpr int kCtrSlot = 8, kDoneSlot = 9;  // 64-bit words in the flag area
 constexpr size_t kDefaultCapFloats = size_t(4) << 20;  // 16 MB per half
 
 struct P2PArgs {
-  const float* src[8];            // rank r's half for this epoch
+  const float* src[8];            // rank r's half 0 (half 1 follows at + cap)
   unsigned long long* flag[8];    // rank r's flag slot for this rank
-  const unsigned long long* mine; // this rank's flags, slot r written by rank r
+  unsigned long long* mine;       // this rank's flag area (slot r written by rank r)
+  int64_t cap;
   float* Y;
   int64_t ldy;
   int M, Ns, N, rank, world;
-  unsigned long long epoch;
   int* err;
 };
 
+__device__ __forceinline__ unsigned long long next_epoch(const unsigned long long* mine) {
+  return *reinterpret_cast<const volatile unsigned long long*>(mine + kCtrSlot) + 1;
+}
+
+__global__ void __launch_bounds__(256) p2p_stage_kernel(const float* __restrict__ local,
+                                                        float* xhalf0, int64_t cap,
+                                                        const unsigned long long* mine,
+                                                        int64_t n) {
+  float* dst = xhalf0 + (next_epoch(mine) & 1) * cap;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = local[i];
+}
+
 __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
   __shared__ int ok;
+  __shared__ unsigned long long epoch;
+  // launched as a programmatic dependent: the slice is complete, and the
+  // epoch counter final, only after the producing grid has finished
+  griddep_launch_dependents();
+  griddep_wait();
   if (threadIdx.x == 0) {
     ok = 1;
+    epoch = next_epoch(a.mine);
+  }
+  __syncthreads();
+  const unsigned long long e = epoch;
+  if (threadIdx.x == 0) {
     // this rank's slice (written by an earlier kernel) before the flag
     __threadfence_system();
     for (int r = 0; r < a.world; r++)
       if (r != a.rank)
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(a.epoch)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(e)
                      : "memory");
     const uint64_t t0 = globaltimer();
     for (int r = 0; r < a.world && ok; r++) {
@@ -54,7 +84,7 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
       for (;;) {
         unsigned long long v;
         asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.mine + r) : "memory");
-        if (v >= a.epoch) break;
+        if (v >= e) break;
         if (globaltimer() - t0 > kWaitLimitNs) {
           record_error(a.err, KERR_WAIT_PEER);
           ok = 0;
@@ -65,13 +95,25 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
     }
   }
   __syncthreads();
-  if (!ok) return;
-  const int64_t total = (int64_t)a.M * a.N;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / a.N), n = (int)(i % a.N);
-    const int r = n / a.Ns, j = n - r * a.Ns;
-    a.Y[m * a.ldy + n] = __ldcv(a.src[r] + (int64_t)m * a.Ns + j);
+  if (ok) {
+    const int64_t half = (int64_t)(e & 1) * a.cap;
+    const int64_t total = (int64_t)a.M * a.N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int m = (int)(i / a.N), n = (int)(i % a.N);
+      const int r = n / a.Ns, j = n - r * a.Ns;
+      a.Y[m * a.ldy + n] = __ldcv(a.src[r] + half + (int64_t)m * a.Ns + j);
+    }
+  }
+  // the last CTA to finish advances the epoch counter (every CTA has read it)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.mine + kDoneSlot, 1ull) == gridDim.x - 1) {
+      a.mine[kDoneSlot] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(a.mine + kCtrSlot) = e;
+    }
   }
 }
 
@@ -161,24 +203,42 @@ void p2p_teardown(ort_cuda_session* s) {
   s->p2p_ok = false;
 }
 
-float* p2p_next_slot(ort_cuda_session* s, int64_t floats) {
-  if (!s->p2p_ok || (size_t)floats > s->xcap) return nullptr;
-  const uint64_t e = s->xepoch + 1;
-  return (float*)((char*)s->xbuf + kFlagBytes) + (e & 1) * s->xcap;
+bool p2p_fits(ort_cuda_session* s, int64_t floats) {
+  return s->p2p_ok && (size_t)floats <= s->xcap;
 }
 
-int p2p_gather(ort_cuda_session* s, int64_t M, int64_t Ns, int64_t N, float* Y) {
-  const uint64_t e = ++s->xepoch;
+YSel p2p_ysel(ort_cuda_session* s) {
+  YSel y;
+  y.half0 = (float*)((char*)s->xbuf + kFlagBytes);
+  y.cap = (int64_t)s->xcap;
+  y.ctr = (const unsigned long long*)s->xbuf + kCtrSlot;
+  return y;
+}
+
+int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, int64_t N,
+               float* Y) {
+  unsigned long long* mine = (unsigned long long*)s->xbuf;
+  float* half0 = (float*)((char*)s->xbuf + kFlagBytes);
+  const int64_t n_local = M * Ns;
+  if (local) {
+    const unsigned sblocks =
+        (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_local + 1023) / 1024, s->sm_count));
+    p2p_stage_kernel<<<sblocks, 256, 0, s->stream>>>(local, half0, (int64_t)s->xcap, mine,
+                                                     n_local);
+    ORTC_CUDA(cudaGetLastError());
+    s->launches++;
+  }
   P2PArgs a;
   for (int r = 0; r < 8; r++) {
     a.src[r] = nullptr;
     a.flag[r] = nullptr;
   }
   for (int r = 0; r < s->world; r++) {
-    a.src[r] = (const float*)((char*)s->xpeer[r] + kFlagBytes) + (e & 1) * s->xcap;
+    a.src[r] = (const float*)((char*)s->xpeer[r] + kFlagBytes);
     a.flag[r] = (unsigned long long*)s->xpeer[r] + s->rank;
   }
-  a.mine = (const unsigned long long*)s->xbuf;
+  a.mine = mine;
+  a.cap = (int64_t)s->xcap;
   a.Y = Y;
   a.ldy = N;
   a.M = (int)M;
@@ -186,13 +246,20 @@ int p2p_gather(ort_cuda_session* s, int64_t M, int64_t Ns, int64_t N, float* Y) 
   a.N = (int)N;
   a.rank = s->rank;
   a.world = s->world;
-  a.epoch = e;
   a.err = s->err_dev;
   const int64_t total = M * N;
   const unsigned blocks =
       (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, s->sm_count * 2));
-  p2p_gather_kernel<<<blocks, 256, 0, s->stream>>>(a);
-  ORTC_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ORTC_CUDA(cudaLaunchKernelEx(&cfg, p2p_gather_kernel, a));
   s->launches++;
   return ORT_CUDA_OK;
 }

@@ -33,6 +33,9 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 int ensure_ws(ort_cuda_session* s, size_t bytes) {
   if (bytes <= s->ws_bytes) return ORT_CUDA_OK;
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+             "a buffer would grow while a CUDA graph is being captured; run every "
+             "operation of the graph once before capturing it");
   size_t want = bytes + bytes / 4 + (1 << 20);
   if (s->ws) {
     ORTC_CUDA(cudaStreamSynchronize(s->stream));
@@ -47,6 +50,9 @@ int ensure_ws(ort_cuda_session* s, size_t bytes) {
 
 int ensure_pinned(ort_cuda_session* s, size_t bytes) {
   if (bytes <= s->pinned_bytes) return ORT_CUDA_OK;
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+             "a buffer would grow while a CUDA graph is being captured; run every "
+             "operation of the graph once before capturing it");
   size_t want = bytes + bytes / 4 + (1 << 20);
   if (s->pinned) {
     ORTC_CUDA(cudaStreamSynchronize(s->stream));
@@ -61,6 +67,9 @@ int ensure_pinned(ort_cuda_session* s, size_t bytes) {
 
 int ensure_kscratch(ort_cuda_session* s, size_t bytes) {
   if (bytes <= s->kscratch_bytes) return ORT_CUDA_OK;
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+             "a buffer would grow while a CUDA graph is being captured; run every "
+             "operation of the graph once before capturing it");
   size_t want = bytes + bytes / 4 + (1 << 20);
   if (s->kscratch) {
     ORTC_CUDA(cudaStreamSynchronize(s->stream));
@@ -398,6 +407,8 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->kscratch) cudaFree(s->kscratch);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
+  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second.exec);
+  s->graphs.clear();
   p2p_teardown(s);
   if (s->nccl) {
     nccl()->CommFinalize((ncclComm_t)s->nccl);
@@ -424,6 +435,7 @@ ORT_CUDA_API int ort_cuda_set_stream(ort_cuda_session* s, void* stream) {
 
 ORT_CUDA_API int ort_cuda_sync(ort_cuda_session* s) {
   ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG, "cannot synchronise during a capture");
   DeviceGuard g(s->device);
   return bounded_sync(s);
 }
@@ -432,6 +444,59 @@ ORT_CUDA_API int ort_cuda_rank_info(ort_cuda_session* s, int* rank, int* world) 
   ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
   if (rank) *rank = s->rank;
   if (world) *world = s->world;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_graph_begin(ort_cuda_session* s) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "NULL session");
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG, "a capture is already in progress");
+  ORTC_CHECK(s->stream != nullptr && s->stream != cudaStreamLegacy &&
+                 s->stream != cudaStreamPerThread,
+             ORT_CUDA_ERR_INVALID_ARG, "the legacy default stream cannot be captured");
+  DeviceGuard g(s->device);
+  ORTC_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeRelaxed));
+  s->capturing = true;
+  s->capture_launch0 = s->launches;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_graph_end(ort_cuda_session* s, int* graph_id) {
+  ORTC_CHECK(s && graph_id, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(s->capturing, ORT_CUDA_ERR_INVALID_ARG, "no capture in progress");
+  DeviceGuard g(s->device);
+  s->capturing = false;
+  cudaGraph_t graph = nullptr;
+  ORTC_CUDA(cudaStreamEndCapture(s->stream, &graph));
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+  const int id = s->next_graph++;
+  s->graphs[id] = {exec, s->launches - s->capture_launch0};
+  s->launches = s->capture_launch0;  // captured launches run when the graph does
+  *graph_id = id;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_graph_launch(ort_cuda_session* s, int graph_id) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "NULL session");
+  auto it = s->graphs.find(graph_id);
+  ORTC_CHECK(it != s->graphs.end(), ORT_CUDA_ERR_NOT_FOUND,
+             "no graph with id " + std::to_string(graph_id));
+  DeviceGuard g(s->device);
+  ORTC_CUDA(cudaGraphLaunch(it->second.exec, s->stream));
+  s->launches += it->second.launches;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_graph_drop(ort_cuda_session* s, int graph_id) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "NULL session");
+  auto it = s->graphs.find(graph_id);
+  ORTC_CHECK(it != s->graphs.end(), ORT_CUDA_ERR_NOT_FOUND,
+             "no graph with id " + std::to_string(graph_id));
+  DeviceGuard g(s->device);
+  cudaGraphExecDestroy(it->second.exec);
+  s->graphs.erase(it);
   return ORT_CUDA_OK;
 }
 
@@ -708,6 +773,8 @@ template <typename F>
 int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems, const float* C,
            int64_t c_elems, float* Y, int64_t M, int flags, F&& compute) {
   const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
   const int64_t N = w.N;
   const bool sharded = s->world > 1;
   WsLayout L;
@@ -749,16 +816,19 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
     dY = (float*)(ws + L.y);
     y_pinned = is_pinned_host(Y);
   }
-  // sharded: the rank's slice goes to its peer-visible exchange half when
-  // that fits (gathered by peer loads), else to the workspace (NCCL)
-  float* xslot = sharded ? p2p_next_slot(s, M * w.ns) : nullptr;
-  float* yloc = sharded ? (xslot ? xslot : (float*)(ws + L.yloc)) : dY;
+  float* yloc = sharded ? (float*)(ws + L.yloc) : dY;
   const int64_t ldy = sharded ? w.ns : N;
+  // peer loads when the slices fit the exchange buffers (a producer that can
+  // writes its slice there itself), else NCCL
+  const bool p2p = sharded && p2p_fits(s, M * w.ns);
+  s->xsel_offer = p2p;
+  s->xsel_taken = false;
   rc = compute(dA, dC, yloc, ldy);
+  s->xsel_offer = false;
   if (rc) return rc;
   if (sharded) {
-    rc = xslot ? p2p_gather(s, M, w.ns, N, dY)
-               : gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
+    rc = p2p ? p2p_gather(s, s->xsel_taken ? nullptr : yloc, M, w.ns, N, dY)
+             : gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
     if (rc) return rc;
   }
   if (host) {
@@ -804,8 +874,14 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if (tc_gemv_ok(w, M)) {
                     int rc = ensure_kscratch(s, tc_gemv_partial_floats(w.K, w.nl, M, s->sm_count) * 4);
                     if (rc) return rc;
+                    YSel ys;
+                    if (s->xsel_offer) {
+                      ys = p2p_ysel(s);
+                      s->xsel_taken = true;
+                    }
                     return launch_tc_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
-                                          s->sm_count, s->stream, &s->launches);
+                                          s->sm_count, s->stream, &s->launches,
+                                          s->xsel_offer ? &ys : nullptr);
                   }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K))

@@ -148,6 +148,23 @@ class CudaSession:
         check(_lib.load().ort_cuda_launch_count(self.handle, ctypes.byref(c)))
         return c.value
 
+    # -- CUDA graphs of device-pointer call sequences -----------------------
+    def graph_begin(self) -> None:
+        """Records the following device-pointer calls instead of running
+        them (run each once before, so no buffer grows during capture)."""
+        check(_lib.load().ort_cuda_graph_begin(self.handle), "ort_cuda_graph_begin")
+
+    def graph_end(self) -> int:
+        gid = ctypes.c_int()
+        check(_lib.load().ort_cuda_graph_end(self.handle, ctypes.byref(gid)), "ort_cuda_graph_end")
+        return gid.value
+
+    def graph_launch(self, graph_id: int) -> None:
+        check(_lib.load().ort_cuda_graph_launch(self.handle, graph_id), "ort_cuda_graph_launch")
+
+    def graph_drop(self, graph_id: int) -> None:
+        check(_lib.load().ort_cuda_graph_drop(self.handle, graph_id), "ort_cuda_graph_drop")
+
     # -- weight residency (uploaded once per session) ----------------------
     def upload_nbits(self, name: str, b_q: np.ndarray, scales: np.ndarray,
                      zero_points: Optional[np.ndarray], *, k: int, n: int, bits: int = 4,

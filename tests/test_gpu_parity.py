@@ -189,6 +189,17 @@ def test_zero_point_per_column_odd_nb(sess):
     assert max_rel(ref, sess.matmul_nbits("pc", A)) <= EXACT_TOL
 
 
+@pytest.mark.parametrize("M", [3, 4, 5])
+@pytest.mark.parametrize("N", [25000, 40000])
+def test_single_d_buffer_many_items(sess, M, N):
+    """Block size 32 at M = 3..5 needs all of the D columns for one item (a
+    single accumulator buffer) and, at these N, each CTA handles several
+    items: the two epilogue groups then share that buffer."""
+    rng = np.random.default_rng(M * 7 + N)
+    ref, y = _nbits_case(sess, rng, M, 1024, N, 32, True)
+    assert max_rel(ref, y) <= EXACT_TOL
+
+
 def test_split_k_repeat_bitwise(sess):
     """Split-K decode GEMVs write chunk partials that a dependent kernel,
     launched to overlap the GEMV's tail, adds in chunk order.  Repeated and
