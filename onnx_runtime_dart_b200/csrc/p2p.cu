@@ -31,6 +31,7 @@ namespace {
 
 constexpr size_t kFlagBytes = 256;
 constexpr int kCtrSlot = 8, kDoneSlot = 9;  // 64-bit words in the flag area
+constexpr int kPull = 4;                    // elements per thread and round
 constexpr size_t kDefaultCapFloats = size_t(4) << 20;  // 16 MB per half
 
 struct P2PArgs {
@@ -72,11 +73,13 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
   __syncthreads();
   const unsigned long long e = epoch;
   if (threadIdx.x == 0) {
-    // this rank's slice (written by an earlier kernel) before the flag
-    __threadfence_system();
+    // The slice lives in this GPU's memory and peers read it through this
+    // GPU's L2; griddepcontrol.wait has made the producing grid's writes
+    // complete and visible, so the flag needs no further fence (a
+    // system-scope fence here cost 4-12 us per operation).
     for (int r = 0; r < a.world; r++)
       if (r != a.rank)
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(e)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(e)
                      : "memory");
     const uint64_t t0 = globaltimer();
     for (int r = 0; r < a.world && ok; r++) {
@@ -96,13 +99,28 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
   }
   __syncthreads();
   if (ok) {
+    // up to kPull elements per thread and round, all loads in flight before
+    // any store (peer loads take microseconds)
     const int64_t half = (int64_t)(e & 1) * a.cap;
     const int64_t total = (int64_t)a.M * a.N;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const int m = (int)(i / a.N), n = (int)(i % a.N);
-      const int r = n / a.Ns, j = n - r * a.Ns;
-      a.Y[m * a.ldy + n] = __ldcv(a.src[r] + half + (int64_t)m * a.Ns + j);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total;
+         i0 += stride * kPull) {
+      float v[kPull];
+#pragma unroll
+      for (int u = 0; u < kPull; u++) {
+        const int64_t i = i0 + u * stride;
+        if (i < total) {
+          const int m = (int)(i / a.N), n = (int)(i % a.N);
+          const int r = n / a.Ns, j = n - r * a.Ns;
+          v[u] = __ldcv(a.src[r] + half + (int64_t)m * a.Ns + j);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPull; u++) {
+        const int64_t i = i0 + u * stride;
+        if (i < total) a.Y[(i / a.N) * a.ldy + i % a.N] = v[u];
+      }
     }
   }
   // the last CTA to finish advances the epoch counter (every CTA has read it)
@@ -248,8 +266,8 @@ int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, i
   a.world = s->world;
   a.err = s->err_dev;
   const int64_t total = M * N;
-  const unsigned blocks =
-      (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, s->sm_count * 2));
+  const unsigned blocks = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>((total + 256 * kPull - 1) / (256 * kPull), s->sm_count * 4));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);
   cfg.blockDim = dim3(256);
