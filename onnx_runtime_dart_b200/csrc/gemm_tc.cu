@@ -223,6 +223,37 @@ __global__ void a16_kernel(const float* __restrict__ A, int M, int K, bool trans
   for (int k = lane; k < K; k += 32) o[k] = to16<BF16>(BF16 ? at(k) : scale_pow2(at(k), -e));
 }
 
+// The same conversion for row-major A with K % 4 == 0 and a 16-byte
+// aligned base: 16-byte loads in both passes, 8-byte stores (same bits).
+template <bool BF16>
+__global__ void a16_vec_kernel(const float* __restrict__ A, int M, int K,
+                               uint16_t* __restrict__ out, int* __restrict__ row_exp) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const float4* row = reinterpret_cast<const float4*>(A + (int64_t)warp * K);
+  const int k4 = K / 4;
+  int e = 0;
+  if (!BF16) {
+    float mx = 0.0f;
+    for (int i = lane; i < k4; i += 32) {
+      const float4 v = __ldg(row + i);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    e = norm_exp(mx);
+    if (lane == 0) row_exp[warp] = e;
+  }
+  uint2* o = reinterpret_cast<uint2*>(out + (int64_t)warp * K);
+  for (int i = lane; i < k4; i += 32) {
+    const float4 v = __ldg(row + i);
+    const uint32_t a = to16<BF16>(BF16 ? v.x : scale_pow2(v.x, -e));
+    const uint32_t b = to16<BF16>(BF16 ? v.y : scale_pow2(v.y, -e));
+    const uint32_t c = to16<BF16>(BF16 ? v.z : scale_pow2(v.z, -e));
+    const uint32_t d = to16<BF16>(BF16 ? v.w : scale_pow2(v.w, -e));
+    o[i] = make_uint2(a | (b << 16), c | (d << 16));
+  }
+}
+
 // Dense weight [K][nl] fp32 -> 16-bit [nl][K] with per-column exponent.
 __global__ void wcol_exp_kernel(const float* __restrict__ W, int K, int nl, int* __restrict__ col_exp) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
@@ -330,7 +361,12 @@ int convert_a(ort_cuda_session* s, const float* A, int64_t M, int64_t K, bool tr
   *row_exp = (int*)(base + al256((size_t)(M * K) * 2));
   const int64_t threads = M * 32;
   const unsigned blocks = (unsigned)((threads + 255) / 256);
-  if (bf16)
+  const bool vec = !transA && K % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+  if (vec && bf16)
+    a16_vec_kernel<true><<<blocks, 256, 0, st>>>(A, (int)M, (int)K, *A16, *row_exp);
+  else if (vec)
+    a16_vec_kernel<false><<<blocks, 256, 0, st>>>(A, (int)M, (int)K, *A16, *row_exp);
+  else if (bf16)
     a16_kernel<true><<<blocks, 256, 0, st>>>(A, (int)M, (int)K, transA, *A16, *row_exp);
   else
     a16_kernel<false><<<blocks, 256, 0, st>>>(A, (int)M, (int)K, transA, *A16, *row_exp);

@@ -103,6 +103,9 @@ struct TcParams {
   int N, K, bs, nch, tiles;
   int tile_major;  // 1: a CTA loops over all chunks of its tiles
   int grid_tiles;  // tile-major: tiles t = blockIdx.x + i*grid_tiles
+  int cluster;     // split-K: the nch CTAs of a tile set form a cluster and
+                   // sum their partials through distributed shared memory
+  uint32_t yacc_bytes;  // tile-major accumulators or cluster partials
   int tg;          // tile-major: tiles per group (y accumulators in smem)
   int cpc;         // split-K: CTAs per chunk
   int bpi, regions, has_zp, z_rows, nbst;
@@ -178,8 +181,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint8_t* Xs = smem;  // two buffers, each X then the digit sums
   uint8_t* Bs = smem + 2 * kXBufBytes;
   float* yacc = reinterpret_cast<float*>(smem + p.yacc_off);  // [tg][M][128]
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(
-      smem + p.yacc_off + (p.tile_major ? p.tg * M * kTile * 4 : 0));
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + p.yacc_off + p.yacc_bytes);
   uint64_t* bempty = bfull + kMaxBStages;
   // ready[h]: item j = 2p + h may be issued (phase p): its A is written (8
   // dequantiser warps) and its D buffer is free (4 epilogue warps, after
@@ -574,6 +576,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ya[m * kTile + nl] = acc;
           if (chunk == p.nch - 1 && n < p.N) ysel_base(p.Y, p.ysel)[m * p.ldy + n] = acc;
         }
+      } else if (p.cluster) {
+        // this chunk's partial of the CTA's ti-th tile, for the cluster sum
+        const int ti = (tile - (int)(blockIdx.x / p.nch)) / p.cpc;
+#pragma unroll
+        for (int m = 0; m < M; m++) yacc[(ti * M + m) * kTile + nl] = part[m];
       } else {
         const int64_t npad = (int64_t)p.tiles * kTile;
 #pragma unroll
@@ -584,6 +591,37 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (p.cluster) {
+    // Split-K across the cluster: CTA rank c sums tiles ti = c, c + nch, ...
+    // of the set over the nch CTAs' partials in chunk order,
+    // ((0 + p_0) + p_1) + ..., as the other paths do.  Only the epilogue
+    // threads (which passed griddepcontrol.wait) write outputs; the second
+    // barrier keeps every CTA's partials alive until all reads are done.
+    cluster_sync_all();
+    if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
+      const int r = (int)(blockIdx.x / p.nch), c = (int)cluster_ctarank();
+      const int ntile = (p.tiles - 1 - r) / p.cpc + 1;
+      const int et = threadIdx.x - kEpiWarp0 * 32;
+      float* Yb = ysel_base(p.Y, p.ysel);
+      const uint32_t base = smem_u32(yacc);
+      for (int ti = c; ti < ntile; ti += p.nch)
+        for (int i = et; i < M * kTile; i += kEpiWarps * 32) {
+          const int m = i / kTile, col = i % kTile;
+          const int n = (r + ti * p.cpc) * kTile + col;
+          const uint32_t off = (uint32_t)(((ti * M + m) * kTile + col) * 4);
+          float v[8];
+#pragma unroll
+          for (int cc = 0; cc < 8; cc++)
+            v[cc] = cc < p.nch ? ld_dsmem_f32(dsmem_addr(base + off, (uint32_t)cc)) : 0.0f;
+          float acc = 0.0f;
+#pragma unroll
+          for (int cc = 0; cc < 8; cc++)
+            if (cc < p.nch) acc = acc + v[cc];
+          if (n < p.N) Yb[m * p.ldy + n] = acc;
+        }
+    }
+    cluster_sync_all();
+  }
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -683,7 +721,58 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
     p.op_d[st] = (uint32_t)(rg * dp.nm);
     if ((st * 32) % (G * w.bs) != 0) p.acc_mask |= 1u << st;
   }
-  const uint32_t yacc_bytes = pl.tile_major ? (uint32_t)(p.tg * M * kTile * 4) : 0;
+  uint32_t yacc_bytes = pl.tile_major ? (uint32_t)(p.tg * M * kTile * 4) : 0;
+  int grid = pl.grid;
+  p.cluster = 0;
+  static int max_clusters[64][9];  // per device and cluster size, 0 = not yet queried
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static unsigned long long configured = 0;
+  if (!(configured & (1ull << (dev & 63)))) {
+    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemLimit));
+    configured |= 1ull << (dev & 63);
+  }
+  if (!pl.tile_major && pl.nch >= 2 && pl.nch <= 8) {
+    // A cluster per tile set, as many as fit at once (a cluster waiting for
+    // a second wave would cost more than the separate reduction it saves;
+    // at one CTA per SM, 15 clusters of 8 fit on 148 SMs).
+    int& mc = max_clusters[dev & 63][pl.nch];
+    if (mc == 0) {
+      cudaLaunchConfig_t qc = {};
+      qc.gridDim = dim3((unsigned)pl.grid);
+      qc.blockDim = dim3(kThreadsTC);
+      qc.dynamicSmemBytes = kSmemLimit;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = (unsigned)pl.nch;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      qc.attrs = qa;
+      qc.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<M>, &qc) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      mc = n > 0 ? n : -1;
+    }
+    const int cpc = std::min(pl.tiles, mc);
+    const int ntile_max = mc > 0 ? (pl.tiles + cpc - 1) / cpc : 0;
+    const uint32_t cbytes = (uint32_t)(ntile_max * M * kTile * 4);
+    const size_t cfixed = 1024 + 2 * kXBufBytes + cbytes + 1024;
+    // worth it while its busiest CTA takes at most one more item than with
+    // the separate reduction (whose kernel boundary costs about three)
+    const int items_c = ntile_max, items_s = (pl.tiles + pl.cpc - 1) / pl.cpc;
+    if (mc > 0 && items_c <= items_s + 1 &&
+        (kSmemLimit - std::min(kSmemLimit, cfixed)) / p.stage_bytes >= 2) {
+      p.cluster = 1;
+      p.cpc = cpc;
+      grid = cpc * pl.nch;
+      yacc_bytes = cbytes;
+    }
+  }
+  p.yacc_bytes = yacc_bytes;
   const size_t fixed = 1024 + 2 * kXBufBytes + yacc_bytes + 1024;
   int nbst = (int)((kSmemLimit - fixed) / p.stage_bytes);
   if (nbst > kMaxBStages) nbst = kMaxBStages;
@@ -691,27 +780,23 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
   p.nbst = nbst;
   p.yacc_off = 2 * kXBufBytes + nbst * p.stage_bytes;
   const size_t smem = fixed + (size_t)nbst * p.stage_bytes;
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kSmemLimit));
-    configured |= 1ull << (dev & 63);
-  }
   // Programmatic dependent launch: this kernel's prologue and weight stream
   // may overlap the previous kernel's tail; it reads activations and writes
   // outputs only after griddepcontrol.wait.
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)pl.grid);
+  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreadsTC);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.cluster ? (unsigned)pl.nch : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.cluster ? 2 : 1;
   ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p));
   return ORT_CUDA_OK;
 }
@@ -798,7 +883,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   }
   if (rc) return rc;
   (*launches)++;
-  if (!pl.tile_major) {
+  if (!pl.tile_major && !p.cluster) {
     const int64_t total = M * w.nl;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::min<int64_t>((total + 127) / 128, (int64_t)sm_count * 4));

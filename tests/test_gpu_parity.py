@@ -411,9 +411,10 @@ def test_launch_counter_counts_own_kernels(sess):
     before = sess.launch_count()
     sess.matmul_nbits("lc", rng.standard_normal((1, 512)).astype(np.float32))
     assert sess.launch_count() == before + 1
-    # two chunks over two column tiles: split-K GEMV plus the chunk-order reduction
+    # two chunks over two column tiles: split-K, summed either by a cluster
+    # of the two chunks' CTAs (one launch) or by a reduction kernel (two)
     B, s, z = O.make_nbits_weight(rng, 1024, 256, 32, zero_points=False)
     sess.upload_nbits("lc2", B, s, z, k=1024, n=256, block_size=32)
     before = sess.launch_count()
     sess.matmul_nbits("lc2", rng.standard_normal((1, 1024)).astype(np.float32))
-    assert sess.launch_count() == before + 2
+    assert sess.launch_count() in (before + 1, before + 2)
