@@ -68,8 +68,8 @@ constexpr int kMaxBStages = 6;      // shared-memory ring depth (runtime <= 6)
 constexpr int kDeWarps = 8;         // dequantisers: 2 groups x 4 lane quarters
 constexpr int kEpiWarp0 = 8;        // epilogue: 2 groups of 4 warps, 8..15
 constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp = 16, kMmaWarp = 17;
-constexpr int kThreadsTC = 18 * 32;
+constexpr int kProducerWarp = 16, kMmaWarp = 17, kXWarp = 18;
+constexpr int kThreadsTC = 19 * 32;
 constexpr int kMinBs = 32;          // one MMA never spans two blocks
 constexpr uint32_t kPackedBytes = kTile * kChunkK / 2;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
@@ -188,15 +188,18 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // reading item j - nd).  One barrier, so the issuer waits once per item.
   uint64_t* ready = bempty + kMaxBStages;
   uint64_t* aempty = ready + kAItems;      // [2] an item's A consumed (MMA commit)
-  // dfull[g]: the D of epilogue group g's next item is complete (MMA
-  // commit).  One barrier per group, each waited by one group in item order,
-  // so a wait never meets a phase two steps away (which a parity wait would
-  // take for complete) even when both groups share one D buffer.
+  // dfull[2 g + d]: the D of epilogue group g's next item in D buffer d is
+  // complete (MMA commit).  Each barrier is waited by one group, in item
+  // order, and the MMA cannot commit that group's next item in buffer d
+  // before the group released the previous one, so a barrier never runs a
+  // phase ahead of its waiter.  (A parity wait on a barrier two phases ahead
+  // would never return: one barrier per group alone allows that when a group
+  // owns two consecutive items in different D buffers.)
   uint64_t* dfull = aempty + kAItems;
-  uint64_t* xfull = dfull + 2;    // [2] X buffer written (8 dequantiser warps)
-  uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 4 epilogue warps)
+  uint64_t* xfull = dfull + 4;    // [2] X buffer written
+  uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 8 epilogue warps)
   uint64_t* fin = xempty + 2;
-  uint64_t* xsync = fin + 1;      // dequantisers, inside an X build
+  uint64_t* xsync = fin + 1;      // dequantisers, inside a split-K X build
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xsync + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -210,9 +213,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&ready[h], kDeWarps + 4);
       mbar_init(&aempty[h], 1);
     }
+    for (int d = 0; d < 4; d++) mbar_init(&dfull[d], 1);
     for (int d = 0; d < 2; d++) {
-      mbar_init(&dfull[d], 1);
-      mbar_init(&xfull[d], kDeWarps);
+      mbar_init(&xfull[d], p.tile_major ? 1 : kDeWarps);
       mbar_init(&xempty[d], 1 + kEpiWarps);
     }
     mbar_init(fin, 1);
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           mma_i8_ts(dbase + p.op_d[st], abase + st * 8, xd0 + xoff, idesc, (p.acc_mask >> st) & 1u);
         }
         mma_commit(&aempty[h]);
-        mma_commit(&dfull[(p.tile_major ? tig : j) & 1]);
+        mma_commit(&dfull[((p.tile_major ? tig : j) & 1) * 2 + d]);
         j++;
         return true;
       });
@@ -306,32 +309,154 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       if (!mbar_wait(fin, 0)) record_error(p.err, KERR_WAIT_MMA);
     }
     __syncwarp();
+  } else if (warp == kXWarp && p.tile_major) {
+    // ---------------- X builder (tile-major) ----------------
+    // One warp builds X, the digit sums, the row exponents and the blocks'
+    // sums of X for chunk c + 1 as soon as its buffer is free, while the
+    // dequantisers stream chunk c.  (Split-K CTAs build their single chunk
+    // once, at the start and on the critical path: the dequantiser warps do
+    // that together, below.)  Unit u = lane + 32 i (i < 4M) is 4
+    // consecutive k of row i / 4 (128 units per row).
+    for (int i = lane; i < 2 * (int)kXBufBytes / 16; i += 32)
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
+                   : "memory");
+    __syncwarp();
+    griddep_wait();  // activations come from the previous kernel in the stream
+    const int seg = min(32, p.bs / 4);  // lanes whose units share a block
+    bool ok = true;
+    int cur = -1, nbuild = 0;
+    for_each_item(p, [&](int, int chunk, int) {
+      if (!ok) return false;
+      if (chunk == cur) return true;
+      cur = chunk;
+      const int xbuf = nbuild & 1;
+      if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
+        record_error(p.err, KERR_WAIT_EMPTY);
+        return ok = false;
+      }
+      uint8_t* xbase = Xs + xbuf * kXBufBytes;
+      int* rexp = reinterpret_cast<int*>(xbase + kXRexp);      // [8]
+      int* csum = reinterpret_cast<int*>(xbase + kXCsum);      // [bpi][M][3]
+      float* xsum = reinterpret_cast<float*>(xbase + kXXsum);  // [bpi][M]
+      for (int i = lane; i < p.bpi * M * 3; i += 32) csum[i] = 0;
+      const int k0 = chunk * kChunkK;
+      auto load = [&](int i) {
+        const int m = i >> 2, k = k0 + (lane + 32 * (i & 3)) * 4;
+        const float* src = p.A + (int64_t)m * p.K + k;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p.a_vec && k + 3 < p.K) {
+          a = __ldg(reinterpret_cast<const float4*>(src));
+        } else {
+          if (k < p.K) a.x = src[0];
+          if (k + 1 < p.K) a.y = src[1];
+          if (k + 2 < p.K) a.z = src[2];
+          if (k + 3 < p.K) a.w = src[3];
+        }
+        return a;
+      };
+      // M <= 2: the first pass's values stay in registers (one round trip to
+      // L2 per build); larger M loads them again in the second pass
+      constexpr int kKeep = M <= 2 ? 4 * M : 1;
+      float4 kept[kKeep];
+      // chunk exponent per row: |rint(a * 2^S)| <= 2^22 for every a of the row
+      int S[M];
+#pragma unroll
+      for (int m = 0; m < M; m++) {
+        unsigned mb = 0;  // largest magnitude as bits; inf / NaN compare above 0x7f7fffff
+#pragma unroll
+        for (int i = 4 * m; i < 4 * m + 4; i++) {
+          const float4 a = load(i);
+          if (M <= 2) kept[M <= 2 ? i : 0] = a;
+          mb = max(mb, max(max(__float_as_uint(a.x) & 0x7fffffffu, __float_as_uint(a.y) & 0x7fffffffu),
+                           max(__float_as_uint(a.z) & 0x7fffffffu, __float_as_uint(a.w) & 0x7fffffffu)));
+        }
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        S[m] = 0;
+        if (mb > 0x7f7fffffu) {
+          S[m] = kNonFinite;
+        } else if (mb != 0) {
+          int ex;
+          frexpf(__uint_as_float(mb), &ex);  // max < 2^ex
+          S[m] = 22 - ex;
+        }
+        if (lane == 0) rexp[m] = S[m];
+      }
+      __syncwarp();
+      const uint32_t xb = smem_u32(xbase);
+#pragma unroll
+      for (int i = 0; i < 4 * M; i++) {
+        const int m = i >> 2, k = (lane + 32 * (i & 3)) * 4;
+        const int bl = k / p.bs, slot = bl % G;
+        const float4 a = M <= 2 ? kept[M <= 2 ? i : 0] : load(i);
+        const float vals[4] = {a.x, a.y, a.z, a.w};
+        uint32_t w0 = 0, w1 = 0, w2 = 0;
+        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+          const int X = S[m] == kNonFinite ? 0 : __float2int_rn(scale_pow2(vals[v], S[m]));
+          // balanced base-256 digits: X = c2*65536 + c1*256 + c0, each in [-128, 127]
+          const int c0 = ((X + 128) & 255) - 128;
+          const int X1 = (X - c0) >> 8;
+          const int c1 = ((X1 + 128) & 255) - 128;
+          const int c2 = (X1 - c1) >> 8;
+          w0 |= (uint32_t)(c0 & 255) << (8 * v);
+          w1 |= (uint32_t)(c1 & 255) << (8 * v);
+          w2 |= (uint32_t)(c2 & 255) << (8 * v);
+          s0 += c0;
+          s1 += c1;
+          s2 += c2;
+        }
+        const int jr = (slot * M + m) * 3;
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
+                     : "memory");
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
+                     : "memory");
+        // digit sums of the block: add across the aligned run of `seg` lanes;
+        // the run leaders of one i hold distinct blocks, so plain adds suffice
+        for (int off = 1; off < seg; off <<= 1) {
+          s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+          s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+          s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+        }
+        if ((lane & (seg - 1)) == 0) {
+          int* cs = csum + (bl * M + m) * 3;
+          cs[0] += s0;
+          cs[1] += s1;
+          cs[2] += s2;
+        }
+        __syncwarp();
+      }
+      // each block's sum of X per row, for the zero-point term z * sum X
+      for (int i = lane; i < p.bpi * M; i += 32)
+        xsum[i] = ((float)csum[i * 3 + 2] * 65536.0f + (float)csum[i * 3 + 1] * 256.0f) +
+                  (float)csum[i * 3];
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xfull[xbuf]);
+      nbuild++;
+      return true;
+    });
   } else if (warp < kDeWarps) {
-    // ---------------- dequantisers (and X builds) ----------------
+    // ---------------- dequantisers ----------------
     const int q = warp & 3, grp = warp >> 2;
     const int nl = q * 32 + lane;  // column within the tile = TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    // Zero both X buffers once: the non-zero pattern is the same for every
-    // chunk, so each build rewrites only those entries.
-    for (int i = threadIdx.x; i < 2 * (int)kXBufBytes / 16; i += kDeWarps * 32)
-      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
-                   : "memory");
-    uint32_t xph = 0;
-    bool ok = warp_group_sync(xsync, xph, p.err);
-    griddep_wait();  // activations come from the previous kernel in the stream
-
-    constexpr int kU = kChunkK / 4;                          // 4-k units per row
-    constexpr int kPer = (M * kU + kDeWarps * 32 - 1) / (kDeWarps * 32);
-    int j = 0, cur = -1, nbuild = 0;
-    for_each_item(p, [&](int, int chunk, int) {
-      if (!ok) return false;
-      if (chunk != cur) {
-        // X, digit sums and row exponents of this chunk, into buffer nbuild & 1.
-        const int xbuf = nbuild & 1;
-        if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
-          record_error(p.err, KERR_WAIT_EMPTY);
-          return ok = false;
-        }
+    bool ok = true;
+    if (!p.tile_major) {
+      // the CTA's one chunk: X, digit sums, row exponents, all 8 warps
+      for (int i = threadIdx.x; i < 2 * (int)kXBufBytes / 16; i += kDeWarps * 32)
+        asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16),
+                     "r"(0u)
+                     : "memory");
+      uint32_t xph = 0;
+      ok = warp_group_sync(xsync, xph, p.err);
+      griddep_wait();  // activations come from the previous kernel in the stream
+      constexpr int kU = kChunkK / 4;  // 4-k units per row
+      constexpr int kPer = (M * kU + kDeWarps * 32 - 1) / (kDeWarps * 32);
+      const int chunk = (int)(blockIdx.x % p.nch), xbuf = 0;
+      {
+        // into buffer 0 (first use: free)
         uint8_t* xbase = Xs + xbuf * kXBufBytes;
         unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXRmax);  // [8]
         int* rexp = reinterpret_cast<int*>(xbase + kXRexp);            // [8]
@@ -339,7 +464,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         float* xsum = reinterpret_cast<float*>(xbase + kXXsum);        // [bpi][M]
         if (threadIdx.x < 8) rmax[threadIdx.x] = 0;
         for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
-        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        if (ok && !warp_group_sync(xsync, xph, p.err)) ok = false;
         // Activations of the chunk, unit u = 4 consecutive k of row u / kU.
         // A warp's 32 units lie in one row.
         const int k0 = chunk * kChunkK;
@@ -367,7 +492,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           av[i] = a;
         }
-        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        if (ok && !warp_group_sync(xsync, xph, p.err)) ok = false;
         const uint32_t xb = smem_u32(xbase);
 #pragma unroll
         for (int i = 0; i < kPer; i++) {
@@ -424,7 +549,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             atomicAdd(cs + 2, s2);
           }
         }
-        if (!warp_group_sync(xsync, xph, p.err)) return ok = false;
+        if (ok && !warp_group_sync(xsync, xph, p.err)) ok = false;
         // each block's sum of X per row, for the zero-point term z * sum X
         for (int i = threadIdx.x; i < p.bpi * M; i += kDeWarps * 32)
           xsum[i] = ((float)csum[i * 3 + 2] * 65536.0f + (float)csum[i * 3 + 1] * 256.0f) +
@@ -432,9 +557,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&xfull[xbuf]);
-        cur = chunk;
-        nbuild++;
       }
+    }
+    int j = 0;
+    for_each_item(p, [&](int, int, int) {
+      if (!ok) return false;
       const int bst = j % p.nbst;
       if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1)) {
         record_error(p.err, KERR_WAIT_FULL);
@@ -483,7 +610,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     griddep_wait();  // outputs and split-K scratch may still be in use upstream
     bool ok = true;
     int S_m[M];
-    int j = 0, cur = -1, nbuild = 0, mine = 0;
+    int j = 0, cur = -1, nbuild = 0, mine[2] = {0, 0};  // waits done per D buffer
     for_each_item(p, [&](int tile, int chunk, int tig) {
       if (!ok) return false;
       if (chunk != cur) {
@@ -506,11 +633,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         return true;
       }
       const int bst = j % p.nbst, d = j % p.nd;
-      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) || !mbar_wait(&dfull[egrp], mine & 1)) {
+      if (!mbar_wait(&bfull[bst], (j / p.nbst) & 1) ||
+          !mbar_wait(&dfull[egrp * 2 + d], mine[d] & 1)) {
         record_error(p.err, KERR_WAIT_MMA);
         return ok = false;
       }
-      mine++;
+      mine[d]++;
       tc_fence_after();
       float y[M];
 #pragma unroll

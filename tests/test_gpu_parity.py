@@ -418,3 +418,38 @@ def test_launch_counter_counts_own_kernels(sess):
     before = sess.launch_count()
     sess.matmul_nbits("lc2", rng.standard_normal((1, 1024)).astype(np.float32))
     assert sess.launch_count() in (before + 1, before + 2)
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 128256, 1), (2048, 148 * 3 * 128, 1), (2048, 148 * 3 * 128, 3)])
+def test_tile_major_back_to_back(K, N, M):
+    """Tile-major decode GEMVs where CTAs own an odd number of tiles, so one
+    epilogue group takes two consecutive items at every chunk boundary,
+    launched many times back to back on device buffers (each launch
+    overlaps its predecessor's tail).  No bounded wait may expire (the
+    session reports it at sync) and every result equals the first bit for
+    bit and matches the oracle."""
+    import torch
+    from onnx_runtime_dart_b200 import CudaSession
+    s = CudaSession(0, mode="exact")
+    try:
+        st = torch.cuda.Stream()
+        s.set_stream(st.cuda_stream)
+        rng = np.random.default_rng(77)
+        B, sc, z = O.make_nbits_weight(rng, K, N, 128, zero_points=True)
+        s.upload_nbits("w", B, sc, z, k=K, n=N, block_size=128)
+        A = rng.standard_normal((M, K)).astype(np.float32)
+        reps = 40
+        with torch.cuda.stream(st):
+            a = torch.from_numpy(A).to("cuda")
+            y = torch.empty(reps, M, N, device="cuda")
+            for r in range(reps):
+                s.matmul_nbits("w", a, out=y[r])
+            st.synchronize()
+        s.sync()
+        out = y.cpu().numpy()
+        for r in range(1, reps):
+            assert np.array_equal(out[r], out[0]), f"launch {r} differs"
+        ref = O.matmul_nbits(A, B, sc, z, K, N, 4, 128, threads=8)
+        assert max_rel(ref, out[0]) <= EXACT_TOL
+    finally:
+        s.close()
