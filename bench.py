@@ -310,6 +310,7 @@ def main():
     launches = sess.launch_count() - launches0
     if gid is not None:
         sess.graph_drop(gid)
+    sess.sync()  # raises if any kernel of the timed steps reported an error
     clk = clocks.stop()
     ms_step = e0.elapsed_time(e1) / args.steps
     big_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
@@ -339,6 +340,7 @@ def main():
         step_prefill(pev[i])
     e1.record(stream)
     barrier()
+    sess.sync()
     pf_ms = e0.elapsed_time(e1) / pf_steps
     pf_big_ms = sum(a.elapsed_time(b) for a, b in pev) / pf_steps
     rank_flops = 0
@@ -405,8 +407,9 @@ def main():
                        "mode": args.mode,
                        "launch": ("op-by-op calls" if args.eager else
                                   "CUDA graph of the timed steps, one replay"),
-                       "parallelism": f"N-sharded x{world}" + (" + NCCL all-gather of Y"
-                                                              if world > 1 else ""),
+                       "parallelism": f"N-sharded x{world}" + (
+                           " + all-gather of Y over peer memory (NCCL where peers cannot "
+                           "be mapped)" if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 387 MB of weights per step)"},
             "roofline": {"bound": "hbm", "kernel": f"int4 GEMV ({big.name})",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",

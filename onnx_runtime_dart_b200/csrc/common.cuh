@@ -185,7 +185,7 @@ int encode_tma_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 // tc_gemv_partial_floats() floats (no initial value needed).
 int prepare_nbits_tc(Weight& w);
 bool tc_gemv_ok(const Weight& w, int64_t M);
-size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count);
+size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count);
 int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
                    float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
                    const YSel* ysel = nullptr);

@@ -79,7 +79,7 @@ constexpr uint32_t kDCols = kTmemCols - kDCol;          // 256 columns for D
 constexpr int kMaxBpi = kChunkK / kMinBs;               // blocks per item
 constexpr uint32_t kXBytesMax = 32 * kChunkK;           // X for NM = 32
 // X buffer: X, then the rows' largest-magnitude bits [8] and exponents [8],
-// the blocks' digit sums [bpi][M][3] (int) and their fp32 totals [bpi][M].
+// the blocks' sums of X [bpi][M] (exact, int64) and their fp32 values.
 constexpr uint32_t kXRmax = kXBytesMax, kXRexp = kXBytesMax + 32, kXCsum = kXBytesMax + 64;
 constexpr uint32_t kXXsum = kXCsum + kMaxBpi * 8 * 3 * 4;
 constexpr uint32_t kXBufBytes = (kXXsum + kMaxBpi * 8 * 4 + 1023) & ~1023u;
@@ -100,13 +100,13 @@ struct TcParams {
   YSel ysel;     // tile-major output redirected to a peer-exchange half
   int* err;
   int64_t ldy;
-  int N, K, bs, nch, tiles;
-  int tile_major;  // 1: a CTA loops over all chunks of its tiles
-  int grid_tiles;  // tile-major: tiles t = blockIdx.x + i*grid_tiles
-  int cluster;     // split-K: the nch CTAs of a tile set form a cluster and
-                   // sum their partials through distributed shared memory
-  uint32_t yacc_bytes;  // tile-major accumulators or cluster partials
-  int tg;          // tile-major: tiles per group (y accumulators in smem)
+  int N, K, bs, bs_log2, nch, tiles;  // bs a power of two
+  int tile_major;  // 1: a CTA loops over chunks [c0, c1) of its tile set
+  int csize;       // tile-major: CTAs per cluster (1: no cluster); rank r
+                   // takes chunks [r*nch/csize, (r+1)*nch/csize)
+  int ncl;         // tile-major: tile sets; set s owns tiles s + i*ncl
+  uint32_t yacc_bytes;  // csize 1: chunk-order sums; else the partials inbox
+  int tg;          // tile-major: tiles per group (chunks outer in a group)
   int cpc;         // split-K: CTAs per chunk
   int bpi, regions, has_zp, z_rows, nbst;
   int a_vec;       // A 16-byte aligned and K % 4 == 0: 16-byte activation loads
@@ -125,11 +125,13 @@ struct TcParams {
 template <typename F>
 __device__ __forceinline__ void for_each_item(const TcParams& p, F&& f) {
   if (p.tile_major) {
-    const int span = p.grid_tiles * p.tg;
-    for (int g0 = blockIdx.x; g0 < p.tiles; g0 += span)
-      for (int c = 0; c < p.nch; c++)
+    const int set = (int)blockIdx.x / p.csize, rank = (int)blockIdx.x % p.csize;
+    const int c0 = rank * p.nch / p.csize, c1 = (rank + 1) * p.nch / p.csize;
+    const int span = p.ncl * p.tg;
+    for (int g0 = set; g0 < p.tiles; g0 += span)
+      for (int c = c0; c < c1; c++)
         for (int i = 0; i < p.tg; i++) {
-          const int t = g0 + i * p.grid_tiles;
+          const int t = g0 + i * p.ncl;
           if (t >= p.tiles) break;
           if (!f(t, c, i)) return;
         }
@@ -170,6 +172,64 @@ __device__ __forceinline__ uint32_t x_addr(uint32_t base, int nm, int j, int k) 
          (kin & 15);
 }
 
+// Scale of one row of a chunk: S with |rint(a * 2^S)| <= 2^22 for every a
+// of the row (mb: its largest magnitude as bits; inf and NaN compare above
+// 0x7f7fffff and give kNonFinite), and 2^S as two exact power-of-two
+// factors applied as (a * f1) * f2, since |S| may exceed a float exponent.
+struct RowScale {
+  int S;
+  float f1, f2;
+};
+__device__ __forceinline__ RowScale row_scale(unsigned mb) {
+  RowScale r;
+  r.S = 0;
+  if (mb > 0x7f7fffffu) {
+    r.S = kNonFinite;
+  } else if (mb != 0) {
+    int ex;
+    frexpf(__uint_as_float(mb), &ex);  // max < 2^ex
+    r.S = 22 - ex;
+  }
+  const int e = r.S == kNonFinite ? 0 : r.S;
+  if (e > 100) {
+    r.f1 = pow2f(100);
+    r.f2 = pow2f(e - 100);
+  } else if (e < -100) {
+    r.f1 = pow2f(-100);
+    r.f2 = pow2f(e + 100);
+  } else {
+    r.f1 = pow2f(e);
+    r.f2 = 1.0f;
+  }
+  return r;
+}
+
+// X = rint(a * 2^S) of four consecutive activations of a row, as three
+// words of int8 digits (word t holds digit t of the four values, X = c2 *
+// 65536 + c1 * 256 + c0 with every c in [-128, 127]) and the sum of the four
+// X.  With U = X + 0x808080 (0 <= U < 2^24 since |X| <= 2^22), byte t of
+// U ^ 0x808080 is c_t as an int8; byte permutes gather the words.
+__device__ __forceinline__ void x_digits(float4 a, const RowScale& r, uint32_t& w0, uint32_t& w1,
+                                         uint32_t& w2, int& sx) {
+  int X0 = 0, X1 = 0, X2 = 0, X3 = 0;
+  if (r.S != kNonFinite) {
+    X0 = __float2int_rn((a.x * r.f1) * r.f2);
+    X1 = __float2int_rn((a.y * r.f1) * r.f2);
+    X2 = __float2int_rn((a.z * r.f1) * r.f2);
+    X3 = __float2int_rn((a.w * r.f1) * r.f2);
+  }
+  sx = (X0 + X1) + (X2 + X3);
+  const uint32_t V0 = (uint32_t)(X0 + 0x808080) ^ 0x808080u;
+  const uint32_t V1 = (uint32_t)(X1 + 0x808080) ^ 0x808080u;
+  const uint32_t V2 = (uint32_t)(X2 + 0x808080) ^ 0x808080u;
+  const uint32_t V3 = (uint32_t)(X3 + 0x808080) ^ 0x808080u;
+  const uint32_t lo01 = __byte_perm(V0, V1, 0x5140), lo23 = __byte_perm(V2, V3, 0x5140);
+  const uint32_t hi01 = __byte_perm(V0, V1, 0x7362), hi23 = __byte_perm(V2, V3, 0x7362);
+  w0 = __byte_perm(lo01, lo23, 0x5410);
+  w1 = __byte_perm(lo01, lo23, 0x7632);
+  w2 = __byte_perm(hi01, hi23, 0x5410);
+}
+
 template <int M>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
@@ -200,7 +260,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* xempty = xfull + 2;   // [2] X buffer released (MMA commit + 8 epilogue warps)
   uint64_t* fin = xempty + 2;
   uint64_t* xsync = fin + 1;      // dequantisers, inside a split-K X build
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xsync + 1);
+  // cluster mode: every epilogue warp of the cluster has delivered its
+  // partials of this CTA's tiles (remote arrivals, csize x 8)
+  uint64_t* ibar = xsync + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ibar + 1);
+  const bool clustered = p.tile_major && p.csize > 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -220,6 +284,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
     mbar_init(fin, 1);
     mbar_init(xsync, kDeWarps);
+    mbar_init(ibar, p.csize * kEpiWarps);
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
@@ -229,6 +294,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // other CTAs of the cluster may arrive on ibar once every CTA has passed
+  // this point (each thread waits before its first remote access)
+  if (clustered) cluster_arrive_relaxed();
   const uint32_t tmem = *tmem_slot;
   // The next kernel in the stream may start its prologue and weight stream
   // as our CTAs retire; it waits for our completion before touching
@@ -270,6 +338,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   } else if (warp == kMmaWarp) {
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_i8(128, NM);
+      // the stage table and D layout, read before the first wait (a first
+      // read of a kernel parameter can miss the constant cache)
+      asm volatile("" ::"r"(p.op_d[0]), "r"(p.op_d[kItemStages - 1]), "r"(p.acc_mask), "r"(p.nd),
+                   "r"(p.dstride));
       int j = 0, cur = -1, nbuild = 0;
       for_each_item(p, [&](int, int chunk, int tig) {
         if (chunk != cur) {
@@ -301,7 +373,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           mma_i8_ts(dbase + p.op_d[st], abase + st * 8, xd0 + xoff, idesc, (p.acc_mask >> st) & 1u);
         }
         mma_commit(&aempty[h]);
-        mma_commit(&dfull[((p.tile_major ? tig : j) & 1) * 2 + d]);
+        mma_commit(&dfull[(((p.tile_major && !clustered) ? tig : j) & 1) * 2 + d]);
         j++;
         return true;
       });
@@ -311,126 +383,120 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     __syncwarp();
   } else if (warp == kXWarp && p.tile_major) {
     // ---------------- X builder (tile-major) ----------------
-    // One warp builds X, the digit sums, the row exponents and the blocks'
-    // sums of X for chunk c + 1 as soon as its buffer is free, while the
-    // dequantisers stream chunk c.  (Split-K CTAs build their single chunk
-    // once, at the start and on the critical path: the dequantiser warps do
-    // that together, below.)  Unit u = lane + 32 i (i < 4M) is 4
-    // consecutive k of row i / 4 (128 units per row).
+    // One warp builds X, the row exponents and the blocks' sums of X for
+    // chunk c + 1 as soon as its buffer is free, while the dequantisers
+    // stream chunk c.  (Split-K CTAs build their single chunk once, at the
+    // start and on the critical path: the dequantiser warps do that
+    // together, below.)  Unit i (< 4M) of a lane is 4 consecutive k of row
+    // i / 4 at k = 4 (lane + 32 (i % 4)); for M <= 2 the next chunk's units
+    // are loaded right after a build, so a build does not wait for them.
     for (int i = lane; i < 2 * (int)kXBufBytes / 16; i += 32)
       asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
                    : "memory");
+    // Every parameter the builds use, read before the dependency wait: a
+    // first read of a kernel parameter can miss the constant cache, and
+    // after the wait it would delay the first X.
+    const int seg = min(32, p.bs / 4);  // lanes whose units share a block
+    // the aligned run of `seg` lanes holding this lane's block
+    const unsigned segmask =
+        seg == 32 ? 0xffffffffu : ((1u << seg) - 1u) << (lane & ~(seg - 1));
+    const int rank = (int)blockIdx.x % p.csize;
+    const int c_first = rank * p.nch / p.csize, c_end = (rank + 1) * p.nch / p.csize;
+    const float* const Ap = p.A;
+    const int K = p.K, a_vec = p.a_vec, bs_log2 = p.bs_log2, bpi = p.bpi;
+    asm volatile("" ::"l"(Ap), "r"(K), "r"(a_vec), "r"(bs_log2), "r"(bpi), "r"(c_first),
+                 "r"(c_end), "r"(segmask));
     __syncwarp();
     griddep_wait();  // activations come from the previous kernel in the stream
-    const int seg = min(32, p.bs / 4);  // lanes whose units share a block
+    auto load = [&](int chunk, int i) {
+      const int m = i >> 2, k = chunk * kChunkK + (lane + 32 * (i & 3)) * 4;
+      const float* src = Ap + (int64_t)m * K + k;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a_vec && k + 3 < K) {
+        a = __ldg(reinterpret_cast<const float4*>(src));
+      } else {
+        if (k < K) a.x = src[0];
+        if (k + 1 < K) a.y = src[1];
+        if (k + 2 < K) a.z = src[2];
+        if (k + 3 < K) a.w = src[3];
+      }
+      return a;
+    };
+    constexpr int kPre = M <= 2 ? 4 * M : 1;
+    float4 pre[kPre];  // M <= 2: the units of chunk pre_chunk
+    int pre_chunk = -1;
     bool ok = true;
     int cur = -1, nbuild = 0;
     for_each_item(p, [&](int, int chunk, int) {
       if (!ok) return false;
       if (chunk == cur) return true;
       cur = chunk;
+      if (M <= 2 && pre_chunk != chunk) {
+#pragma unroll
+        for (int i = 0; i < kPre; i++) pre[i] = load(chunk, i);
+      }
       const int xbuf = nbuild & 1;
       if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
         record_error(p.err, KERR_WAIT_EMPTY);
         return ok = false;
       }
       uint8_t* xbase = Xs + xbuf * kXBufBytes;
-      int* rexp = reinterpret_cast<int*>(xbase + kXRexp);      // [8]
-      int* csum = reinterpret_cast<int*>(xbase + kXCsum);      // [bpi][M][3]
-      float* xsum = reinterpret_cast<float*>(xbase + kXXsum);  // [bpi][M]
-      for (int i = lane; i < p.bpi * M * 3; i += 32) csum[i] = 0;
-      const int k0 = chunk * kChunkK;
-      auto load = [&](int i) {
-        const int m = i >> 2, k = k0 + (lane + 32 * (i & 3)) * 4;
-        const float* src = p.A + (int64_t)m * p.K + k;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (p.a_vec && k + 3 < p.K) {
-          a = __ldg(reinterpret_cast<const float4*>(src));
-        } else {
-          if (k < p.K) a.x = src[0];
-          if (k + 1 < p.K) a.y = src[1];
-          if (k + 2 < p.K) a.z = src[2];
-          if (k + 3 < p.K) a.w = src[3];
-        }
-        return a;
-      };
-      // M <= 2: the first pass's values stay in registers (one round trip to
-      // L2 per build); larger M loads them again in the second pass
-      constexpr int kKeep = M <= 2 ? 4 * M : 1;
-      float4 kept[kKeep];
-      // chunk exponent per row: |rint(a * 2^S)| <= 2^22 for every a of the row
-      int S[M];
+      int* rexp = reinterpret_cast<int*>(xbase + kXRexp);              // [8]
+      long long* csum = reinterpret_cast<long long*>(xbase + kXCsum);  // [bpi][M]
+      float* xsum = reinterpret_cast<float*>(xbase + kXXsum);          // [bpi][M]
+      for (int i = lane; i < bpi * M; i += 32) csum[i] = 0;
+      RowScale rs[M];
 #pragma unroll
       for (int m = 0; m < M; m++) {
-        unsigned mb = 0;  // largest magnitude as bits; inf / NaN compare above 0x7f7fffff
+        unsigned mb = 0;
 #pragma unroll
         for (int i = 4 * m; i < 4 * m + 4; i++) {
-          const float4 a = load(i);
-          if (M <= 2) kept[M <= 2 ? i : 0] = a;
+          const float4 a = M <= 2 ? pre[M <= 2 ? i : 0] : load(chunk, i);
           mb = max(mb, max(max(__float_as_uint(a.x) & 0x7fffffffu, __float_as_uint(a.y) & 0x7fffffffu),
                            max(__float_as_uint(a.z) & 0x7fffffffu, __float_as_uint(a.w) & 0x7fffffffu)));
         }
-        mb = __reduce_max_sync(0xffffffffu, mb);
-        S[m] = 0;
-        if (mb > 0x7f7fffffu) {
-          S[m] = kNonFinite;
-        } else if (mb != 0) {
-          int ex;
-          frexpf(__uint_as_float(mb), &ex);  // max < 2^ex
-          S[m] = 22 - ex;
-        }
-        if (lane == 0) rexp[m] = S[m];
+        rs[m] = row_scale(__reduce_max_sync(0xffffffffu, mb));
+        if (lane == 0) rexp[m] = rs[m].S;
       }
       __syncwarp();
       const uint32_t xb = smem_u32(xbase);
+      // per row, three passes, so that the units' independent work overlaps:
+      // digits and stores, the blocks' sums over their runs of lanes, the
+      // leaders' adds (|sum| <= 2^29; a block always has the same leader
+      // lane, so its adds are ordered)
 #pragma unroll
-      for (int i = 0; i < 4 * M; i++) {
-        const int m = i >> 2, k = (lane + 32 * (i & 3)) * 4;
-        const int bl = k / p.bs, slot = bl % G;
-        const float4 a = M <= 2 ? kept[M <= 2 ? i : 0] : load(i);
-        const float vals[4] = {a.x, a.y, a.z, a.w};
-        uint32_t w0 = 0, w1 = 0, w2 = 0;
-        int s0 = 0, s1 = 0, s2 = 0;
+      for (int m = 0; m < M; m++) {
+        int sx[4];
 #pragma unroll
-        for (int v = 0; v < 4; v++) {
-          const int X = S[m] == kNonFinite ? 0 : __float2int_rn(scale_pow2(vals[v], S[m]));
-          // balanced base-256 digits: X = c2*65536 + c1*256 + c0, each in [-128, 127]
-          const int c0 = ((X + 128) & 255) - 128;
-          const int X1 = (X - c0) >> 8;
-          const int c1 = ((X1 + 128) & 255) - 128;
-          const int c2 = (X1 - c1) >> 8;
-          w0 |= (uint32_t)(c0 & 255) << (8 * v);
-          w1 |= (uint32_t)(c1 & 255) << (8 * v);
-          w2 |= (uint32_t)(c2 & 255) << (8 * v);
-          s0 += c0;
-          s1 += c1;
-          s2 += c2;
+        for (int q4 = 0; q4 < 4; q4++) {
+          const int i = 4 * m + q4, k = (lane + 32 * q4) * 4;
+          const int slot = (k >> bs_log2) % G;
+          uint32_t w0, w1, w2;
+          x_digits(M <= 2 ? pre[M <= 2 ? i : 0] : load(chunk, i), rs[m], w0, w1, w2, sx[q4]);
+          const int jr = (slot * M + m) * 3;
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
+                       : "memory");
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
+                       : "memory");
         }
-        const int jr = (slot * M + m) * 3;
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
-                     : "memory");
-        asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
-                     : "memory");
-        // digit sums of the block: add across the aligned run of `seg` lanes;
-        // the run leaders of one i hold distinct blocks, so plain adds suffice
-        for (int off = 1; off < seg; off <<= 1) {
-          s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-          s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-          s2 += __shfl_xor_sync(0xffffffffu, s2, off);
-        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) sx[q4] = __reduce_add_sync(segmask, sx[q4]);
         if ((lane & (seg - 1)) == 0) {
-          int* cs = csum + (bl * M + m) * 3;
-          cs[0] += s0;
-          cs[1] += s1;
-          cs[2] += s2;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; q4++)
+            csum[(((lane + 32 * q4) * 4) >> bs_log2) * M + m] += sx[q4];
         }
-        __syncwarp();
       }
+      if (M <= 2) {  // the next chunk this CTA builds (or a harmless reload)
+        const int nx = chunk + 1 < c_end ? chunk + 1 : c_first;
+#pragma unroll
+        for (int i = 0; i < kPre; i++) pre[i] = load(nx, i);
+        pre_chunk = nx;
+      }
+      __syncwarp();
       // each block's sum of X per row, for the zero-point term z * sum X
-      for (int i = lane; i < p.bpi * M; i += 32)
-        xsum[i] = ((float)csum[i * 3 + 2] * 65536.0f + (float)csum[i * 3 + 1] * 256.0f) +
-                  (float)csum[i * 3];
+      for (int i = lane; i < bpi * M; i += 32) xsum[i] = (float)csum[i];
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&xfull[xbuf]);
@@ -451,6 +517,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                      : "memory");
       uint32_t xph = 0;
       ok = warp_group_sync(xsync, xph, p.err);
+      // parameters of the build, read before the dependency wait
+      asm volatile("" ::"l"(p.A), "r"(p.K), "r"(p.a_vec), "r"(p.bs_log2), "r"(p.bs), "r"(p.bpi));
       griddep_wait();  // activations come from the previous kernel in the stream
       constexpr int kU = kChunkK / 4;  // 4-k units per row
       constexpr int kPer = (M * kU + kDeWarps * 32 - 1) / (kDeWarps * 32);
@@ -458,12 +526,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       {
         // into buffer 0 (first use: free)
         uint8_t* xbase = Xs + xbuf * kXBufBytes;
-        unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXRmax);  // [8]
-        int* rexp = reinterpret_cast<int*>(xbase + kXRexp);            // [8]
-        int* csum = reinterpret_cast<int*>(xbase + kXCsum);            // [bpi][M][3]
-        float* xsum = reinterpret_cast<float*>(xbase + kXXsum);        // [bpi][M]
+        unsigned* rmax = reinterpret_cast<unsigned*>(xbase + kXRmax);    // [8]
+        int* rexp = reinterpret_cast<int*>(xbase + kXRexp);              // [8]
+        long long* csum = reinterpret_cast<long long*>(xbase + kXCsum);  // [bpi][M]
+        float* xsum = reinterpret_cast<float*>(xbase + kXXsum);          // [bpi][M]
         if (threadIdx.x < 8) rmax[threadIdx.x] = 0;
-        for (int i = threadIdx.x; i < p.bpi * M * 3; i += kDeWarps * 32) csum[i] = 0;
+        for (int i = threadIdx.x; i < p.bpi * M; i += kDeWarps * 32) csum[i] = 0;
         if (ok && !warp_group_sync(xsync, xph, p.err)) ok = false;
         // Activations of the chunk, unit u = 4 consecutive k of row u / kU.
         // A warp's 32 units lie in one row.
@@ -499,61 +567,33 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int u = threadIdx.x + i * kDeWarps * 32;
           if (u >= M * kU) continue;
           const int m = u / kU, k = (u % kU) * 4;
-          const int bl = k / p.bs, slot = bl % G;
-          // chunk exponent: |rint(a * 2^S)| <= 2^22 for every a of the row
-          const unsigned mb = rmax[m];
-          int S = 0;
-          if (mb > 0x7f7fffffu) {
-            S = kNonFinite;
-          } else if (mb != 0) {
-            int ex;
-            frexpf(__uint_as_float(mb), &ex);  // max < 2^ex
-            S = 22 - ex;
-          }
-          if ((u % kU) == 0) rexp[m] = S;
-          const float vals[4] = {av[i].x, av[i].y, av[i].z, av[i].w};
-          uint32_t w0 = 0, w1 = 0, w2 = 0;
-          int s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-          for (int v = 0; v < 4; v++) {
-            const int X = S == kNonFinite ? 0 : __float2int_rn(scale_pow2(vals[v], S));
-            // balanced base-256 digits: X = c2*65536 + c1*256 + c0, each in [-128, 127]
-            const int c0 = ((X + 128) & 255) - 128;
-            const int X1 = (X - c0) >> 8;
-            const int c1 = ((X1 + 128) & 255) - 128;
-            const int c2 = (X1 - c1) >> 8;
-            w0 |= (uint32_t)(c0 & 255) << (8 * v);
-            w1 |= (uint32_t)(c1 & 255) << (8 * v);
-            w2 |= (uint32_t)(c2 & 255) << (8 * v);
-            s0 += c0;
-            s1 += c1;
-            s2 += c2;
-          }
+          const int bl = k >> p.bs_log2, slot = bl % G;
+          const RowScale rs = row_scale(rmax[m]);
+          if ((u % kU) == 0) rexp[m] = rs.S;
+          uint32_t w0, w1, w2;
+          int sx;
+          x_digits(av[i], rs, w0, w1, w2, sx);
           const int jr = (slot * M + m) * 3;
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
                        : "memory");
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 2, k)), "r"(w2)
                        : "memory");
-          // digit sums of the block: lanes of one block form an aligned run of
-          // min(32, bs / 4) units; add across it, one atomic per run and digit
-          for (int off = 1; off < p.bs / 4 && off < 32; off <<= 1) {
-            s0 += __shfl_xor_sync(0xffffffffu, s0, off);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, off);
-            s2 += __shfl_xor_sync(0xffffffffu, s2, off);
-          }
-          if ((lane & (min(32, p.bs / 4) - 1)) == 0) {
-            int* cs = csum + (bl * M + m) * 3;
-            atomicAdd(cs + 0, s0);
-            atomicAdd(cs + 1, s1);
-            atomicAdd(cs + 2, s2);
-          }
+          // the block's sum of X: a warp's 32 units are 128 consecutive k of
+          // one row, a block an aligned run of min(32, bs / 4) of its lanes;
+          // one reduction per run, one atomic per run (blocks over 128 k
+          // span several warps)
+          const int seg = min(32, p.bs / 4);
+          const unsigned segmask =
+              seg == 32 ? 0xffffffffu : ((1u << seg) - 1u) << (lane & ~(seg - 1));
+          sx = __reduce_add_sync(segmask, sx);
+          if ((lane & (seg - 1)) == 0)
+            atomicAdd(reinterpret_cast<unsigned long long*>(csum + bl * M + m),
+                      (unsigned long long)(long long)sx);
         }
         if (ok && !warp_group_sync(xsync, xph, p.err)) ok = false;
         // each block's sum of X per row, for the zero-point term z * sum X
-        for (int i = threadIdx.x; i < p.bpi * M; i += kDeWarps * 32)
-          xsum[i] = ((float)csum[i * 3 + 2] * 65536.0f + (float)csum[i * 3 + 1] * 256.0f) +
-                    (float)csum[i * 3];
+        for (int i = threadIdx.x; i < p.bpi * M; i += kDeWarps * 32) xsum[i] = (float)csum[i];
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&xfull[xbuf]);
@@ -598,9 +638,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     });
   } else if (warp < kEpiWarp0 + kEpiWarps) {
     // ---------------- epilogue ----------------
-    // Two groups share the items.  Tile-major: a tile's items always go to
-    // the group of its tile-in-group parity, so its chunk sums in shared
-    // memory stay in chunk order; split-K: items alternate.
+    // Two groups share the items.  Tile-major without a cluster: a tile's
+    // items always go to the group of its tile-in-group parity, so its chunk
+    // sums in shared memory stay in chunk order; otherwise items alternate.
     const int q = warp & 3, egrp = (warp - kEpiWarp0) >> 2;
     const int nl = q * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
@@ -608,6 +648,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (lane == 0 && egrp == 0)
       for (int e = 0; e < p.nd; e++) mbar_arrive(&ready[e]);
     griddep_wait();  // outputs and split-K scratch may still be in use upstream
+    __syncwarp();    // .aligned cluster barrier: the whole warp, converged
+    if (clustered) cluster_wait();
+    const int set = (int)blockIdx.x / p.csize;
     bool ok = true;
     int S_m[M];
     int j = 0, cur = -1, nbuild = 0, mine[2] = {0, 0};  // waits done per D buffer
@@ -628,7 +671,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         cur = chunk;
         nbuild++;
       }
-      if (((p.tile_major ? tig : j) & 1) != egrp) {
+      if ((((p.tile_major && !clustered) ? tig : j) & 1) != egrp) {
         j++;
         return true;
       }
@@ -695,7 +738,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int m = 0; m < M; m++)
         part[m] = S_m[m] == kNonFinite ? __int_as_float(0x7fc00000) : scale_pow2(y[m], -S_m[m]);
       const int n = tile * kTile + nl;
-      if (p.tile_major) {
+      if (p.tile_major && !clustered) {
         // chunk partials summed in chunk order: ((0 + p0) + p1) + ...
         float* ya = yacc + (size_t)tig * M * kTile;
 #pragma unroll
@@ -704,11 +747,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           ya[m * kTile + nl] = acc;
           if (chunk == p.nch - 1 && n < p.N) ysel_base(p.Y, p.ysel)[m * p.ldy + n] = acc;
         }
-      } else if (p.cluster) {
-        // this chunk's partial of the CTA's ti-th tile, for the cluster sum
-        const int ti = (tile - (int)(blockIdx.x / p.nch)) / p.cpc;
+      } else if (clustered) {
+        // into the inbox of the CTA that sums this tile: rank ti % csize,
+        // slot ti / csize, laid out [slot][chunk][m][128]
+        const int ti = (tile - set) / p.ncl;
+        const uint32_t dst = dsmem_addr(
+            smem_u32(yacc) + (uint32_t)((((ti / p.csize) * p.nch + chunk) * M * kTile + nl) * 4),
+            (uint32_t)(ti % p.csize));
 #pragma unroll
-        for (int m = 0; m < M; m++) yacc[(ti * M + m) * kTile + nl] = part[m];
+        for (int m = 0; m < M; m++) st_dsmem_f32(dst + (uint32_t)(m * kTile * 4), part[m]);
       } else {
         const int64_t npad = (int64_t)p.tiles * kTile;
 #pragma unroll
@@ -716,40 +763,56 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
       return true;
     });
+    if (clustered) {
+      // Deliver (also after an error, so that no CTA waits for a delivery
+      // that cannot come): the warp's inbox stores are ordered before lane
+      // 0's cluster fence by the warp barrier, the fence before the relaxed
+      // arrivals, one per summing CTA of the set, from lanes 0 .. nsum-1.
+      const int ntile = (p.tiles - 1 - set) / p.ncl + 1;
+      const int nsum = min(p.csize, ntile);
+      __syncwarp();
+      if (lane == 0) fence_acq_rel_cluster();
+      __syncwarp();
+      if (lane < nsum) mbar_arrive_remote_relaxed(dsmem_addr(smem_u32(ibar), (uint32_t)lane));
+      // Sum the inbox: tiles ti = rank, rank + csize, ... of the set, every
+      // column's nch partials in chunk order ((0 + p_0) + p_1) + ..., the
+      // sum the other paths form.  Only epilogue threads (past
+      // griddepcontrol.wait) write outputs.
+      const int rank = (int)blockIdx.x % p.csize;
+      if (rank < nsum) {
+        if (!mbar_wait_cluster(ibar, 0)) {
+          record_error(p.err, KERR_WAIT_PEER);
+        } else {
+          // every epilogue thread takes (tile, row, column) triples of the
+          // CTA's tiles; partials loaded 8 at a time, added in chunk order
+          const int et = threadIdx.x - kEpiWarp0 * 32;
+          float* Yb = ysel_base(p.Y, p.ysel);
+          const int per = M * kTile, nmine = (ntile - rank + p.csize - 1) / p.csize;
+          for (int i = et; i < nmine * per; i += kEpiWarps * 32) {
+            const int sl = i / per, r = i % per;  // inbox slot = tile rank + sl * csize
+            const int m = r / kTile, n = (set + (rank + sl * p.csize) * p.ncl) * kTile + r % kTile;
+            const float* col = yacc + (size_t)sl * p.nch * per + r;
+            float acc = 0.0f;
+            int c = 0;
+            for (; c + 8 <= p.nch; c += 8) {
+              float v[8];
+#pragma unroll
+              for (int u = 0; u < 8; u++) v[u] = col[(size_t)(c + u) * per];
+#pragma unroll
+              for (int u = 0; u < 8; u++) acc = acc + v[u];
+            }
+            for (; c < p.nch; c++) acc = acc + col[(size_t)c * per];
+            if (n < p.N) Yb[m * p.ldy + n] = acc;
+          }
+        }
+      }
+    }
   }
+  // the other warps' half of the cluster barrier begun after setup
+  __syncwarp();
+  if (clustered && !(warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps)) cluster_wait();
   tc_fence_before();
   __syncthreads();
-  if (p.cluster) {
-    // Split-K across the cluster: CTA rank c sums tiles ti = c, c + nch, ...
-    // of the set over the nch CTAs' partials in chunk order,
-    // ((0 + p_0) + p_1) + ..., as the other paths do.  Only the epilogue
-    // threads (which passed griddepcontrol.wait) write outputs; the second
-    // barrier keeps every CTA's partials alive until all reads are done.
-    cluster_sync_all();
-    if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
-      const int r = (int)(blockIdx.x / p.nch), c = (int)cluster_ctarank();
-      const int ntile = (p.tiles - 1 - r) / p.cpc + 1;
-      const int et = threadIdx.x - kEpiWarp0 * 32;
-      float* Yb = ysel_base(p.Y, p.ysel);
-      const uint32_t base = smem_u32(yacc);
-      for (int ti = c; ti < ntile; ti += p.nch)
-        for (int i = et; i < M * kTile; i += kEpiWarps * 32) {
-          const int m = i / kTile, col = i % kTile;
-          const int n = (r + ti * p.cpc) * kTile + col;
-          const uint32_t off = (uint32_t)(((ti * M + m) * kTile + col) * 4);
-          float v[8];
-#pragma unroll
-          for (int cc = 0; cc < 8; cc++)
-            v[cc] = cc < p.nch ? ld_dsmem_f32(dsmem_addr(base + off, (uint32_t)cc)) : 0.0f;
-          float acc = 0.0f;
-#pragma unroll
-          for (int cc = 0; cc < 8; cc++)
-            if (cc < p.nch) acc = acc + v[cc];
-          if (n < p.N) Yb[m * p.ldy + n] = acc;
-        }
-    }
-    cluster_sync_all();
-  }
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -787,33 +850,141 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
   }
 }
 
-// Work decomposition.  Tile-major when the tiles spread evenly over the SMs
-// (at least one per SM, at least 90% balance); split-K otherwise.  Both sum
-// the chunk partials in chunk order, so the choice never changes a bit.
+// Shared memory of one pipeline stage: the packed item, its block scales
+// (fp32) and its zero points.
+uint32_t tc_stage_bytes(const Weight& w) {
+  const int bpi = kChunkK / w.bs, z_rows = bpi >= 2 ? bpi / 2 : 1;
+  const uint32_t z_off = kPackedBytes + (uint32_t)bpi * kTile * 4;
+  const uint32_t zbytes = w.has_zp ? (uint32_t)z_rows * kTile : 0;
+  return (z_off + zbytes + 1023) & ~1023u;
+}
+
+// Raises the GEMV's shared-memory limit, once per device.
+template <int M>
+int configure_m() {
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemLimit));
+    configured |= 1ull << (dev & 63);
+  }
+  return ORT_CUDA_OK;
+}
+
+// Clusters of `csize` GEMV CTAs (one CTA per SM) resident at once on this
+// device, cached; -1 when none can be launched.
+template <int M>
+int max_clusters_m(int csize) {
+  static int cache[64][9];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& mc = cache[dev & 63][csize];
+  if (mc == 0) {
+    int n = 0;
+    if (configure_m<M>() == ORT_CUDA_OK) {
+      cudaLaunchConfig_t qc = {};
+      qc.gridDim = dim3((unsigned)csize);
+      qc.blockDim = dim3(kThreadsTC);
+      qc.dynamicSmemBytes = kSmemLimit;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = (unsigned)csize;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      qc.attrs = qa;
+      qc.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<M>, &qc) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    mc = n > 0 ? n : -1;
+  }
+  return mc;
+}
+
+int max_clusters(int64_t M, int csize) {
+  switch (M) {
+    case 1: return max_clusters_m<1>(csize);
+    case 2: return max_clusters_m<2>(csize);
+    case 3: return max_clusters_m<3>(csize);
+    case 4: return max_clusters_m<4>(csize);
+    case 5: return max_clusters_m<5>(csize);
+    case 6: return max_clusters_m<6>(csize);
+    case 7: return max_clusters_m<7>(csize);
+    case 8: return max_clusters_m<8>(csize);
+  }
+  return -1;
+}
+
+// Work decomposition.  Every candidate sums a column's chunk partials in
+// chunk order, ((0 + p_0) + p_1) + ..., from identical partials, so the
+// choice never changes a bit:
+//  - tile-major: a CTA owns whole tiles and loops over all their chunks;
+//  - clusters of csize CTAs: a cluster owns a tile set, rank r takes chunks
+//    [r*nch/csize, (r+1)*nch/csize) and stores its partials into the shared
+//    memory of the CTA that sums the tile;
+//  - split-K: CTAs own one chunk of a tile set, a second kernel sums.
+// The plan whose busiest CTA costs least wins; ties go to more CTAs, then
+// to the earlier candidate.  Cost in items: a chunk of T tiles costs
+// max(T, 1.5), since the builder warp takes about 1.5 items' time for a
+// chunk's X and hides it only behind that chunk's items; split-K builds its
+// one chunk with eight warps and pays about three items for the kernel
+// boundary before its sum.  The cluster inbox must leave room for three
+// pipeline stages.
 struct Plan {
   bool tile_major;
-  int nch, tiles, grid, cpc, tg;
+  int nch, tiles, grid, cpc, tg, csize, ncl;
+  uint32_t yacc_bytes;
   size_t partial_floats;
 };
 
-Plan make_plan(int64_t K, int64_t nl, int64_t M, int sm_count) {
-  Plan pl;
-  pl.nch = (int)((K + kChunkK - 1) / kChunkK);
-  pl.tiles = (int)((nl + kTile - 1) / kTile);
-  const int gt = std::min(pl.tiles, sm_count);
-  const double per = (double)pl.tiles / gt;
-  const double eff = per / std::ceil(per);
-  pl.tile_major = pl.nch == 1 || pl.nch > sm_count || (pl.tiles >= sm_count && eff >= 0.9);
-  if (pl.tile_major) {
-    pl.grid = gt;
-    pl.cpc = 0;
-    pl.tg = std::max<int>(1, (int)(32 / M));
-    pl.partial_floats = 0;
-  } else {
-    pl.cpc = std::min(pl.tiles, sm_count / pl.nch);
-    pl.grid = pl.cpc * pl.nch;
-    pl.tg = 1;
-    pl.partial_floats = (size_t)pl.nch * M * pl.tiles * kTile;
+Plan make_plan(const Weight& w, int64_t M, int sm_count) {
+  Plan pl = {};
+  pl.nch = (int)((w.K + kChunkK - 1) / kChunkK);
+  pl.tiles = (int)((w.nl + kTile - 1) / kTile);
+  const size_t stage = tc_stage_bytes(w);
+  const size_t tile_bytes = (size_t)M * kTile * 4;
+  pl.tile_major = true;
+  pl.csize = 1;
+  pl.ncl = std::min(pl.tiles, sm_count);
+  pl.tg = std::max<int>(1, (int)(32 / M));
+  pl.grid = pl.ncl;
+  pl.yacc_bytes = (uint32_t)(pl.tg * tile_bytes);
+  // costs in half items
+  auto chunk_cost = [](int T) { return (int64_t)std::max(2 * T, 3); };
+  int64_t best = chunk_cost((pl.tiles + pl.ncl - 1) / pl.ncl) * pl.nch;
+  int best_ctas = pl.ncl;
+  for (int c = 2; c <= 8 && c <= pl.nch; c++) {
+    const int mc = max_clusters(M, c);
+    if (mc <= 0) continue;
+    const int ncl = std::min(pl.tiles, mc), T = (pl.tiles + ncl - 1) / ncl;
+    const size_t inbox = (size_t)((T + c - 1) / c) * pl.nch * tile_bytes;
+    if (1024 + 2 * (size_t)kXBufBytes + inbox + 1024 + 3 * stage > kSmemLimit) continue;
+    const int64_t items = chunk_cost(T) * ((pl.nch + c - 1) / c);
+    if (items < best || (items == best && ncl * c > best_ctas)) {
+      best = items;
+      best_ctas = ncl * c;
+      pl.csize = c;
+      pl.ncl = ncl;
+      pl.tg = T;
+      pl.grid = ncl * c;
+      pl.yacc_bytes = (uint32_t)inbox;
+    }
+  }
+  if (pl.nch <= sm_count) {
+    const int cpc = std::min(pl.tiles, sm_count / pl.nch);
+    if (2 * ((int64_t)((pl.tiles + cpc - 1) / cpc) + 3) < best) {
+      pl.tile_major = false;
+      pl.csize = 1;
+      pl.cpc = cpc;
+      pl.grid = cpc * pl.nch;
+      pl.tg = 1;
+      pl.yacc_bytes = 0;
+      pl.partial_floats = (size_t)pl.nch * M * pl.tiles * kTile;
+    }
   }
   return pl;
 }
@@ -849,57 +1020,9 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
     p.op_d[st] = (uint32_t)(rg * dp.nm);
     if ((st * 32) % (G * w.bs) != 0) p.acc_mask |= 1u << st;
   }
-  uint32_t yacc_bytes = pl.tile_major ? (uint32_t)(p.tg * M * kTile * 4) : 0;
-  int grid = pl.grid;
-  p.cluster = 0;
-  static int max_clusters[64][9];  // per device and cluster size, 0 = not yet queried
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static unsigned long long configured = 0;
-  if (!(configured & (1ull << (dev & 63)))) {
-    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kSmemLimit));
-    configured |= 1ull << (dev & 63);
-  }
-  if (!pl.tile_major && pl.nch >= 2 && pl.nch <= 8) {
-    // A cluster per tile set, as many as fit at once (a cluster waiting for
-    // a second wave would cost more than the separate reduction it saves;
-    // at one CTA per SM, 15 clusters of 8 fit on 148 SMs).
-    int& mc = max_clusters[dev & 63][pl.nch];
-    if (mc == 0) {
-      cudaLaunchConfig_t qc = {};
-      qc.gridDim = dim3((unsigned)pl.grid);
-      qc.blockDim = dim3(kThreadsTC);
-      qc.dynamicSmemBytes = kSmemLimit;
-      cudaLaunchAttribute qa[1];
-      qa[0].id = cudaLaunchAttributeClusterDimension;
-      qa[0].val.clusterDim.x = (unsigned)pl.nch;
-      qa[0].val.clusterDim.y = 1;
-      qa[0].val.clusterDim.z = 1;
-      qc.attrs = qa;
-      qc.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<M>, &qc) != cudaSuccess) {
-        cudaGetLastError();
-        n = 0;
-      }
-      mc = n > 0 ? n : -1;
-    }
-    const int cpc = std::min(pl.tiles, mc);
-    const int ntile_max = mc > 0 ? (pl.tiles + cpc - 1) / cpc : 0;
-    const uint32_t cbytes = (uint32_t)(ntile_max * M * kTile * 4);
-    const size_t cfixed = 1024 + 2 * kXBufBytes + cbytes + 1024;
-    // worth it while its busiest CTA takes at most one more item than with
-    // the separate reduction (whose kernel boundary costs about three)
-    const int items_c = ntile_max, items_s = (pl.tiles + pl.cpc - 1) / pl.cpc;
-    if (mc > 0 && items_c <= items_s + 1 &&
-        (kSmemLimit - std::min(kSmemLimit, cfixed)) / p.stage_bytes >= 2) {
-      p.cluster = 1;
-      p.cpc = cpc;
-      grid = cpc * pl.nch;
-      yacc_bytes = cbytes;
-    }
-  }
+  ORTC_CHECK(configure_m<M>() == ORT_CUDA_OK, ORT_CUDA_ERR_CUDA, "tc gemv: configure");
+  const uint32_t yacc_bytes = pl.yacc_bytes;
+  const int grid = pl.grid;
   p.yacc_bytes = yacc_bytes;
   const size_t fixed = 1024 + 2 * kXBufBytes + yacc_bytes + 1024;
   int nbst = (int)((kSmemLimit - fixed) / p.stage_bytes);
@@ -920,11 +1043,11 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = p.cluster ? (unsigned)pl.nch : 1;
+  attr[1].val.clusterDim.x = (unsigned)pl.csize;
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = p.cluster ? 2 : 1;
+  cfg.numAttrs = pl.csize > 1 ? 2 : 1;
   ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p));
   return ORT_CUDA_OK;
 }
@@ -935,7 +1058,9 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
 int prepare_nbits_tc(Weight& w) {
   w.tc_ok = false;
   const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
-  if (w.bs < kMinBs || w.bs > kChunkK || col_bytes % 16 != 0 || w.nl == 0) return ORT_CUDA_OK;
+  if (w.bs < kMinBs || w.bs > kChunkK || (w.bs & (w.bs - 1)) != 0 || col_bytes % 16 != 0 ||
+      w.nl == 0)
+    return ORT_CUDA_OK;
   const int bpi = kChunkK / w.bs;
   int rc = encode_tma_2d(&w.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes,
                          (uint64_t)w.nl, (uint64_t)col_bytes, 128, kTile,
@@ -962,15 +1087,15 @@ bool tc_gemv_ok(const Weight& w, int64_t M) {
   return d_plan(M, w.bs).nd > 0;
 }
 
-size_t tc_gemv_partial_floats(int64_t K, int64_t nl, int64_t M, int sm_count) {
-  return make_plan(K, nl, M, sm_count).partial_floats;
+size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count) {
+  return make_plan(w, M, sm_count).partial_floats;
 }
 
 int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
                    float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
                    const YSel* ysel) {
   if (w.nl == 0) return ORT_CUDA_OK;
-  const Plan pl = make_plan(w.K, w.nl, M, sm_count);
+  const Plan pl = make_plan(w, M, sm_count);
   TcParams p;
   p.A = A;
   p.Y = Y;
@@ -979,10 +1104,13 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   p.N = (int)w.nl;
   p.K = (int)w.K;
   p.bs = w.bs;
+  p.bs_log2 = 0;
+  while ((1 << p.bs_log2) < w.bs) p.bs_log2++;
   p.nch = pl.nch;
   p.tiles = pl.tiles;
   p.tile_major = pl.tile_major ? 1 : 0;
-  p.grid_tiles = pl.grid;
+  p.csize = pl.csize;
+  p.ncl = pl.ncl;
   p.tg = pl.tg;
   p.cpc = pl.cpc;
   p.part = pl.tile_major ? nullptr : partials;
@@ -995,7 +1123,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   p.s_off = kPackedBytes;
   p.z_off = kPackedBytes + (uint32_t)p.bpi * kTile * 4;
   const uint32_t zbytes = p.has_zp ? (uint32_t)z_rows * kTile : 0;
-  p.stage_bytes = (p.z_off + zbytes + 1023) & ~1023u;
+  p.stage_bytes = tc_stage_bytes(w);
   p.stage_tx = kPackedBytes + (uint32_t)p.bpi * kTile * 4 + zbytes;
   int rc;
   switch (M) {
@@ -1011,7 +1139,7 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
   }
   if (rc) return rc;
   (*launches)++;
-  if (!pl.tile_major && !p.cluster) {
+  if (!pl.tile_major) {
     const int64_t total = M * w.nl;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)std::min<int64_t>((total + 127) / 128, (int64_t)sm_count * 4));

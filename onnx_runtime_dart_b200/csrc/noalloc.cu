@@ -69,7 +69,7 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
              "no-allocation MatMulNBits takes 1 <= M <= 4, got M=" + std::to_string(M));
   ORTC_CHECK(tc_gemv_ok(w, M), ORT_CUDA_ERR_UNSUPPORTED,
              "no-allocation MatMulNBits needs 32 <= block_size <= 512");
-  const size_t pf = tc_gemv_partial_floats(w.K, w.nl, M, s->sm_count);
+  const size_t pf = tc_gemv_partial_floats(w, M, s->sm_count);
   ORTC_CHECK(pf <= kNoAllocPartialFloats, ORT_CUDA_ERR_INVALID_ARG,
              "no-allocation MatMulNBits: this shape needs " + std::to_string(pf) +
                  " partial floats; the static scratch holds " +

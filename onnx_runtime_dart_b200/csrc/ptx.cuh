@@ -179,6 +179,45 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// The cluster barrier in two halves: every thread arrives once its CTA's
+// mbarriers are initialised (after fence_mbarrier_init) and waits only
+// before its first access to another CTA's shared memory (or before exit).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+// Arrives on an mbarrier of another CTA of the cluster (address from
+// dsmem_addr) without ordering of its own: preceded by fence_acq_rel_cluster
+// it publishes the writes ordered before that fence.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+// Bounded wait on a local mbarrier that other CTAs of the cluster arrive
+// on; its completion acquires their released writes.  False on timeout.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+}
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) *reinterpret_cast<volatile int*>(err) = code;

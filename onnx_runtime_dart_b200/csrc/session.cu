@@ -872,7 +872,7 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
                   if (tc_gemv_ok(w, M)) {
-                    int rc = ensure_kscratch(s, tc_gemv_partial_floats(w.K, w.nl, M, s->sm_count) * 4);
+                    int rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count) * 4);
                     if (rc) return rc;
                     YSel ys;
                     if (s->xsel_offer) {

@@ -453,3 +453,51 @@ def test_tile_major_back_to_back(K, N, M):
         assert max_rel(ref, out[0]) <= EXACT_TOL
     finally:
         s.close()
+
+
+def test_opcase_single_op_timer(capsys):
+    """The single-op timing utility runs both decode and prefill cases and
+    reads the session's error word after its timed launches."""
+    import json
+    from onnx_runtime_dart_b200 import opcase
+    for argv in (["--k", "1024", "--n", "2048", "--m", "1"],
+                 ["--k", "1024", "--n", "1024", "--m", "256", "--mode", "mma_f16"]):
+        opcase.main(argv + ["--reps", "2", "--warmup", "1"])
+        line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert line["us_per_launch"] > 0 and line["m"] == int(argv[5])
+
+
+@pytest.mark.parametrize("K,N,M,bs,zp", [
+    (4096, 6144, 1, 128, True),     # 48 tiles x 8 chunks
+    (4096, 4096, 2, 64, False),     # 32 tiles
+    (14336, 4096, 1, 128, True),    # 28 chunks over a cluster
+    (14336, 512, 3, 32, True),      # 4 tiles, 28 chunks, bs 32
+    (4096, 28672, 4, 256, True),    # 224 tiles
+    (2560, 3000, 8, 128, False),    # 5 chunks, ragged last tile
+    (1536, 16032, 5, 128, True),    # 3 chunks, 126 tiles
+])
+def test_cluster_plans_parity_and_slice_invariance(sess, K, N, M, bs, zp):
+    """Shapes whose plans share tile sets across clusters of 2-8 CTAs (chunk
+    ranges per rank, partials summed in the owning CTA's shared memory).
+    Results match the oracle, and the first 128 columns uploaded alone (a
+    different plan) give the same bits."""
+    rng = np.random.default_rng(K * 7 + N + M)
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=zp)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("cl", B, s, z, k=K, n=N, block_size=bs)
+    y = sess.matmul_nbits("cl", A)
+    ref = O.matmul_nbits(A, B, s, z, K, N, 4, bs, threads=8)
+    assert max_rel(ref, y) <= EXACT_TOL
+    nb = K // bs if K % bs == 0 else K // bs + 1
+    n1 = 128
+    zs = None
+    if zp:
+        zv = np.stack([z & 0xF, z >> 4], 1).ravel()[:N * nb].reshape(N, nb)[:n1].ravel()
+        if zv.size % 2:
+            zv = np.append(zv, 0)
+        zs = (zv[0::2] | (zv[1::2] << 4)).astype(np.uint8)
+    sess.upload_nbits("cl1", B[:n1], s.reshape(N, nb)[:n1].ravel(), zs, k=K, n=n1, block_size=bs)
+    y1 = sess.matmul_nbits("cl1", A)
+    assert np.array_equal(y1, y[:, :n1])
+    sess.drop_weight("cl")
+    sess.drop_weight("cl1")

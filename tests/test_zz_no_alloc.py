@@ -3,7 +3,8 @@
 Some hosts cannot call cudaMalloc once they are running (a device-memory
 budget fixed at start-up, memory owned by another runtime's allocator, or a
 latency path that cannot take cudaMalloc's implicit device synchronisation).
-This entry point keeps its split-K scratch in a static device array of the
+This entry point keeps its split-K scratch (needed by the shapes whose
+cluster plan does not fit in shared memory) in a static device array of the
 library.  The test calls it through the C ABI on device buffers and checks
 it against the regular entry point on two calls in a row; the file is named
 to be collected last.
@@ -21,10 +22,12 @@ TOL = 1e-5  # exact-mode bar used by every GPU parity test
 
 
 @pytest.mark.parametrize("K,N,bs,zp,M", [
-    (4096, 3000, 128, True, 1),     # split-K: chunk partials in the static array
+    (4096, 3000, 128, True, 1),     # cluster plan: no scratch needed
     (14336, 1024, 128, True, 4),    # 28 chunks, M = 4
     (512, 777, 32, False, 2),       # single chunk: no scratch needed
     (2048, 128256 // 2, 128, True, 1),  # many tiles: no scratch needed
+    (40960, 4096, 128, True, 3),    # cluster inbox too large: split-K, partials
+                                    # in the static array
 ])
 def test_noalloc_matches_regular_entry_point(K, N, bs, zp, M):
     from onnx_runtime_dart_b200 import CudaSession, DeviceTensor, _lib
