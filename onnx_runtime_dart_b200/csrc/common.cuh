@@ -63,6 +63,8 @@ struct Weight {
   int64_t w16_rows = 0, w16_k = 0;
   int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
   uint32_t* sz16 = nullptr;  // nbits f16 MMA: per-(blk,col) {1024 + z, scale * 2^-col_exp} as fp16
+  // decode GEMV: the plan (candidate index) timing chose for each M in 1..8
+  int8_t gemv_plan[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
 };
 
 // ---- device layout of a MatMulNBits weight ---------------------------------
@@ -182,13 +184,24 @@ int encode_tma_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 
 // Decode GEMV on tensor cores, exact mode: Y[M, ldy] (columns [0, nl)) =
 // A[M, K] . dequant(W) for M <= 8 (tc_gemv_ok).  `partials` holds
-// tc_gemv_partial_floats() floats (no initial value needed).
+// tc_gemv_partial_floats(.., plan) floats (no initial value needed).
 int prepare_nbits_tc(Weight& w);
 bool tc_gemv_ok(const Weight& w, int64_t M);
-size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count);
-int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
+// The work plan a call uses: the one tune_tc_gemv chose for (w, M) when its
+// partial sums fit in max_partial_floats, else the heuristic's; -1 if
+// neither fits.
+int tc_gemv_plan(const Weight& w, int64_t M, int sm_count,
+                 size_t max_partial_floats = (size_t)-1);
+// Partial-sum floats of plan `plan` (-1: the most any candidate needs).
+size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count, int plan);
+int launch_tc_gemv(const Weight& w, int plan, const float* A, int64_t M, float* Y, int64_t ldy,
                    float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
                    const YSel* ysel = nullptr);
+// Times every candidate plan on this call's operands and records the
+// fastest in w.gemv_plan[M] (launches not counted; `partials` holds
+// tc_gemv_partial_floats(w, M, sm, -1) floats).  Not while capturing.
+int tune_tc_gemv(Weight& w, const float* A, int64_t M, float* Y, int64_t ldy, float* partials,
+                 int* err, int sm_count, cudaStream_t st, const YSel* ysel);
 // General CUDA-core tiled GEMM over an nbits or dense weight (any M).
 // strict=true reproduces the reference's rounding bit for bit.
 int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, float* Y,

@@ -52,6 +52,8 @@
 // owns: N-sharded results are bitwise equal to 1-GPU results.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <vector>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -927,66 +929,76 @@ int max_clusters(int64_t M, int csize) {
 //    [r*nch/csize, (r+1)*nch/csize) and stores its partials into the shared
 //    memory of the CTA that sums the tile;
 //  - split-K: CTAs own one chunk of a tile set, a second kernel sums.
-// The plan whose busiest CTA costs least wins; ties go to more CTAs, then
-// to the earlier candidate.  Cost in items: a chunk of T tiles costs
-// max(T, 1.5), since the builder warp takes about 1.5 items' time for a
-// chunk's X and hides it only behind that chunk's items; split-K builds its
-// one chunk with eight warps and pays about three items for the kernel
-// boundary before its sum.  The cluster inbox must leave room for three
-// pipeline stages.
+// plan_candidates lists the feasible ones in that order (a cluster inbox
+// must leave room for three pipeline stages); which is fastest depends on
+// the shape and on DRAM locality, so the first eager call times them
+// (tune_tc_gemv) and the weight keeps the winner.  heuristic_plan is the
+// choice before that: the busiest CTA's cost in items, where a chunk of T
+// tiles costs max(T, 1.5) (the builder warp takes about 1.5 items' time
+// for a chunk's X and hides it only behind that chunk's items) and split-K
+// pays about three items for the boundary before its sum; ties go to more
+// CTAs, then to the earlier candidate.
 struct Plan {
   bool tile_major;
   int nch, tiles, grid, cpc, tg, csize, ncl;
   uint32_t yacc_bytes;
   size_t partial_floats;
+  int64_t cost2;  // heuristic cost in half items
 };
 
-Plan make_plan(const Weight& w, int64_t M, int sm_count) {
-  Plan pl = {};
-  pl.nch = (int)((w.K + kChunkK - 1) / kChunkK);
-  pl.tiles = (int)((w.nl + kTile - 1) / kTile);
+std::vector<Plan> plan_candidates(const Weight& w, int64_t M, int sm_count) {
+  std::vector<Plan> out;
+  Plan base = {};
+  base.nch = (int)((w.K + kChunkK - 1) / kChunkK);
+  base.tiles = (int)((w.nl + kTile - 1) / kTile);
   const size_t stage = tc_stage_bytes(w);
   const size_t tile_bytes = (size_t)M * kTile * 4;
-  pl.tile_major = true;
-  pl.csize = 1;
-  pl.ncl = std::min(pl.tiles, sm_count);
-  pl.tg = std::max<int>(1, (int)(32 / M));
-  pl.grid = pl.ncl;
-  pl.yacc_bytes = (uint32_t)(pl.tg * tile_bytes);
-  // costs in half items
   auto chunk_cost = [](int T) { return (int64_t)std::max(2 * T, 3); };
-  int64_t best = chunk_cost((pl.tiles + pl.ncl - 1) / pl.ncl) * pl.nch;
-  int best_ctas = pl.ncl;
-  for (int c = 2; c <= 8 && c <= pl.nch; c++) {
+  Plan tm = base;
+  tm.tile_major = true;
+  tm.csize = 1;
+  tm.ncl = std::min(base.tiles, sm_count);
+  tm.tg = std::max<int>(1, (int)(32 / M));
+  tm.grid = tm.ncl;
+  tm.yacc_bytes = (uint32_t)(tm.tg * tile_bytes);
+  tm.cost2 = chunk_cost((base.tiles + tm.ncl - 1) / tm.ncl) * base.nch;
+  out.push_back(tm);
+  for (int c = 2; c <= 8 && c <= base.nch; c++) {
     const int mc = max_clusters(M, c);
     if (mc <= 0) continue;
-    const int ncl = std::min(pl.tiles, mc), T = (pl.tiles + ncl - 1) / ncl;
-    const size_t inbox = (size_t)((T + c - 1) / c) * pl.nch * tile_bytes;
+    const int ncl = std::min(base.tiles, mc), T = (base.tiles + ncl - 1) / ncl;
+    const size_t inbox = (size_t)((T + c - 1) / c) * base.nch * tile_bytes;
     if (1024 + 2 * (size_t)kXBufBytes + inbox + 1024 + 3 * stage > kSmemLimit) continue;
-    const int64_t items = chunk_cost(T) * ((pl.nch + c - 1) / c);
-    if (items < best || (items == best && ncl * c > best_ctas)) {
-      best = items;
-      best_ctas = ncl * c;
-      pl.csize = c;
-      pl.ncl = ncl;
-      pl.tg = T;
-      pl.grid = ncl * c;
-      pl.yacc_bytes = (uint32_t)inbox;
-    }
+    Plan cl = base;
+    cl.tile_major = true;
+    cl.csize = c;
+    cl.ncl = ncl;
+    cl.tg = T;
+    cl.grid = ncl * c;
+    cl.yacc_bytes = (uint32_t)inbox;
+    cl.cost2 = chunk_cost(T) * ((base.nch + c - 1) / c);
+    out.push_back(cl);
   }
-  if (pl.nch <= sm_count) {
-    const int cpc = std::min(pl.tiles, sm_count / pl.nch);
-    if (2 * ((int64_t)((pl.tiles + cpc - 1) / cpc) + 3) < best) {
-      pl.tile_major = false;
-      pl.csize = 1;
-      pl.cpc = cpc;
-      pl.grid = cpc * pl.nch;
-      pl.tg = 1;
-      pl.yacc_bytes = 0;
-      pl.partial_floats = (size_t)pl.nch * M * pl.tiles * kTile;
-    }
+  if (base.nch <= sm_count) {
+    Plan sk = base;
+    sk.tile_major = false;
+    sk.csize = 1;
+    sk.cpc = std::min(base.tiles, sm_count / base.nch);
+    sk.grid = sk.cpc * base.nch;
+    sk.tg = 1;
+    sk.partial_floats = (size_t)base.nch * M * base.tiles * kTile;
+    sk.cost2 = 2 * ((int64_t)((base.tiles + sk.cpc - 1) / sk.cpc) + 3);
+    out.push_back(sk);
   }
-  return pl;
+  return out;
+}
+
+int heuristic_plan(const std::vector<Plan>& c) {
+  int best = 0;
+  for (int i = 1; i < (int)c.size(); i++)
+    if (c[i].cost2 < c[best].cost2 || (c[i].cost2 == c[best].cost2 && c[i].grid > c[best].grid))
+      best = i;
+  return best;
 }
 
 // TMEM layout of D for one item: regions of G blocks, NM columns each.  Two
@@ -1087,15 +1099,11 @@ bool tc_gemv_ok(const Weight& w, int64_t M) {
   return d_plan(M, w.bs).nd > 0;
 }
 
-size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count) {
-  return make_plan(w, M, sm_count).partial_floats;
-}
+namespace {
 
-int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t ldy,
-                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
-                   const YSel* ysel) {
-  if (w.nl == 0) return ORT_CUDA_OK;
-  const Plan pl = make_plan(w, M, sm_count);
+int launch_plan(const Weight& w, const Plan& pl, const float* A, int64_t M, float* Y,
+                int64_t ldy, float* partials, int* err, int sm_count, cudaStream_t st,
+                int64_t* launches, const YSel* ysel) {
   TcParams p;
   p.A = A;
   p.Y = Y;
@@ -1155,6 +1163,77 @@ int launch_tc_gemv(const Weight& w, const float* A, int64_t M, float* Y, int64_t
     (*launches)++;
   }
   return ORT_CUDA_OK;
+}
+
+}  // namespace
+
+int tc_gemv_plan(const Weight& w, int64_t M, int sm_count, size_t max_partial_floats) {
+  const std::vector<Plan> c = plan_candidates(w, M, sm_count);
+  const int t = (M >= 1 && M <= 8) ? w.gemv_plan[M] : -1;
+  if (t >= 0 && t < (int)c.size() && c[t].partial_floats <= max_partial_floats) return t;
+  const int h = heuristic_plan(c);
+  return c[h].partial_floats <= max_partial_floats ? h : -1;
+}
+
+size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count, int plan) {
+  const std::vector<Plan> c = plan_candidates(w, M, sm_count);
+  if (plan < 0) {
+    size_t mx = 0;
+    for (const Plan& q : c) mx = std::max(mx, q.partial_floats);
+    return mx;
+  }
+  return plan < (int)c.size() ? c[plan].partial_floats : 0;
+}
+
+int launch_tc_gemv(const Weight& w, int plan, const float* A, int64_t M, float* Y, int64_t ldy,
+                   float* partials, int* err, int sm_count, cudaStream_t st, int64_t* launches,
+                   const YSel* ysel) {
+  if (w.nl == 0) return ORT_CUDA_OK;
+  const std::vector<Plan> c = plan_candidates(w, M, sm_count);
+  ORTC_CHECK(plan >= 0 && plan < (int)c.size(), ORT_CUDA_ERR_INVALID_ARG, "tc gemv: bad plan");
+  return launch_plan(w, c[plan], A, M, Y, ldy, partials, err, sm_count, st, launches, ysel);
+}
+
+// Times every candidate plan on this call's operands (one warm launch, then
+// kTuneReps back to back between two events) and keeps the fastest in
+// w.gemv_plan[M].  All plans give identical bits, so the choice only moves
+// time.  `partials` holds tc_gemv_partial_floats(w, M, sm, -1) floats.
+int tune_tc_gemv(Weight& w, const float* A, int64_t M, float* Y, int64_t ldy, float* partials,
+                 int* err, int sm_count, cudaStream_t st, const YSel* ysel) {
+  constexpr int kTuneReps = 3;
+  if (M < 1 || M > 8 || w.nl == 0) return ORT_CUDA_OK;
+  const std::vector<Plan> c = plan_candidates(w, M, sm_count);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  ORTC_CUDA(cudaEventCreate(&e0));
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: cudaEventCreate");
+  }
+  int best = -1, rc = ORT_CUDA_OK;
+  float best_ms = 0.0f;
+  int64_t uncounted = 0;
+  for (int i = 0; i < (int)c.size() && rc == ORT_CUDA_OK; i++) {
+    rc = launch_plan(w, c[i], A, M, Y, ldy, partials, err, sm_count, st, &uncounted, ysel);
+    if (rc) break;
+    if (cudaEventRecord(e0, st) != cudaSuccess) { rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: record"); break; }
+    for (int r = 0; r < kTuneReps && rc == ORT_CUDA_OK; r++)
+      rc = launch_plan(w, c[i], A, M, Y, ldy, partials, err, sm_count, st, &uncounted, ysel);
+    if (rc) break;
+    float ms = 0.0f;
+    if (cudaEventRecord(e1, st) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) {
+      rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: timing");
+      break;
+    }
+    if (best < 0 || ms < best_ms) {
+      best = i;
+      best_ms = ms;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc == ORT_CUDA_OK && best >= 0) w.gemv_plan[M] = (int8_t)best;
+  return rc;
 }
 
 }  // namespace ortc

@@ -69,11 +69,16 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
              "no-allocation MatMulNBits takes 1 <= M <= 4, got M=" + std::to_string(M));
   ORTC_CHECK(tc_gemv_ok(w, M), ORT_CUDA_ERR_UNSUPPORTED,
              "no-allocation MatMulNBits needs 32 <= block_size <= 512");
-  const size_t pf = tc_gemv_partial_floats(w, M, s->sm_count);
-  ORTC_CHECK(pf <= kNoAllocPartialFloats, ORT_CUDA_ERR_INVALID_ARG,
-             "no-allocation MatMulNBits: this shape needs " + std::to_string(pf) +
-                 " partial floats; the static scratch holds " +
-                 std::to_string(kNoAllocPartialFloats));
+  // the plan the regular entry point would use, unless its partial sums do
+  // not fit the static scratch (then the heuristic's, if that fits)
+  const int plan = tc_gemv_plan(w, M, s->sm_count, kNoAllocPartialFloats);
+  if (plan < 0) {
+    const size_t pf = tc_gemv_partial_floats(w, M, s->sm_count, tc_gemv_plan(w, M, s->sm_count));
+    ORTC_CHECK(false, ORT_CUDA_ERR_INVALID_ARG,
+               "no-allocation MatMulNBits: this shape needs " + std::to_string(pf) +
+                   " partial floats; the static scratch holds " +
+                   std::to_string(kNoAllocPartialFloats));
+  }
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != s->device) ORTC_CUDA(cudaSetDevice(s->device));
@@ -82,8 +87,8 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
   // starting value (every partial is written before it is read).
   int rc = slot_for(s->device, &sl);
   if (rc == ORT_CUDA_OK)
-    rc = launch_tc_gemv(w, A, M, Y, w.nl, sl->partials, s->err_dev, s->sm_count, s->stream,
-                        &s->launches, nullptr);
+    rc = launch_tc_gemv(w, plan, A, M, Y, w.nl, sl->partials, s->err_dev, s->sm_count,
+                        s->stream, &s->launches, nullptr);
   if (prev >= 0 && prev != s->device) cudaSetDevice(prev);
   return rc;
 }

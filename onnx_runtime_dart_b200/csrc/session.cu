@@ -7,6 +7,7 @@
 // onnx_graph.dart:51-56) and its column-split worker pool
 // (lib/src/parallel_pool.dart:108-205), which becomes NCCL N-sharding.
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -63,6 +64,17 @@ int ensure_pinned(ort_cuda_session* s, size_t bytes) {
   ORTC_CUDA(cudaMallocHost(&s->pinned, want));
   s->pinned_bytes = want;
   return ORT_CUDA_OK;
+}
+
+// The decode GEMV times its candidate plans on a weight's first eager call
+// for each M (once; results never depend on the plan).
+// ORT_CUDA_GEMV_TUNE=0 keeps the heuristic choice instead.
+static bool gemv_tuning_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("ORT_CUDA_GEMV_TUNE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int ensure_kscratch(ort_cuda_session* s, size_t bytes) {
@@ -872,16 +884,25 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
                   if (tc_gemv_ok(w, M)) {
-                    int rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count) * 4);
-                    if (rc) return rc;
                     YSel ys;
                     if (s->xsel_offer) {
                       ys = p2p_ysel(s);
                       s->xsel_taken = true;
                     }
-                    return launch_tc_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
-                                          s->sm_count, s->stream, &s->launches,
-                                          s->xsel_offer ? &ys : nullptr);
+                    const YSel* ysp = s->xsel_offer ? &ys : nullptr;
+                    int rc;
+                    if (w.gemv_plan[M] < 0 && !s->capturing && gemv_tuning_enabled()) {
+                      rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count, -1) * 4);
+                      if (rc) return rc;
+                      rc = tune_tc_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
+                                        s->sm_count, s->stream, ysp);
+                      if (rc) return rc;
+                    }
+                    const int plan = tc_gemv_plan(w, M, s->sm_count);
+                    rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count, plan) * 4);
+                    if (rc) return rc;
+                    return launch_tc_gemv(w, plan, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
+                                          s->sm_count, s->stream, &s->launches, ysp);
                   }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K))
