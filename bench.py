@@ -7,7 +7,14 @@ down 14336->4096, lm_head 4096->128256 — bits 4, block 128, fp16 scales,
 packed uint4 zero points, random-init weights (seed 5), A ~ N(0,1).
 Weights are uploaded once; activations stay on the device.  With N GPUs
 the output columns of every weight are sharded over the ranks and Y is
-all-gathered over NCCL inside each op (strong scaling: total work fixed).
+all-gathered inside each op, over peer memory (NCCL where peers cannot be
+mapped) (strong scaling: total work fixed).  Each op's work plan is timed
+and chosen on its first (warm-up) call.
+
+Timing: the K steps are recorded as one CUDA graph and replayed once
+between two events; `roofline` times the lm_head op with an event pair
+around it in a second replay of the same K steps (events between kernels
+end their programmatic overlap, so they stay out of the timed replay).
 
 `value` = whole-job algorithmic bytes per step / device time per step
 (max over ranks), GB/s.  Algorithmic bytes per op = packed B + scales +
@@ -56,6 +63,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="time op-by-op calls instead of a CUDA graph of the timed steps")
+    ap.add_argument("--save-plans", default=None,
+                    help="write the decode-GEMV plans chosen in warm-up to this JSON file "
+                         "(per rank: .rankR appended when N > 1)")
+    ap.add_argument("--load-plans", default=None,
+                    help="use the plans of a --save-plans file instead of timing them")
     return ap.parse_args()
 
 
@@ -233,6 +245,10 @@ def main():
         B, s, z = weights[p.name]
         sess.upload_nbits(p.name, B, s, z, k=p.K, n=p.N, block_size=BS)
     M = 1
+    suffix = f".rank{rank}" if world > 1 else ""
+    if args.load_plans:
+        for name, plan in json.load(open(args.load_plans + suffix)).items():
+            sess.set_gemv_plan(name, M, int(plan))
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev).manual_seed(SEED)
     A = {K: torch.randn(M, K, device=dev, generator=gen) for K in sorted({p.K for p in projs})}
@@ -276,27 +292,37 @@ def main():
     for _ in range(args.warmup):
         step()
     barrier()
+    plans = {p.name: sess.gemv_plan(p.name, M) for p in projs}
+    if args.save_plans:
+        with open(args.save_plans + suffix, "w") as f:
+            json.dump(plans, f)
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gid = None
+    # Two replays of the same K steps.  The timed one has no events inside
+    # (an event between two kernels ends their programmatic overlap); the
+    # second records an event pair around each step's lm_head GEMV for the
+    # roofline.  Eager mode runs the same two passes op by op.
+    gid = gid_ev = None
     if not args.eager:
-        # the K timed steps recorded once (with their lm_head event pairs)
-        # and replayed with one launch; one untimed replay first
         for a, b in kev:  # torch creates its events on first use
             a.record(stream)
             b.record(stream)
         barrier()
         sess.graph_begin()
+        for i in range(args.steps):
+            step()
+        gid = sess.graph_end()
+        sess.graph_begin()
         capturing[0] = True
         for i in range(args.steps):
             step(kev[i])
         capturing[0] = False
-        gid = sess.graph_end()
-        sess.graph_launch(gid)
+        gid_ev = sess.graph_end()
+        sess.graph_launch(gid)  # one untimed replay
         barrier()
     launches0 = sess.launch_count()
     e0.record(stream)
@@ -304,12 +330,19 @@ def main():
         sess.graph_launch(gid)
     else:
         for i in range(args.steps):
-            step(kev[i])
+            step()
     e1.record(stream)
     barrier()
     launches = sess.launch_count() - launches0
-    if gid is not None:
-        sess.graph_drop(gid)
+    if gid_ev is not None:
+        sess.graph_launch(gid_ev)
+    else:
+        for i in range(args.steps):
+            step(kev[i])
+    barrier()
+    for g in (gid, gid_ev):
+        if g is not None:
+            sess.graph_drop(g)
     sess.sync()  # raises if any kernel of the timed steps reported an error
     clk = clocks.stop()
     ms_step = e0.elapsed_time(e1) / args.steps
@@ -405,13 +438,17 @@ def main():
                                    "4096x4096, gate_up 4096x28672, down 14336x4096, lm_head "
                                    "4096x128256; bits 4, block 128, fp16 scales, packed zp",
                        "mode": args.mode,
+                       "gemv_plans": plans,
                        "launch": ("op-by-op calls" if args.eager else
                                   "CUDA graph of the timed steps, one replay"),
                        "parallelism": f"N-sharded x{world}" + (
                            " + all-gather of Y over peer memory (NCCL where peers cannot "
                            "be mapped)" if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 387 MB of weights per step)"},
-            "roofline": {"bound": "hbm", "kernel": f"int4 GEMV ({big.name})",
+            "roofline": {"bound": "hbm",
+                         "kernel": f"int4 GEMV op ({big.name}: the GEMV launch, plus the "
+                                   "chunk-sum launch when its tuned plan is split-K)",
+                         "timing": "event pair around the op in a second replay of the steps",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic, "bytes_per_launch": big_bytes},

@@ -231,6 +231,17 @@ ORT_CUDA_API int ort_cuda_graph_end(ort_cuda_session* s, int* graph_id);
 ORT_CUDA_API int ort_cuda_graph_launch(ort_cuda_session* s, int graph_id);
 ORT_CUDA_API int ort_cuda_graph_drop(ort_cuda_session* s, int graph_id);
 
+/* Decode-GEMV work plan of MatMulNBits weight `name` for M rows (1..8):
+ * the candidate decomposition the library timed and chose on the weight's
+ * first call with that M, -1 while none is chosen.  Setting a plan (or -1)
+ * replaces that choice, e.g. to reuse choices saved from an earlier
+ * session of the same shapes on the same device instead of timing again;
+ * every plan gives identical results.  ORT_CUDA_ERR_INVALID_ARG for a plan
+ * outside [-1, number of candidates).  No counterpart in the reference,
+ * whose one CPU kernel has no plans (lib/src/onnx_qlinear_ops.dart:114). */
+ORT_CUDA_API int ort_cuda_gemv_plan_get(ort_cuda_session* s, const char* name, int M, int* plan);
+ORT_CUDA_API int ort_cuda_gemv_plan_set(ort_cuda_session* s, const char* name, int M, int plan);
+
 /* Kernel launches issued by this session since it was opened (all of
  * them this library's own kernels; a graph launch counts the kernels it
  * holds). */

@@ -192,6 +192,8 @@ bool tc_gemv_ok(const Weight& w, int64_t M);
 // neither fits.
 int tc_gemv_plan(const Weight& w, int64_t M, int sm_count,
                  size_t max_partial_floats = (size_t)-1);
+// Number of candidate plans for (w, M) on this device.
+int tc_gemv_plan_count(const Weight& w, int64_t M, int sm_count);
 // Partial-sum floats of plan `plan` (-1: the most any candidate needs).
 size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count, int plan);
 int launch_tc_gemv(const Weight& w, int plan, const float* A, int64_t M, float* Y, int64_t ldy,

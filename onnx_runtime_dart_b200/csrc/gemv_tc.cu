@@ -1175,6 +1175,10 @@ int tc_gemv_plan(const Weight& w, int64_t M, int sm_count, size_t max_partial_fl
   return c[h].partial_floats <= max_partial_floats ? h : -1;
 }
 
+int tc_gemv_plan_count(const Weight& w, int64_t M, int sm_count) {
+  return (int)plan_candidates(w, M, sm_count).size();
+}
+
 size_t tc_gemv_partial_floats(const Weight& w, int64_t M, int sm_count, int plan) {
   const std::vector<Plan> c = plan_candidates(w, M, sm_count);
   if (plan < 0) {
@@ -1194,13 +1198,15 @@ int launch_tc_gemv(const Weight& w, int plan, const float* A, int64_t M, float* 
   return launch_plan(w, c[plan], A, M, Y, ldy, partials, err, sm_count, st, launches, ysel);
 }
 
-// Times every candidate plan on this call's operands (one warm launch, then
-// kTuneReps back to back between two events) and keeps the fastest in
-// w.gemv_plan[M].  All plans give identical bits, so the choice only moves
-// time.  `partials` holds tc_gemv_partial_floats(w, M, sm, -1) floats.
+// Times every candidate plan on this call's operands and keeps the fastest
+// in w.gemv_plan[M]: per candidate one warm launch, then kTuneReps back to
+// back between two events, best of kTuneRounds rounds (rounds interleave
+// the candidates, so a slow moment does not single one out).  All plans
+// give identical bits, so the choice only moves time.  `partials` holds
+// tc_gemv_partial_floats(w, M, sm, -1) floats.
 int tune_tc_gemv(Weight& w, const float* A, int64_t M, float* Y, int64_t ldy, float* partials,
                  int* err, int sm_count, cudaStream_t st, const YSel* ysel) {
-  constexpr int kTuneReps = 3;
+  constexpr int kTuneReps = 4, kTuneRounds = 2;
   if (M < 1 || M > 8 || w.nl == 0) return ORT_CUDA_OK;
   const std::vector<Plan> c = plan_candidates(w, M, sm_count);
   cudaEvent_t e0 = nullptr, e1 = nullptr;
@@ -1209,27 +1215,32 @@ int tune_tc_gemv(Weight& w, const float* A, int64_t M, float* Y, int64_t ldy, fl
     cudaEventDestroy(e0);
     return fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: cudaEventCreate");
   }
-  int best = -1, rc = ORT_CUDA_OK;
-  float best_ms = 0.0f;
+  std::vector<float> ms_best(c.size(), -1.0f);
+  int rc = ORT_CUDA_OK;
   int64_t uncounted = 0;
-  for (int i = 0; i < (int)c.size() && rc == ORT_CUDA_OK; i++) {
-    rc = launch_plan(w, c[i], A, M, Y, ldy, partials, err, sm_count, st, &uncounted, ysel);
-    if (rc) break;
-    if (cudaEventRecord(e0, st) != cudaSuccess) { rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: record"); break; }
-    for (int r = 0; r < kTuneReps && rc == ORT_CUDA_OK; r++)
+  for (int round = 0; round < kTuneRounds && rc == ORT_CUDA_OK; round++) {
+    for (int i = 0; i < (int)c.size() && rc == ORT_CUDA_OK; i++) {
       rc = launch_plan(w, c[i], A, M, Y, ldy, partials, err, sm_count, st, &uncounted, ysel);
-    if (rc) break;
-    float ms = 0.0f;
-    if (cudaEventRecord(e1, st) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess ||
-        cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) {
-      rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: timing");
-      break;
-    }
-    if (best < 0 || ms < best_ms) {
-      best = i;
-      best_ms = ms;
+      if (rc) break;
+      if (cudaEventRecord(e0, st) != cudaSuccess) {
+        rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: record");
+        break;
+      }
+      for (int r = 0; r < kTuneReps && rc == ORT_CUDA_OK; r++)
+        rc = launch_plan(w, c[i], A, M, Y, ldy, partials, err, sm_count, st, &uncounted, ysel);
+      if (rc) break;
+      float ms = 0.0f;
+      if (cudaEventRecord(e1, st) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess ||
+          cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) {
+        rc = fail(ORT_CUDA_ERR_CUDA, "tc gemv tune: timing");
+        break;
+      }
+      if (ms_best[i] < 0.0f || ms < ms_best[i]) ms_best[i] = ms;
     }
   }
+  int best = -1;
+  for (int i = 0; i < (int)c.size(); i++)
+    if (ms_best[i] >= 0.0f && (best < 0 || ms_best[i] < ms_best[best])) best = i;
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   if (rc == ORT_CUDA_OK && best >= 0) w.gemv_plan[M] = (int8_t)best;

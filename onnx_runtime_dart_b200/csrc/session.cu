@@ -715,6 +715,33 @@ ORT_CUDA_API int ort_cuda_drop_weight(ort_cuda_session* s, const char* name) {
   return ORT_CUDA_OK;
 }
 
+ORT_CUDA_API int ort_cuda_gemv_plan_get(ort_cuda_session* s, const char* name, int M, int* plan) {
+  ORTC_CHECK(s && name && plan, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 1 && M <= 8, ORT_CUDA_ERR_INVALID_ARG, "M must be in 1..8");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  *plan = it->second.gemv_plan[M];
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_gemv_plan_set(ort_cuda_session* s, const char* name, int M, int plan) {
+  ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 1 && M <= 8, ORT_CUDA_ERR_INVALID_ARG, "M must be in 1..8");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  Weight& w = it->second;
+  ORTC_CHECK(w.kind == W_NBITS && tc_gemv_ok(w, M), ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + name + "' has no decode-GEMV plans for this M");
+  DeviceGuard g(s->device);
+  const int n = tc_gemv_plan_count(w, M, s->sm_count);
+  ORTC_CHECK(plan >= -1 && plan < n, ORT_CUDA_ERR_INVALID_ARG,
+             "plan " + std::to_string(plan) + " outside [-1, " + std::to_string(n) + ")");
+  w.gemv_plan[M] = (int8_t)plan;
+  return ORT_CUDA_OK;
+}
+
 ORT_CUDA_API int ort_cuda_weight_shape(ort_cuda_session* s, const char* name, int64_t* K,
                                        int64_t* N) {
   ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");

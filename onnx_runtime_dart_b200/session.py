@@ -143,6 +143,18 @@ class CudaSession:
     def sync(self) -> None:
         check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")
 
+    def gemv_plan(self, name: str, m: int) -> int:
+        """Decode-GEMV plan chosen for weight `name` at M=m (-1: none yet)."""
+        p = ctypes.c_int()
+        check(_lib.load().ort_cuda_gemv_plan_get(self.handle, name.encode(), m, ctypes.byref(p)),
+              "ort_cuda_gemv_plan_get")
+        return p.value
+
+    def set_gemv_plan(self, name: str, m: int, plan: int) -> None:
+        """Sets (or with -1 clears) the decode-GEMV plan of `name` at M=m."""
+        check(_lib.load().ort_cuda_gemv_plan_set(self.handle, name.encode(), m, plan),
+              "ort_cuda_gemv_plan_set")
+
     def launch_count(self) -> int:
         c = ctypes.c_int64()
         check(_lib.load().ort_cuda_launch_count(self.handle, ctypes.byref(c)))

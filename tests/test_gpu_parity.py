@@ -501,3 +501,36 @@ def test_cluster_plans_parity_and_slice_invariance(sess, K, N, M, bs, zp):
     assert np.array_equal(y1, y[:, :n1])
     sess.drop_weight("cl")
     sess.drop_weight("cl1")
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 6144, 1), (14336, 1024, 2), (1536, 5000, 4)])
+def test_every_gemv_plan_gives_the_same_bits(sess, K, N, M):
+    """Every candidate decomposition of the decode GEMV (tile-major, the
+    cluster sizes that fit, split-K), set through ort_cuda_gemv_plan_set,
+    gives bit-identical results that match the oracle; plans outside the
+    candidate range are refused and -1 restores the automatic choice."""
+    rng = np.random.default_rng(K + N + M)
+    B, s, z = O.make_nbits_weight(rng, K, N, 128, zero_points=True)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("pl", B, s, z, k=K, n=N, block_size=128)
+    ref = O.matmul_nbits(A, B, s, z, K, N, 4, 128, threads=8)
+    first = None
+    plan = 0
+    while True:
+        try:
+            sess.set_gemv_plan("pl", M, plan)
+        except ValueError:  # ORT_CUDA_ERR_INVALID_ARG: past the last candidate
+            break
+        assert sess.gemv_plan("pl", M) == plan
+        y = sess.matmul_nbits("pl", A)
+        if first is None:
+            first = y
+            assert max_rel(ref, y) <= EXACT_TOL
+        assert np.array_equal(y, first), f"plan {plan} differs"
+        plan += 1
+    assert plan >= 2  # tile-major and at least one other candidate
+    sess.set_gemv_plan("pl", M, -1)
+    assert sess.gemv_plan("pl", M) == -1
+    assert np.array_equal(sess.matmul_nbits("pl", A), first)
+    assert sess.gemv_plan("pl", M) >= 0  # timed and chosen on that call
+    sess.drop_weight("pl")
