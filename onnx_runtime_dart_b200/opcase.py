@@ -28,6 +28,9 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--plan", type=int, default=None,
+                    help="decode-GEMV plan to use (ort_cuda_gemv_plan_set) instead of timing "
+                         "the candidates on the first call; M <= 8 in the exact mode")
     args = ap.parse_args(argv)
 
     import torch
@@ -43,6 +46,8 @@ def main(argv=None) -> None:
         B, sc, z = make_nbits_weight(rng, args.k, args.n, args.block_size, zero_points=True,
                                      scale_dtype=np.float16)
         s.upload_nbits("w", B, sc, z, k=args.k, n=args.n, block_size=args.block_size)
+        if args.plan is not None:
+            s.set_gemv_plan("w", args.m, args.plan)
         flags = _lib.flags_mode(_lib.MODES[args.mode])
         with torch.cuda.stream(st):
             gen = torch.Generator(device="cuda").manual_seed(args.seed)
@@ -59,8 +64,9 @@ def main(argv=None) -> None:
             st.synchronize()
         s.sync()
         us = e0.elapsed_time(e1) * 1000 / args.reps
+        plan = s.gemv_plan("w", args.m) if args.mode == "exact" and args.m <= 8 else None
         print(json.dumps({"op": "MatMulNBits", "k": args.k, "n": args.n, "m": args.m,
-                          "block_size": args.block_size, "mode": args.mode,
+                          "block_size": args.block_size, "mode": args.mode, "gemv_plan": plan,
                           "us_per_launch": us, "reps": args.reps,
                           "tflops": 2 * args.m * args.k * args.n / (us * 1e-6) / 1e12}))
     finally:
