@@ -48,6 +48,8 @@ struct Weight {
                              // word reordered (nbits_nibble below)
   float* scales = nullptr;   // [nb][s_pitch] fp32 (transposed: block-major)
   int64_t s_pitch = 0;       // >= nl, multiple of 4
+  uint16_t* scales16 = nullptr;  // the same as fp16 when uploaded as fp16 (the
+  int64_t s16_pitch = 0;         // decode GEMV streams these); pitch % 8 == 0
   uint8_t* zp = nullptr;     // [ceil(nb/2)][z_pitch] bytes: byte (b/2, n) holds
                              // blocks 2j (low nibble) and 2j+1 of column n
   int64_t z_pitch = 0;       // >= nl, multiple of 16

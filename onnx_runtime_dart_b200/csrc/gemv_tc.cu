@@ -119,6 +119,7 @@ struct TcParams {
   // thread does no integer division.
   uint32_t op_d[kItemStages];
   uint32_t acc_mask;
+  int s16;         // block scales streamed as fp16 (widened exactly in the epilogue)
   uint32_t stage_bytes, stage_tx, s_off, z_off, yacc_off;
 };
 
@@ -690,6 +691,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       for (int m = 0; m < M; m++) y[m] = 0.0f;
       const uint8_t* stg = Bs + bst * p.stage_bytes;
       const float* stile = reinterpret_cast<const float*>(stg + p.s_off);
+      const __half* stile16 = reinterpret_cast<const __half*>(stg + p.s_off);
       const float* xsum =
           reinterpret_cast<const float*>(Xs + ((nbuild - 1) & 1) * kXBufBytes + kXXsum);
       // zero points of the item's blocks for column nl: block b is nibble
@@ -714,7 +716,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int slot = 0; slot < G; slot++) {
           const int b = rg * G + slot;
           if (b < p.bpi) {
-            const float sc = stile[b * kTile + nl];
+            const float sc = p.s16 ? __half2float(stile16[b * kTile + nl]) : stile[b * kTile + nl];
             const float zf = (float)((uint32_t)(zbits >> (4 * b + zsh)) & 0xFu);
 #pragma unroll
             for (int m = 0; m < M; m++) {
@@ -853,10 +855,10 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
 }
 
 // Shared memory of one pipeline stage: the packed item, its block scales
-// (fp32) and its zero points.
+// (fp16 when they were uploaded as fp16, else fp32) and its zero points.
 uint32_t tc_stage_bytes(const Weight& w) {
   const int bpi = kChunkK / w.bs, z_rows = bpi >= 2 ? bpi / 2 : 1;
-  const uint32_t z_off = kPackedBytes + (uint32_t)bpi * kTile * 4;
+  const uint32_t z_off = kPackedBytes + (uint32_t)bpi * kTile * (w.scales16 ? 2 : 4);
   const uint32_t zbytes = w.has_zp ? (uint32_t)z_rows * kTile : 0;
   return (z_off + zbytes + 1023) & ~1023u;
 }
@@ -1078,9 +1080,14 @@ int prepare_nbits_tc(Weight& w) {
                          (uint64_t)w.nl, (uint64_t)col_bytes, 128, kTile,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_tma_2d(&w.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales, (uint64_t)w.nl,
-                     (uint64_t)w.nb, (uint64_t)w.s_pitch * 4, kTile, bpi,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (w.scales16)
+    rc = encode_tma_2d(&w.tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.scales16, (uint64_t)w.nl,
+                       (uint64_t)w.nb, (uint64_t)w.s16_pitch * 2, kTile, bpi,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    rc = encode_tma_2d(&w.tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales, (uint64_t)w.nl,
+                       (uint64_t)w.nb, (uint64_t)w.s_pitch * 4, kTile, bpi,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   if (w.has_zp) {
     rc = encode_tma_2d(&w.tmZ, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.zp, (uint64_t)w.nl,
@@ -1128,11 +1135,13 @@ int launch_plan(const Weight& w, const Plan& pl, const float* A, int64_t M, floa
   p.has_zp = w.has_zp ? 1 : 0;
   const int z_rows = p.bpi >= 2 ? p.bpi / 2 : 1;
   p.z_rows = z_rows;
+  p.s16 = w.scales16 ? 1 : 0;
+  const uint32_t sbytes = (uint32_t)p.bpi * kTile * (p.s16 ? 2 : 4);
   p.s_off = kPackedBytes;
-  p.z_off = kPackedBytes + (uint32_t)p.bpi * kTile * 4;
+  p.z_off = kPackedBytes + sbytes;
   const uint32_t zbytes = p.has_zp ? (uint32_t)z_rows * kTile : 0;
   p.stage_bytes = tc_stage_bytes(w);
-  p.stage_tx = kPackedBytes + (uint32_t)p.bpi * kTile * 4 + zbytes;
+  p.stage_tx = kPackedBytes + sbytes + zbytes;
   int rc;
   switch (M) {
     case 1: rc = launch_m<1>(w, p, pl, st); break;

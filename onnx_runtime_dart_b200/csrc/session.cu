@@ -119,7 +119,7 @@ bool is_pinned_host(const void* p) {
 }
 
 int free_weight(ortc::Weight& w) {
-  void* ptrs[] = {w.B, w.scales, w.zp, w.W, w.W16, w.col_exp, w.sz16};
+  void* ptrs[] = {w.B, w.scales, w.scales16, w.zp, w.W, w.W16, w.col_exp, w.sz16};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   w = ortc::Weight();
@@ -610,6 +610,18 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
     cudaFree(tmpS);
     if (tmpT) cudaFree(tmpT);
     if (rc) return cleanup(rc);
+    if (f16) {
+      // fp16 scales also block-major [nb][s16_pitch] as fp16: the decode
+      // GEMV streams these (half the bytes; widened exactly in its epilogue)
+      w.s16_pitch = (nl + 7) / 8 * 8;
+      std::vector<uint16_t> t((size_t)(nb * w.s16_pitch), 0);
+      const uint16_t* src = (const uint16_t*)scales + w.n0 * nb;
+      for (int64_t c = 0; c < nl; c++)
+        for (int64_t b = 0; b < nb; b++) t[(size_t)(b * w.s16_pitch + c)] = src[c * nb + b];
+      e = cudaMalloc(&w.scales16, t.size() * 2);
+      if (e == cudaSuccess) e = cudaMemcpy(w.scales16, t.data(), t.size() * 2, cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "fp16 scales"));
+    }
     if (zp) {
       // Zero points from either input layout (the reference's flat nibble
       // n*nb + blk, onnx_qlinear_ops.dart:135-137, or ORT's per-column
