@@ -14,7 +14,7 @@
 //
 // Persistent kernel, one CTA per SM, tiles of 128 (m) x 256 (n), 64-k stages:
 //   warp 0      TMA producer: A tile (128 x 64 fp16, 128-byte swizzle), the
-//               packed int4 tile (256 columns x 32 bytes) and the stage's
+//               packed int4 tile (256 columns x 32 bytes, 32-byte swizzle) and the stage's
 //               {1024 + z, scale'} table (fp16 pairs) into a 4-stage ring
 //   warps 2-9   converters: thread n owns weight column n of the tile; per
 //               8 weights two masks, four byte permutes (nibble | 0x6400 is
@@ -227,9 +227,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           break;
         }
         const uint8_t* st = raw + s * kRawBytes;
+        // the packed tile lands with the 32-byte swizzle (16-byte half h of
+        // column n at n*32 + ((h ^ bit 2 of n) << 4)): the 8 columns a
+        // quarter-warp reads then cover all 32 banks once
         const uint32_t qa = smem_u32(st + kABytes) + n * 32;
         const uint32_t* sz = reinterpret_cast<const uint32_t*>(st + kABytes + kQBytes);
-        const uint4 w0 = lds128(qa), w1 = lds128(qa + 16);
+        const uint32_t qsw = (uint32_t)((n >> 2) & 1) << 4;
+        const uint4 w0 = lds128(qa + qsw), w1 = lds128(qa + (16 ^ qsw));
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         const uint32_t cb = smem_u32(conv + c * kCBytes) + rowoff;
 #pragma unroll
@@ -342,7 +346,7 @@ int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_e
                          (uint64_t)K * 2, PBK, PBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_tma_2d(&tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes, (uint64_t)nl,
-                     (uint64_t)col_bytes, PBK / 2, PBN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                     (uint64_t)col_bytes, PBK / 2, PBN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   int bs_shift = 0;
   while ((1 << bs_shift) < w.bs) bs_shift++;
