@@ -922,26 +922,45 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if (mode == ORT_CUDA_MODE_STRICT)
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
+                  // tensor-core GEMV over rows [r, r + m): timed plan choice on
+                  // the first eager call for (w, m), then the launch
+                  auto gemv_rows = [&](const float* a, int64_t m, float* y,
+                                       const YSel* ysp) -> int {
+                    int rc;
+                    if (w.gemv_plan[m] < 0 && !s->capturing && gemv_tuning_enabled()) {
+                      rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, -1) * 4);
+                      if (rc) return rc;
+                      rc = tune_tc_gemv(w, a, m, y, ldy, (float*)s->kscratch, s->err_dev,
+                                        s->sm_count, s->stream, ysp);
+                      if (rc) return rc;
+                    }
+                    const int plan = tc_gemv_plan(w, m, s->sm_count);
+                    rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, plan) * 4);
+                    if (rc) return rc;
+                    return launch_tc_gemv(w, plan, a, m, y, ldy, (float*)s->kscratch, s->err_dev,
+                                          s->sm_count, s->stream, &s->launches, ysp);
+                  };
                   if (tc_gemv_ok(w, M)) {
                     YSel ys;
                     if (s->xsel_offer) {
                       ys = p2p_ysel(s);
                       s->xsel_taken = true;
                     }
-                    const YSel* ysp = s->xsel_offer ? &ys : nullptr;
-                    int rc;
-                    if (w.gemv_plan[M] < 0 && !s->capturing && gemv_tuning_enabled()) {
-                      rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count, -1) * 4);
-                      if (rc) return rc;
-                      rc = tune_tc_gemv(w, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
-                                        s->sm_count, s->stream, ysp);
+                    return gemv_rows(dA, M, yl, s->xsel_offer ? &ys : nullptr);
+                  }
+                  // Up to 8 passes of the GEMV over row chunks (each streams the
+                  // weight again) still beat the CUDA-core GEMM at decode-sized
+                  // M, and every row keeps the exact arithmetic.
+                  int cmax = 0;
+                  for (int m = 8; m >= 1 && !cmax; m--)
+                    if (tc_gemv_ok(w, m)) cmax = m;
+                  if (cmax > 0 && M > cmax && M <= 8 * cmax) {
+                    for (int64_t r = 0; r < M; r += cmax) {
+                      const int64_t m = std::min<int64_t>(cmax, M - r);
+                      int rc = gemv_rows(dA + r * w.K, m, yl + r * ldy, nullptr);
                       if (rc) return rc;
                     }
-                    const int plan = tc_gemv_plan(w, M, s->sm_count);
-                    rc = ensure_kscratch(s, tc_gemv_partial_floats(w, M, s->sm_count, plan) * 4);
-                    if (rc) return rc;
-                    return launch_tc_gemv(w, plan, dA, M, yl, ldy, (float*)s->kscratch, s->err_dev,
-                                          s->sm_count, s->stream, &s->launches, ysp);
+                    return ORT_CUDA_OK;
                   }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K))

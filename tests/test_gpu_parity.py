@@ -534,3 +534,27 @@ def test_every_gemv_plan_gives_the_same_bits(sess, K, N, M):
     assert np.array_equal(sess.matmul_nbits("pl", A), first)
     assert sess.gemv_plan("pl", M) >= 0  # timed and chosen on that call
     sess.drop_weight("pl")
+
+
+@pytest.mark.parametrize("M,bs", [(9, 128), (16, 128), (37, 128), (64, 128), (16, 32), (40, 32)])
+def test_decode_rows_beyond_eight_use_row_chunks(sess, M, bs):
+    """Decode-sized M above the GEMV's 8 rows (north_star's M <= 16 family,
+    cfg1 and cfg5 M=16) runs the exact tensor-core GEMV over row chunks
+    (8 rows; 5 for block size 32): each row matches the oracle and equals
+    the same row computed alone bit for bit."""
+    rng = np.random.default_rng(M * 31 + bs)
+    K, N = 2048, 3000
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    sess.upload_nbits("rc", B, s, z, k=K, n=N, block_size=bs)
+    before = sess.launch_count()
+    y = sess.matmul_nbits("rc", A)
+    chunk = 8 if bs >= 64 else 5
+    passes = -(-M // chunk)
+    # one GEMV launch per chunk, plus a chunk-sum launch where a plan is split-K
+    assert passes <= sess.launch_count() - before <= 2 * passes
+    ref = O.matmul_nbits(A, B, s, z, K, N, 4, bs, threads=8)
+    assert max_rel(ref, y) <= EXACT_TOL
+    for r in (0, M - 1):
+        assert np.array_equal(sess.matmul_nbits("rc", A[r:r + 1]), y[r:r + 1])
+    sess.drop_weight("rc")
