@@ -88,6 +88,13 @@ constexpr uint32_t kXBufBytes = (kXXsum + kMaxBpi * 8 * 4 + 1023) & ~1023u;
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr int kNonFinite = -100000;  // exponent of a chunk row holding an inf or NaN
 
+// Shared memory staging two chunks of A for the X builder: M >= 3 rows
+// (M <= 2 keep the next chunk in registers) when the rows allow 16-byte
+// bulk copies.
+__host__ __device__ constexpr uint32_t a_stage_bytes(int64_t M, int a_vec) {
+  return (M >= 3 && a_vec) ? (uint32_t)(2 * M * kChunkK * 4) : 0u;
+}
+
 // Compile-time shape of the X operand for M rows.
 template <int M>
 struct XShape {
@@ -121,6 +128,7 @@ struct TcParams {
   uint32_t acc_mask;
   int s16;         // block scales streamed as fp16 (widened exactly in the epilogue)
   uint32_t stage_bytes, stage_tx, s_off, z_off, yacc_off;
+  uint32_t a_off;  // M >= 3 with 16-byte activation rows: staging of 2 chunks of A
 };
 
 // Calls f(tile, chunk, tile_in_group) for this CTA's work items, in the
@@ -244,7 +252,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint8_t* Xs = smem;  // two buffers, each X then the digit sums
   uint8_t* Bs = smem + 2 * kXBufBytes;
   float* yacc = reinterpret_cast<float*>(smem + p.yacc_off);  // [tg][M][128]
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + p.yacc_off + p.yacc_bytes);
+  uint8_t* As = smem + p.a_off;  // [2][M][kChunkK] fp32 when staging
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + p.a_off + a_stage_bytes(M, p.a_vec));
   uint64_t* bempty = bfull + kMaxBStages;
   // ready[h]: item j = 2p + h may be issued (phase p): its A is written (8
   // dequantiser warps) and its D buffer is free (4 epilogue warps, after
@@ -266,7 +275,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // cluster mode: every epilogue warp of the cluster has delivered its
   // partials of this CTA's tiles (remote arrivals, csize x 8)
   uint64_t* ibar = xsync + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ibar + 1);
+  uint64_t* abar = ibar + 1;  // [2] a chunk of A staged (bulk copies, M >= 3)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(abar + 2);
   const bool clustered = p.tile_major && p.csize > 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -288,6 +298,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     mbar_init(fin, 1);
     mbar_init(xsync, kDeWarps);
     mbar_init(ibar, p.csize * kEpiWarps);
+    mbar_init(&abar[0], 1);
+    mbar_init(&abar[1], 1);
     fence_mbarrier_init();
   }
   if (warp == kMmaWarp) {
@@ -428,6 +440,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     constexpr int kPre = M <= 2 ? 4 * M : 1;
     float4 pre[kPre];  // M <= 2: the units of chunk pre_chunk
     int pre_chunk = -1;
+    // M >= 3: chunks of A arrive by bulk copies into two staging buffers,
+    // build n reading buffer n & 1; the copy for the next chunk is issued as
+    // soon as a build starts, so it lands while the build runs
+    const bool staged = a_stage_bytes(M, a_vec) != 0;
+    auto issue = [&](int chunk, int buf) {
+      const int k0 = chunk * kChunkK;
+      const uint32_t bytes = (uint32_t)min(kChunkK, K - k0) * 4;
+      mbar_arrive_expect_tx(&abar[buf], bytes * M);
+#pragma unroll
+      for (int m = 0; m < M; m++)
+        bulk_load(As + (buf * M + m) * kChunkK * 4, Ap + (int64_t)m * K + k0, bytes, &abar[buf]);
+    };
+    int issued = 0, waited = 0;  // staged copies requested / completed (copy n: build n)
     bool ok = true;
     int cur = -1, nbuild = 0;
     for_each_item(p, [&](int, int chunk, int) {
@@ -438,6 +463,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int i = 0; i < kPre; i++) pre[i] = load(chunk, i);
       }
+      const uint8_t* abuf = As + (nbuild & 1) * M * kChunkK * 4;
+      if (staged) {
+        if (issued == nbuild) {  // the first build: nothing was prefetched
+          if (lane == 0) issue(chunk, nbuild & 1);
+          issued++;
+        }
+        if (!mbar_wait(&abar[nbuild & 1], (nbuild >> 1) & 1)) {
+          record_error(p.err, KERR_WAIT_FULL);
+          return ok = false;
+        }
+        waited++;
+        // buffer (n + 1) & 1 was last read by build n - 1, which has ended
+        const int nx = chunk + 1 < c_end ? chunk + 1 : c_first;
+        if (lane == 0) issue(nx, (nbuild + 1) & 1);
+        issued++;
+      }
+      const int k0s = chunk * kChunkK;
+      // unit i of this lane: registers (M <= 2), the staging buffer, or A
+      auto unit = [&](int i) {
+        if (M <= 2) return pre[M <= 2 ? i : 0];
+        if (!staged) return load(chunk, i);
+        const int m = i >> 2, kk = (lane + 32 * (i & 3)) * 4;
+        if (k0s + kk >= K) return make_float4(0.f, 0.f, 0.f, 0.f);
+        return lds128f(smem_u32(abuf + (m * kChunkK + kk) * 4));
+      };
       const int xbuf = nbuild & 1;
       if (!mbar_wait(&xempty[xbuf], ((nbuild >> 1) & 1) ^ 1)) {
         record_error(p.err, KERR_WAIT_EMPTY);
@@ -454,7 +504,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         unsigned mb = 0;
 #pragma unroll
         for (int i = 4 * m; i < 4 * m + 4; i++) {
-          const float4 a = M <= 2 ? pre[M <= 2 ? i : 0] : load(chunk, i);
+          const float4 a = unit(i);
           mb = max(mb, max(max(__float_as_uint(a.x) & 0x7fffffffu, __float_as_uint(a.y) & 0x7fffffffu),
                            max(__float_as_uint(a.z) & 0x7fffffffu, __float_as_uint(a.w) & 0x7fffffffu)));
         }
@@ -475,7 +525,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int i = 4 * m + q4, k = (lane + 32 * q4) * 4;
           const int slot = (k >> bs_log2) % G;
           uint32_t w0, w1, w2;
-          x_digits(M <= 2 ? pre[M <= 2 ? i : 0] : load(chunk, i), rs[m], w0, w1, w2, sx[q4]);
+          x_digits(unit(i), rs[m], w0, w1, w2, sx[q4]);
           const int jr = (slot * M + m) * 3;
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr, k)), "r"(w0) : "memory");
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(x_addr(xb, NM, jr + 1, k)), "r"(w1)
@@ -506,6 +556,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       nbuild++;
       return true;
     });
+    // copies still in flight (the last prefetch) land before the CTA's
+    // shared memory is released; copy j is phase j >> 1 of abar[j & 1]
+    for (int j = waited; j < issued; j++)
+      if (!mbar_wait(&abar[j & 1], (j >> 1) & 1)) {
+        record_error(p.err, KERR_WAIT_DRAIN);
+        break;
+      }
   } else if (warp < kDeWarps) {
     // ---------------- dequantisers ----------------
     const int q = warp & 3, grp = warp >> 2;
@@ -970,7 +1027,10 @@ std::vector<Plan> plan_candidates(const Weight& w, int64_t M, int sm_count) {
     if (mc <= 0) continue;
     const int ncl = std::min(base.tiles, mc), T = (base.tiles + ncl - 1) / ncl;
     const size_t inbox = (size_t)((T + c - 1) / c) * base.nch * tile_bytes;
-    if (1024 + 2 * (size_t)kXBufBytes + inbox + 1024 + 3 * stage > kSmemLimit) continue;
+    if (1024 + 2 * (size_t)kXBufBytes + inbox + a_stage_bytes(M, w.K % 4 == 0) + 1024 +
+            3 * stage >
+        kSmemLimit)
+      continue;
     Plan cl = base;
     cl.tile_major = true;
     cl.csize = c;
@@ -1038,12 +1098,13 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
   const uint32_t yacc_bytes = pl.yacc_bytes;
   const int grid = pl.grid;
   p.yacc_bytes = yacc_bytes;
-  const size_t fixed = 1024 + 2 * kXBufBytes + yacc_bytes + 1024;
+  const size_t fixed = 1024 + 2 * kXBufBytes + yacc_bytes + a_stage_bytes(M, p.a_vec) + 1024;
   int nbst = (int)((kSmemLimit - fixed) / p.stage_bytes);
   if (nbst > kMaxBStages) nbst = kMaxBStages;
   if (nbst < 2) return fail(ORT_CUDA_ERR_UNSUPPORTED, "tc gemv: shared memory too small");
   p.nbst = nbst;
   p.yacc_off = 2 * kXBufBytes + nbst * p.stage_bytes;
+  p.a_off = p.yacc_off + yacc_bytes;
   const size_t smem = fixed + (size_t)nbst * p.stage_bytes;
   // Programmatic dependent launch: this kernel's prologue and weight stream
   // may overlap the previous kernel's tail; it reads activations and writes

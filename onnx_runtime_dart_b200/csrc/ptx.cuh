@@ -110,6 +110,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Untiled bulk copy from global memory into this CTA's shared memory,
+// completing on `bar` (both addresses 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Same, with an L2 eviction-priority hint (for data read exactly once).
 __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map,
                                                  uint64_t* bar, int x, int y, uint64_t policy) {
