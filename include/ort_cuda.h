@@ -79,6 +79,10 @@ extern "C" {
 /* Zero points per column, ceil(nb/2) bytes per column (the ORT
  * com.microsoft spec).  Differs from the reference only when nb is odd. */
 #define ORT_CUDA_ZP_PER_COLUMN 0x10
+/* ort_cuda_argmax: ArgMin instead of ArgMax; ties to the last index
+ * (ONNX select_last_index=1) instead of the first */
+#define ORT_CUDA_ARG_MIN 0x20
+#define ORT_CUDA_ARG_SELECT_LAST 0x40
 
 typedef struct ort_cuda_session ort_cuda_session;
 
@@ -241,6 +245,18 @@ ORT_CUDA_API int ort_cuda_graph_drop(ort_cuda_session* s, int graph_id);
  * whose one CPU kernel has no plans (lib/src/onnx_qlinear_ops.dart:114). */
 ORT_CUDA_API int ort_cuda_gemv_plan_get(ort_cuda_session* s, const char* name, int M, int* plan);
 ORT_CUDA_API int ort_cuda_gemv_plan_set(ort_cuda_session* s, const char* name, int M, int plan);
+
+/* ArgMax (or, with ORT_CUDA_ARG_MIN, ArgMin) over the last axis of X, a
+ * [rows x cols] fp32 matrix with row stride ldx: out[r] is the int64 index
+ * the reference's opArgMinMax (lib/src/onnx_ops.dart:2198-2237) gives for
+ * row r — ties to the first index (the last with ORT_CUDA_ARG_SELECT_LAST),
+ * a NaN selected only when it is the row's first element.  Replaces the
+ * body of an `ArgMax` node whose input is on the device (the lm_head logits
+ * of a greedy decode step), so a step reads back rows x 8 bytes instead of
+ * the logits.  X and out are device pointers (stream-ordered) unless
+ * ORT_CUDA_HOST_IO is set.  Other axes: move the axis last first. */
+ORT_CUDA_API int ort_cuda_argmax(ort_cuda_session* s, const float* X, int64_t rows, int64_t cols,
+                                 int64_t ldx, int64_t* out, int flags);
 
 /* Kernel launches issued by this session since it was opened (all of
  * them this library's own kernels; a graph launch counts the kernels it

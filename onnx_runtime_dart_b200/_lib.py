@@ -45,6 +45,8 @@ SCALES_F32 = 0
 SCALES_F16 = 1
 ZP_FLAT = 0x0
 ZP_PER_COLUMN = 0x10
+ARG_MIN = 0x20  # ort_cuda_argmax flags
+ARG_SELECT_LAST = 0x40
 
 # Every symbol include/ort_cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -79,6 +81,7 @@ SIGNATURES = {
     "ort_cuda_matmul_batched": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _int]),
     "ort_cuda_gemv_plan_get": (_int, [_vp, _cp, _int, ctypes.POINTER(_int)]),
     "ort_cuda_gemv_plan_set": (_int, [_vp, _cp, _int, _int]),
+    "ort_cuda_argmax": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _int]),
     "ort_cuda_launch_count": (_int, [_vp, ctypes.POINTER(_i64)]),
     "ort_cuda_graph_begin": (_int, [_vp]),
     "ort_cuda_graph_end": (_int, [_vp, ctypes.POINTER(_int)]),

@@ -116,6 +116,11 @@ struct ort_cuda_session {
   // grow-only kernel scratch for split-K partials (no initial value needed)
   void* kscratch = nullptr;
   size_t kscratch_bytes = 0;
+  // grow-only ArgMax scratch: per-row tickets (arg_rows_cap, first) then
+  // segment candidates (arg_cand_cap); zeroed when allocated, and every call
+  // returns the tickets it used to zero
+  void* argscratch = nullptr;
+  int64_t arg_rows_cap = 0, arg_cand_cap = 0;
   // N-sharded sessions: peer-memory exchange of Y (csrc/p2p.cu).  xbuf holds
   // a 256-byte flag area (8 peer flags, epoch counter, CTA counter) then two
   // halves of xcap floats; xpeer[r] is rank r's xbuf mapped into this
@@ -216,6 +221,16 @@ int launch_simt_batched(const float* A, const float* B, int64_t batch, int64_t m
                         int64_t n, int64_t b_batch_stride, float* Y, bool strict,
                         cudaStream_t st, int64_t* launches);
 // Upload-time device prepack helpers.
+// ArgMax / ArgMin over the last axis of X[rows][ldx] (first `cols` columns)
+// into out[rows] (device), the reference's tie and NaN rules.  Rows of more
+// than one 16K-column segment use argminmax_candidates(rows, cols) slots of
+// argminmax_candidate_bytes() in `candidates` and rows tickets, which must
+// be zero on entry and are zero again when the kernel ends.
+int64_t argminmax_candidates(int64_t rows, int64_t cols);
+size_t argminmax_candidate_bytes();
+int launch_argminmax(const float* X, int64_t rows, int64_t cols, int64_t ldx, bool is_min,
+                     bool last, int64_t* out, unsigned* tickets, void* candidates,
+                     cudaStream_t st, int64_t* launches);
 int launch_permute_nibbles(const uint32_t* in, uint32_t* out, int64_t nwords, cudaStream_t st,
                            int64_t* launches);
 int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,

@@ -417,6 +417,7 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   s->allocs.clear();
   if (s->ws) cudaFree(s->ws);
   if (s->kscratch) cudaFree(s->kscratch);
+  if (s->argscratch) cudaFree(s->argscratch);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second.exec);
@@ -802,6 +803,58 @@ ORT_CUDA_API int ort_cuda_d2h(ort_cuda_session* s, void* dst, const void* src, i
   ORTC_CHECK(s && dst && src && bytes >= 0, ORT_CUDA_ERR_INVALID_ARG, "bad argument");
   DeviceGuard g(s->device);
   ORTC_CUDA(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
+}
+
+ORT_CUDA_API int ort_cuda_argmax(ort_cuda_session* s, const float* X, int64_t rows,
+                                 int64_t cols, int64_t ldx, int64_t* out, int flags) {
+  ORTC_CHECK(s && X && out, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(rows >= 0 && cols >= 1 && ldx >= cols, ORT_CUDA_ERR_INVALID_ARG,
+             "ArgMax: need rows >= 0 and 1 <= cols <= ldx");
+  if (rows == 0) return ORT_CUDA_OK;
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  DeviceGuard g(s->device);
+  const int64_t ncand = argminmax_candidates(rows, cols);
+  if (ncand > 0 && (rows > s->arg_rows_cap || ncand > s->arg_cand_cap)) {
+    ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+               "a buffer would grow while a CUDA graph is being captured; run every "
+               "operation of the graph once before capturing it");
+    if (s->argscratch) {
+      ORTC_CUDA(cudaStreamSynchronize(s->stream));
+      ORTC_CUDA(cudaFree(s->argscratch));
+      s->argscratch = nullptr;
+      s->arg_rows_cap = s->arg_cand_cap = 0;
+    }
+    const int64_t rcap = std::max<int64_t>(rows, 64), ccap = std::max<int64_t>(ncand, 512);
+    const size_t bytes = ((size_t)rcap * 4 + 255) / 256 * 256 + (size_t)ccap * argminmax_candidate_bytes();
+    ORTC_CUDA(cudaMalloc(&s->argscratch, bytes));
+    ORTC_CUDA(cudaMemsetAsync(s->argscratch, 0, bytes, s->stream));
+    s->arg_rows_cap = rcap;
+    s->arg_cand_cap = ccap;
+  }
+  unsigned* tickets = static_cast<unsigned*>(s->argscratch);
+  void* cands = s->argscratch
+                    ? static_cast<char*>(s->argscratch) + ((size_t)s->arg_rows_cap * 4 + 255) / 256 * 256
+                    : nullptr;
+  const bool is_min = (flags & ORT_CUDA_ARG_MIN) != 0;
+  const bool last = (flags & ORT_CUDA_ARG_SELECT_LAST) != 0;
+  if (!host)
+    return launch_argminmax(X, rows, cols, ldx, is_min, last, out, tickets, cands, s->stream,
+                            &s->launches);
+  // host buffers: the rows in, the indices back, synchronously
+  const size_t xbytes = (size_t)(rows * cols) * 4, obytes = (size_t)rows * 8;
+  int rc = ensure_ws(s, xbytes + obytes + 256);
+  if (rc) return rc;
+  float* dx = static_cast<float*>(s->ws);
+  int64_t* dout = reinterpret_cast<int64_t*>(static_cast<char*>(s->ws) + ((xbytes + 255) & ~(size_t)255));
+  ORTC_CUDA(cudaMemcpy2DAsync(dx, (size_t)cols * 4, X, (size_t)ldx * 4, (size_t)cols * 4,
+                              (size_t)rows, cudaMemcpyHostToDevice, s->stream));
+  rc = launch_argminmax(dx, rows, cols, cols, is_min, last, dout, tickets, cands, s->stream,
+                        &s->launches);
+  if (rc) return rc;
+  ORTC_CUDA(cudaMemcpyAsync(out, dout, obytes, cudaMemcpyDeviceToHost, s->stream));
   return bounded_sync(s);
 }
 

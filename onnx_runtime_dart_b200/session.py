@@ -249,6 +249,45 @@ class CudaSession:
         del L
         return y
 
+    def argmax(self, x, *, is_min: bool = False, select_last: bool = False,
+               keepdims: bool = False):
+        """ArgMax (ArgMin) over the last axis with the reference's tie and
+        NaN rules (opArgMinMax, lib/src/onnx_ops.dart:2198-2237).  A torch
+        CUDA tensor gives a torch int64 tensor on its device (stream-ordered);
+        a numpy array or a DeviceTensor gives a numpy int64 array."""
+        L = _lib.load()
+        shape = tuple(x.shape)
+        if not shape or shape[-1] < 1:
+            raise ValueError("ArgMax needs a non-empty last axis")
+        cols = shape[-1]
+        rows = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        out_shape = shape[:-1] + ((1,) if keepdims else ())
+        flags = (_lib.ARG_MIN if is_min else 0) | (_lib.ARG_SELECT_LAST if select_last else 0)
+        if hasattr(x, "data_ptr"):  # torch CUDA tensor
+            import torch
+            x = x.contiguous().float()
+            out = torch.empty(out_shape, dtype=torch.int64, device=x.device)
+            check(L.ort_cuda_argmax(self.handle, x.data_ptr(), rows, cols, cols, out.data_ptr(),
+                                    flags), "ort_cuda_argmax")
+            return out
+        if isinstance(x, DeviceTensor):
+            p = ctypes.c_void_p()
+            check(L.ort_cuda_alloc(self.handle, rows * 8, ctypes.byref(p)), "ort_cuda_alloc")
+            try:
+                check(L.ort_cuda_argmax(self.handle, x.ptr, rows, cols, cols, p.value, flags),
+                      "ort_cuda_argmax")
+                out = np.empty(out_shape, np.int64)
+                check(L.ort_cuda_d2h(self.handle, out.ctypes.data, p.value, rows * 8),
+                      "ort_cuda_d2h")
+            finally:
+                check(L.ort_cuda_free(self.handle, p.value), "ort_cuda_free")
+            return out
+        a = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(out_shape, np.int64)
+        check(L.ort_cuda_argmax(self.handle, a.ctypes.data, rows, cols, cols, out.ctypes.data,
+                                flags | _lib.HOST_IO), "ort_cuda_argmax")
+        return out
+
     def matmul_nbits(self, name: str, a: Tensorish, flags: int = 0, out=None):
         kind, k, n = self.weights[name]
         shape = tuple(a.shape)

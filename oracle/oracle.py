@@ -178,3 +178,31 @@ def matmul(a, b, threads: int = 1) -> np.ndarray:
 # Seeded synthetic inputs come from the package's workload definitions
 # (data generation only; no arithmetic of the path lives there).
 from onnx_runtime_dart_b200.workloads import make_nbits_weight, pack_nibbles  # noqa: E402,F401
+
+
+def argminmax(x, axis: int = 0, keepdims: bool = True, is_max: bool = True,
+              select_last: bool = False) -> np.ndarray:
+    """ArgMax / ArgMin, restating opArgMinMax (lib/src/onnx_ops.dart:2198-2237):
+    along `axis`, a scan from element 0 that replaces the best on a strictly
+    better value (or also an equal one with select_last_index), with plain
+    comparisons, so ties keep the first (last) index and a NaN wins only as
+    element 0.  int64 result; plain Python loops (small inputs)."""
+    x = np.asarray(x, dtype=np.float32)
+    ax = axis + x.ndim if axis < 0 else axis
+    xm = np.moveaxis(x, ax, -1)
+    flat = xm.reshape(-1, xm.shape[-1])
+    out = np.empty(flat.shape[0], np.int64)
+    for r in range(flat.shape[0]):
+        row = flat[r].tolist()
+        best, best_i = row[0], 0
+        for d in range(1, len(row)):
+            v = row[d]
+            if is_max:
+                better = v >= best if select_last else v > best
+            else:
+                better = v <= best if select_last else v < best
+            if better:
+                best, best_i = v, d
+        out[r] = best_i
+    out = out.reshape(xm.shape[:-1])
+    return np.expand_dims(out, ax) if keepdims else out

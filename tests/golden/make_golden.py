@@ -28,6 +28,11 @@ CASES = [
     "matmulnbits_partial_block",
     "gemm_transB_bias",
     "matmul_batched",
+    # device ArgMax / ArgMin over the last axis (the lm_head -> ArgMax step
+    # of greedy decoding), pinned to the reference's ORT fixtures
+    "argmax_axis1",
+    "argmax_nan",
+    "argmin_nokeep_last",
 ]
 
 _ONNX_DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 6: np.int32, 7: np.int64,

@@ -168,3 +168,23 @@ def test_oracle_rejects_bits8():
     with pytest.raises(NotImplementedError):
         O.matmul_nbits(np.zeros((1, 32), np.float32), np.zeros((1, 1, 16), np.uint8),
                        np.ones(1, np.float32), None, 32, 1, 8, 32)
+
+
+def _argminmax_fixture(golden, case):
+    g = golden(case)
+    meta = g["meta"]
+    a = meta["attrs"]
+    return g, dict(axis=int(a.get("axis", 0)), keepdims=bool(a.get("keepdims", 1)),
+                   is_max=meta["op_type"] == "ArgMax",
+                   select_last=bool(a.get("select_last_index", 0)))
+
+
+@pytest.mark.parametrize("case", ["argmax_axis1", "argmax_nan", "argmin_nokeep_last"])
+def test_oracle_argminmax_fixtures(golden, case):
+    """ArgMax / ArgMin restatement against the reference's ORT fixtures
+    (ties to the first or, with select_last_index, last index; a NaN wins
+    only as the first element).  Integer output: exact."""
+    g, kw = _argminmax_fixture(golden, case)
+    got = O.argminmax(g["in_x"], **kw)
+    assert got.dtype == np.int64
+    assert np.array_equal(got, g["expected"])
