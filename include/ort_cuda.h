@@ -155,6 +155,24 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
 ORT_CUDA_API int ort_cuda_upload_dense(ort_cuda_session* s, const char* name, const float* B,
                                        int64_t rows, int64_t cols, int trans_b);
 
+/* The same weight read straight from a file of ONNX external data (the
+ * companion `.onnx.data` of a model too large to hold in host memory): packed
+ * B at byte b_offset (N * ceil(K/bs) * bs/2 bytes), scales at scales_offset
+ * (N * ceil(K/bs) fp32, or fp16 with ORT_CUDA_SCALES_F16), zero points at
+ * zp_offset (< 0: none; flat or ORT_CUDA_ZP_PER_COLUMN size).  B streams
+ * through a small pinned buffer and an N-sharded rank reads only its own
+ * columns, so no host copy of the weight is made.  `path` is the resolved
+ * companion file (the host keeps the reference's rules for which paths a
+ * model may name); a range outside the file or a short read returns
+ * ORT_CUDA_ERR_INVALID_ARG (the reference's FormatException).  Replaces, for
+ * MatMulNBits initializers, the resolve() of loadOnnxModel
+ * (lib/onnx_runtime_dart_io.dart:19-45) feeding _rawBytes
+ * (lib/src/onnx_proto_loader.dart:89-112). */
+ORT_CUDA_API int ort_cuda_upload_nbits_file(ort_cuda_session* s, const char* name,
+                                            const char* path, int64_t b_offset,
+                                            int64_t scales_offset, int64_t zp_offset, int64_t K,
+                                            int64_t N, int bits, int block_size, int flags);
+
 /* Releases one weight. */
 ORT_CUDA_API int ort_cuda_drop_weight(ort_cuda_session* s, const char* name);
 

@@ -67,6 +67,8 @@ SIGNATURES = {
     "ort_cuda_sync": (_int, [_vp]),
     "ort_cuda_rank_info": (_int, [_vp, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
     "ort_cuda_upload_nbits": (_int, [_vp, _cp, _vp, _vp, _vp, _i64, _i64, _int, _int, _int]),
+    "ort_cuda_upload_nbits_file": (_int, [_vp, _cp, _cp, _i64, _i64, _i64, _i64, _i64, _int,
+                                          _int, _int]),
     "ort_cuda_upload_dense": (_int, [_vp, _cp, _vp, _i64, _i64, _int]),
     "ort_cuda_drop_weight": (_int, [_vp, _cp]),
     "ort_cuda_weight_shape": (_int, [_vp, _cp, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),

@@ -6,9 +6,15 @@
 // state the reference keeps for them (_initializers, _prepackedGemmB,
 // onnx_graph.dart:51-56) and its column-split worker pool
 // (lib/src/parallel_pool.dart:108-205), which becomes NCCL N-sharding.
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <thread>
 #include <vector>
@@ -521,10 +527,16 @@ ORT_CUDA_API int ort_cuda_launch_count(ort_cuda_session* s, int64_t* count) {
 
 // ---- weights ---------------------------------------------------------------
 
-ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, const uint8_t* B,
-                                       const void* scales, const uint8_t* zp, int64_t K,
-                                       int64_t N, int bits, int block_size, int flags) {
-  ORTC_CHECK(s && name && B && scales, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+}  // extern "C"
+
+namespace {
+// Fills dst (device) with bytes [off, off + bytes) of the packed B of a
+// MatMulNBits weight, on the session stream.
+using BSource = std::function<int(void* dst, int64_t off, int64_t bytes)>;
+
+int upload_nbits_impl(ort_cuda_session* s, const char* name, const BSource& Bsrc,
+                      const void* scales, const uint8_t* zp, int64_t K, int64_t N, int bits,
+                      int block_size, int flags) {
   if (bits != 4)
     return fail(ORT_CUDA_ERR_UNSUPPORTED,
                 "MatMulNBits: only bits=4 supported, got " + std::to_string(bits));
@@ -558,12 +570,11 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
     e = cudaMalloc(&tmpB, (size_t)(nl * col_bytes));
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc(B staging)"));
     e = cudaMalloc(&w.B, (size_t)(nl * col_bytes));
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(tmpB, B + w.n0 * col_bytes, (size_t)(nl * col_bytes),
-                          cudaMemcpyHostToDevice, s->stream);
-    int rc = e == cudaSuccess ? launch_permute_nibbles((const uint32_t*)tmpB, (uint32_t*)w.B,
-                                                       nl * col_bytes / 4, s->stream, &s->launches)
-                              : cuda_fail(e, "copy B");
+    int rc = e == cudaSuccess ? Bsrc(tmpB, w.n0 * col_bytes, nl * col_bytes)
+                              : cuda_fail(e, "cudaMalloc(B)");
+    if (!rc)
+      rc = launch_permute_nibbles((const uint32_t*)tmpB, (uint32_t*)w.B, nl * col_bytes / 4,
+                                  s->stream, &s->launches);
     cudaStreamSynchronize(s->stream);
     cudaFree(tmpB);
     if (rc) return cleanup(rc);
@@ -664,6 +675,102 @@ ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, co
   }
   s->weights.emplace(name, w);
   return ORT_CUDA_OK;
+}
+
+// Reads [off, off + len) of an open file completely (pread loops over short
+// reads); false on error or end of file.
+bool read_at(int fd, void* dst, int64_t off, int64_t len) {
+  char* p = static_cast<char*>(dst);
+  while (len > 0) {
+    const ssize_t r = pread(fd, p, (size_t)std::min<int64_t>(len, 1 << 30), (off_t)off);
+    if (r <= 0) return false;
+    p += r;
+    off += r;
+    len -= r;
+  }
+  return true;
+}
+
+struct FdCloser {
+  int fd;
+  ~FdCloser() {
+    if (fd >= 0) close(fd);
+  }
+};
+}  // namespace
+
+extern "C" {
+
+ORT_CUDA_API int ort_cuda_upload_nbits(ort_cuda_session* s, const char* name, const uint8_t* B,
+                                       const void* scales, const uint8_t* zp, int64_t K,
+                                       int64_t N, int bits, int block_size, int flags) {
+  ORTC_CHECK(s && name && B && scales, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  const BSource from_host = [&](void* dst, int64_t off, int64_t bytes) -> int {
+    ORTC_CUDA(cudaMemcpyAsync(dst, B + off, (size_t)bytes, cudaMemcpyHostToDevice, s->stream));
+    return ORT_CUDA_OK;
+  };
+  return upload_nbits_impl(s, name, from_host, scales, zp, K, N, bits, block_size, flags);
+}
+
+ORT_CUDA_API int ort_cuda_upload_nbits_file(ort_cuda_session* s, const char* name,
+                                            const char* path, int64_t b_offset,
+                                            int64_t scales_offset, int64_t zp_offset, int64_t K,
+                                            int64_t N, int bits, int block_size, int flags) {
+  ORTC_CHECK(s && name && path, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+             "weights cannot be uploaded while a CUDA graph is being captured");
+  ORTC_CHECK(K > 0 && N > 0 && K < (1ll << 31) && N < (1ll << 31) && block_size >= 16,
+             ORT_CUDA_ERR_INVALID_ARG, "MatMulNBits: bad K, N or block_size");
+  const int fd = open(path, O_RDONLY);
+  ORTC_CHECK(fd >= 0, ORT_CUDA_ERR_INVALID_ARG, std::string("cannot open '") + path + "'");
+  FdCloser closer{fd};
+  struct stat st;
+  ORTC_CHECK(fstat(fd, &st) == 0, ORT_CUDA_ERR_INVALID_ARG, std::string("cannot stat '") + path + "'");
+  const int64_t fsize = (int64_t)st.st_size;
+  const int64_t nb = (K + block_size - 1) / block_size;
+  const int64_t col_bytes = nb * block_size / 2;
+  const bool f16 = (flags & ORT_CUDA_SCALES_F16) != 0;
+  const int64_t b_bytes = N * col_bytes, s_bytes = N * nb * (f16 ? 2 : 4);
+  const int64_t z_bytes =
+      (flags & ORT_CUDA_ZP_PER_COLUMN) ? N * ((nb + 1) / 2) : (N * nb + 1) / 2;
+  // every range inside the file (the reference rejects a reference outside
+  // the companion file, onnx_runtime_dart_io.dart:55-80)
+  auto inside = [&](int64_t off, int64_t len) { return off >= 0 && off <= fsize - len; };
+  ORTC_CHECK(inside(b_offset, b_bytes) && inside(scales_offset, s_bytes) &&
+                 (zp_offset < 0 || inside(zp_offset, z_bytes)),
+             ORT_CUDA_ERR_INVALID_ARG,
+             std::string("MatMulNBits external data: a range lies outside '") + path + "' (" +
+                 std::to_string(fsize) + " bytes)");
+  std::vector<uint8_t> sc((size_t)s_bytes), zz(zp_offset >= 0 ? (size_t)z_bytes : 0);
+  ORTC_CHECK(read_at(fd, sc.data(), scales_offset, s_bytes) &&
+                 (zp_offset < 0 || read_at(fd, zz.data(), zp_offset, z_bytes)),
+             ORT_CUDA_ERR_INVALID_ARG, std::string("short read from '") + path + "'");
+  DeviceGuard g(s->device);
+  // B through two pinned bounce buffers: the read of one chunk overlaps the
+  // copy of the previous one
+  constexpr int64_t kChunk = 16 << 20;
+  int rc = ensure_pinned(s, 2 * kChunk);
+  if (rc) return rc;
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  for (auto& ev : done) ORTC_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  const BSource from_file = [&](void* dst, int64_t off, int64_t bytes) -> int {
+    for (int64_t c = 0, i = 0; c < bytes; c += kChunk, i++) {
+      const int64_t len = std::min(kChunk, bytes - c);
+      char* buf = static_cast<char*>(s->pinned) + (i & 1) * kChunk;
+      ORTC_CUDA(cudaEventSynchronize(done[i & 1]));  // its previous copy has ended
+      if (!read_at(fd, buf, b_offset + off + c, len))
+        return fail(ORT_CUDA_ERR_INVALID_ARG, std::string("short read from '") + path + "'");
+      ORTC_CUDA(cudaMemcpyAsync(static_cast<char*>(dst) + c, buf, (size_t)len,
+                                cudaMemcpyHostToDevice, s->stream));
+      ORTC_CUDA(cudaEventRecord(done[i & 1], s->stream));
+    }
+    return ORT_CUDA_OK;
+  };
+  rc = upload_nbits_impl(s, name, from_file, sc.data(), zp_offset >= 0 ? zz.data() : nullptr, K,
+                         N, bits, block_size, flags);
+  cudaStreamSynchronize(s->stream);
+  for (auto& ev : done) cudaEventDestroy(ev);
+  return rc;
 }
 
 ORT_CUDA_API int ort_cuda_upload_dense(ort_cuda_session* s, const char* name, const float* B,

@@ -17,6 +17,7 @@ this module computes a matmul on the CPU.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Dict, List, Optional, Sequence, Union
 
 import numpy as np
@@ -204,6 +205,21 @@ class CudaSession:
         check(_lib.load().ort_cuda_upload_nbits(self.handle, name.encode(), b_q.ctypes.data,
                                                 sc.ctypes.data, _ptr(zp), k, n, bits,
                                                 block_size, flags), "ort_cuda_upload_nbits")
+        self.weights[name] = ("nbits", k, n)
+
+    def upload_nbits_file(self, name: str, path: str, *, b_offset: int, scales_offset: int,
+                          zp_offset: Optional[int], k: int, n: int, block_size: int,
+                          bits: int = 4, scales_f16: bool = False,
+                          zp_per_column: bool = False) -> None:
+        """A MatMulNBits weight read straight from an external-data file
+        (ort_cuda_upload_nbits_file): byte offsets of B, scales and zero
+        points (None: no zero points) in `path`."""
+        flags = (_lib.ZP_PER_COLUMN if zp_per_column else _lib.ZP_FLAT) | \
+            (_lib.SCALES_F16 if scales_f16 else 0)
+        check(_lib.load().ort_cuda_upload_nbits_file(
+            self.handle, name.encode(), os.fsencode(path), b_offset, scales_offset,
+            -1 if zp_offset is None else zp_offset, k, n, bits, block_size, flags),
+            "ort_cuda_upload_nbits_file")
         self.weights[name] = ("nbits", k, n)
 
     def upload_dense(self, name: str, b: np.ndarray, trans_b: bool = False) -> None:
