@@ -206,3 +206,55 @@ def argminmax(x, axis: int = 0, keepdims: bool = True, is_max: bool = True,
         out[r] = best_i
     out = out.reshape(xm.shape[:-1])
     return np.expand_dims(out, ax) if keepdims else out
+
+
+def matmul_integer(a, b, a_zp=None, b_zp=None) -> np.ndarray:
+    """MatMulInteger, restating opMatMulInteger
+    (lib/src/onnx_qlinear_ops.dart:26-79): Y = (A - a_zp) . (B - b_zp),
+    exact integers (int64, as the reference stores them); a_zp scalar or per
+    row [M], b_zp scalar or per column [N]; batch dims as in MatMul (equal or
+    1)."""
+    a = np.asarray(a).astype(np.int64)
+    b = np.asarray(b).astype(np.int64)
+    m, n = a.shape[-2], b.shape[-1]
+    az = 0 if a_zp is None else np.asarray(a_zp).astype(np.int64).reshape(-1)
+    bz = 0 if b_zp is None else np.asarray(b_zp).astype(np.int64).reshape(-1)
+    if a_zp is not None and az.size not in (1, m):
+        raise ValueError("MatMulInteger: a_zp must be scalar or per-row [M]")
+    if b_zp is not None and bz.size not in (1, n):
+        raise ValueError("MatMulInteger: b_zp must be scalar or per-column [N]")
+    ac = a - (az.reshape(-1, 1) if np.size(az) == m and m != 1 else np.reshape(az, ()))
+    bc = b - (np.reshape(bz, ()) if np.size(bz) == 1 else bz)
+    return np.matmul(ac, bc)
+
+
+def _round_even(v: float) -> int:
+    """Round half to even (the reference's _roundEven,
+    onnx_qlinear_ops.dart:17-24)."""
+    f = np.floor(v)
+    frac = v - f
+    if frac > 0.5:
+        return int(f) + 1
+    if frac < 0.5:
+        return int(f)
+    i = int(f)
+    return i if i % 2 == 0 else i + 1
+
+
+def dynamic_quantize_linear(x):
+    """DynamicQuantizeLinear, restating opDynamicQuantizeLinear
+    (lib/src/onnx_ops.dart:2556-2580): range [min(0, min x), max(0, max x)];
+    scale = fp32((mx - mn) / 255); zp = round-half-even(clamp(fp32(-mn /
+    scale), 0, 255)); y = saturate(round-half-even(fp32(x / scale)) + zp).
+    Returns (uint8 y, float32 scale, int zp)."""
+    xf = np.asarray(x, dtype=np.float32).reshape(-1)
+    mn = min(0.0, float(xf.min())) if xf.size else 0.0
+    mx = max(0.0, float(xf.max())) if xf.size else 0.0
+    scale = float(np.float32((mx - mn) / 255.0))
+    zpf = 0.0 if scale == 0 else float(np.float32(-mn / scale))
+    zp = _round_even(min(max(zpf, 0.0), 255.0))
+    out = np.empty(xf.size, np.uint8)
+    for k, v in enumerate(xf.tolist()):
+        q = zp if scale == 0 else _round_even(float(np.float32(v / scale))) + zp
+        out[k] = 0 if q < 0 else (255 if q > 255 else q)
+    return out.reshape(np.shape(x)), np.float32(scale), zp

@@ -33,6 +33,13 @@ CASES = [
     "argmax_axis1",
     "argmax_nan",
     "argmin_nokeep_last",
+    # the int8 dynamic-quantisation path: DynamicQuantizeLinear and
+    # MatMulInteger (scalar / per-column zero points, u8 x i8, batched)
+    "dynamicquantizelinear",
+    "matmulinteger_nozp",
+    "matmulinteger_percol_bzp",
+    "matmulinteger_u8i8",
+    "matmulinteger_batched",
 ]
 
 _ONNX_DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 6: np.int32, 7: np.int64,
@@ -171,8 +178,12 @@ def main(ref_root):
             arrays["in_" + k] = np.array(v["data"], dtype=v["dtype"]).reshape(v["shape"])
         for k, v in inits.items():
             arrays["init_" + k] = v
-        (ok, ov), = cj["expected"].items()
-        arrays["expected"] = np.array(ov["data"], dtype=ov["dtype"]).reshape(ov["shape"])
+        outs = list(cj["expected"].items())
+        for ok, ov in outs:  # every output; the only one also as "expected"
+            arr = np.array(ov["data"], dtype=ov["dtype"]).reshape(ov["shape"])
+            arrays["expected_" + ok] = arr
+            if len(outs) == 1:
+                arrays["expected"] = arr
         meta = dict(nodes[0])
         meta["source"] = f"test/fixtures/{case}"
         arrays["meta"] = np.array(json.dumps(meta))

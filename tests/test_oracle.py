@@ -188,3 +188,21 @@ def test_oracle_argminmax_fixtures(golden, case):
     got = O.argminmax(g["in_x"], **kw)
     assert got.dtype == np.int64
     assert np.array_equal(got, g["expected"])
+
+
+@pytest.mark.parametrize("case", ["matmulinteger_nozp", "matmulinteger_percol_bzp",
+                                  "matmulinteger_u8i8", "matmulinteger_batched"])
+def test_oracle_matmul_integer_fixtures(golden, case):
+    """MatMulInteger restatement against the reference's ORT fixtures:
+    exact integers."""
+    g = golden(case)
+    got = O.matmul_integer(g["init_a"], g["init_b"], g.get("init_az"), g.get("init_bz"))
+    assert np.array_equal(got, g["expected"])
+
+
+def test_oracle_dynamic_quantize_linear_fixture(golden):
+    g = golden("dynamicquantizelinear")
+    y, scale, zp = O.dynamic_quantize_linear(g["in_x"])
+    assert np.array_equal(y.astype(np.int64), g["expected_out0"])
+    assert np.float32(scale) == np.float32(g["expected_out1"])
+    assert zp == int(g["expected_out2"])
