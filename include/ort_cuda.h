@@ -173,6 +173,15 @@ ORT_CUDA_API int ort_cuda_upload_nbits_file(ort_cuda_session* s, const char* nam
                                             int64_t scales_offset, int64_t zp_offset, int64_t K,
                                             int64_t N, int bits, int block_size, int flags);
 
+/* MatMulInteger weight (the int8 dynamic-quantisation path of
+ * opMatMulInteger, lib/src/onnx_qlinear_ops.dart:26-79): B [K x N] row-major
+ * bytes, int8 when b_signed else uint8; zero points b_zp (same type, host)
+ * scalar (b_zp_len 1) or per column (N), or NULL.  Packed once, K-major with
+ * per-column sums, like the reference's prepacked Gemm B. */
+ORT_CUDA_API int ort_cuda_upload_int8(ort_cuda_session* s, const char* name, const void* B,
+                                      int64_t K, int64_t N, int b_signed, const void* b_zp,
+                                      int64_t b_zp_len);
+
 /* Releases one weight. */
 ORT_CUDA_API int ort_cuda_drop_weight(ort_cuda_session* s, const char* name);
 
@@ -263,6 +272,27 @@ ORT_CUDA_API int ort_cuda_graph_drop(ort_cuda_session* s, int graph_id);
  * whose one CPU kernel has no plans (lib/src/onnx_qlinear_ops.dart:114). */
 ORT_CUDA_API int ort_cuda_gemv_plan_get(ort_cuda_session* s, const char* name, int M, int* plan);
 ORT_CUDA_API int ort_cuda_gemv_plan_set(ort_cuda_session* s, const char* name, int M, int plan);
+
+/* MatMulInteger: Y[M x N] (int32) = (A - a_zp) . (B - b_zp) over the
+ * uploaded weight `name`, as opMatMulInteger (lib/src/onnx_qlinear_ops.dart:
+ * 26-79) computes it (the reference keeps int64; int32 holds every result for
+ * K <= 33025, ONNX's int32 output type).  A [M x K] bytes, int8 when
+ * a_signed else uint8 (the output of DynamicQuantizeLinear); a_zp of A's type,
+ * scalar (a_zp_len 1) or per row (M), or NULL.  A, a_zp and Y are device
+ * pointers (stream-ordered) unless ORT_CUDA_HOST_IO is set. */
+ORT_CUDA_API int ort_cuda_matmul_integer(ort_cuda_session* s, const char* name, const void* A,
+                                         int64_t M, int a_signed, const void* a_zp,
+                                         int64_t a_zp_len, int32_t* Y, int flags);
+
+/* DynamicQuantizeLinear (opDynamicQuantizeLinear, lib/src/onnx_ops.dart:
+ * 2556-2580) of X[n] fp32: Y[n] uint8, *scale fp32, *zp uint8, with the
+ * reference's range, float32 rounding and round-half-even steps (defined for
+ * finite X; the reference raises on inf or NaN).  The device half of the int8
+ * path ahead of ort_cuda_matmul_integer; all pointers device (stream-ordered)
+ * unless ORT_CUDA_HOST_IO is set. */
+ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const float* X, int64_t n,
+                                                  uint8_t* Y, float* scale, uint8_t* zp,
+                                                  int flags);
 
 /* ArgMax (or, with ORT_CUDA_ARG_MIN, ArgMin) over the last axis of X, a
  * [rows x cols] fp32 matrix with row stride ldx: out[r] is the int64 index

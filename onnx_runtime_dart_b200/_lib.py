@@ -84,6 +84,9 @@ SIGNATURES = {
     "ort_cuda_gemv_plan_get": (_int, [_vp, _cp, _int, ctypes.POINTER(_int)]),
     "ort_cuda_gemv_plan_set": (_int, [_vp, _cp, _int, _int]),
     "ort_cuda_argmax": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _int]),
+    "ort_cuda_upload_int8": (_int, [_vp, _cp, _vp, _i64, _i64, _int, _vp, _i64]),
+    "ort_cuda_dynamic_quantize_linear": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _int]),
+    "ort_cuda_matmul_integer": (_int, [_vp, _cp, _vp, _i64, _int, _vp, _i64, _vp, _int]),
     "ort_cuda_launch_count": (_int, [_vp, ctypes.POINTER(_i64)]),
     "ort_cuda_graph_begin": (_int, [_vp]),
     "ort_cuda_graph_end": (_int, [_vp, ctypes.POINTER(_int)]),

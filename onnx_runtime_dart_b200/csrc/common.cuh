@@ -32,7 +32,7 @@ int cuda_fail(cudaError_t e, const char* what);
   } while (0)
 
 // ---- weights -------------------------------------------------------------
-enum WeightKind { W_NBITS = 1, W_DENSE = 2 };
+enum WeightKind { W_NBITS = 1, W_DENSE = 2, W_INT8 = 3 };
 
 // One uploaded initializer, resident for the session.  For an N-sharded
 // session only this rank's columns [n0, n0 + nl) are stored.
@@ -65,6 +65,14 @@ struct Weight {
   int64_t w16_rows = 0, w16_k = 0;
   int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
   uint32_t* sz16 = nullptr;  // nbits f16 MMA: per-(blk,col) {1024 + z, scale * 2^-col_exp} as fp16
+  // MatMulInteger weight (W_INT8): this rank's columns K-major [nl][kpitch]
+  // (kpitch = K rounded up to 16), their column sums and zero points (int32)
+  uint8_t* Wi8 = nullptr;
+  int64_t kpitch = 0;
+  int i8_signed = 0;
+  int32_t* colsum = nullptr;
+  int32_t* bzp = nullptr;  // [nl], or null without zero points
+  CUtensorMap tmW8;
   // decode GEMV: the plan (candidate index) timing chose for each M in 1..8
   int8_t gemv_plan[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
 };
@@ -121,6 +129,9 @@ struct ort_cuda_session {
   // returns the tickets it used to zero
   void* argscratch = nullptr;
   int64_t arg_rows_cap = 0, arg_cand_cap = 0;
+  // DynamicQuantizeLinear scratch (ticket, scale and zero point, per-CTA
+  // ranges); zeroed once, every call returns the ticket to zero
+  void* dqscratch = nullptr;
   // N-sharded sessions: peer-memory exchange of Y (csrc/p2p.cu).  xbuf holds
   // a 256-byte flag area (8 peer flags, epoch counter, CTA counter) then two
   // halves of xcap floats; xpeer[r] is rank r's xbuf mapped into this
@@ -231,6 +242,18 @@ size_t argminmax_candidate_bytes();
 int launch_argminmax(const float* X, int64_t rows, int64_t cols, int64_t ldx, bool is_min,
                      bool last, int64_t* out, unsigned* tickets, void* candidates,
                      cudaStream_t st, int64_t* launches);
+// MatMulInteger (int32 Y[M][ldy] over this rank's columns) on tensor cores;
+// A rows 16-byte aligned with lda % 16 == 0; rowsum holds M int32 when the
+// weight has zero points.
+// DynamicQuantizeLinear of X[n] into Y[n] (uint8), *scale, *zp (device)
+size_t dynamic_quant_scratch_bytes(int sm_count);
+int launch_dynamic_quant(const float* X, int64_t n, uint8_t* Y, float* scale, uint8_t* zp,
+                         void* scratch, int sm_count, cudaStream_t st, int64_t* launches);
+int prepare_int8_tc(Weight& w);
+int launch_matmul_i8(const Weight& w, const uint8_t* A, int64_t lda, int64_t M, int a_signed,
+                     const uint8_t* azp, int64_t az_len, int32_t* Y, int64_t ldy,
+                     int32_t* rowsum, int* err, int sm_count, cudaStream_t st,
+                     int64_t* launches);
 int launch_permute_nibbles(const uint32_t* in, uint32_t* out, int64_t nwords, cudaStream_t st,
                            int64_t* launches);
 int launch_half_to_float(const uint16_t* h, float* out, int64_t n, cudaStream_t st,

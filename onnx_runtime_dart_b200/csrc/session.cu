@@ -125,7 +125,8 @@ bool is_pinned_host(const void* p) {
 }
 
 int free_weight(ortc::Weight& w) {
-  void* ptrs[] = {w.B, w.scales, w.scales16, w.zp, w.W, w.W16, w.col_exp, w.sz16};
+  void* ptrs[] = {w.B, w.scales, w.scales16, w.zp, w.W, w.W16, w.col_exp, w.sz16,
+                  w.Wi8, w.colsum, w.bzp};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   w = ortc::Weight();
@@ -424,6 +425,7 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->ws) cudaFree(s->ws);
   if (s->kscratch) cudaFree(s->kscratch);
   if (s->argscratch) cudaFree(s->argscratch);
+  if (s->dqscratch) cudaFree(s->dqscratch);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second.exec);
@@ -773,6 +775,67 @@ ORT_CUDA_API int ort_cuda_upload_nbits_file(ort_cuda_session* s, const char* nam
   return rc;
 }
 
+ORT_CUDA_API int ort_cuda_upload_int8(ort_cuda_session* s, const char* name, const void* B,
+                                      int64_t K, int64_t N, int b_signed, const void* b_zp,
+                                      int64_t b_zp_len) {
+  ORTC_CHECK(s && name && B, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(K > 0 && N > 0 && K < (1ll << 30) && N < (1ll << 31), ORT_CUDA_ERR_INVALID_ARG,
+             "MatMulInteger: K and N must be positive");
+  ORTC_CHECK(b_zp == nullptr || b_zp_len == 1 || b_zp_len == N, ORT_CUDA_ERR_UNSUPPORTED,
+             "MatMulInteger: b_zp must be scalar or per-column [N]");
+  DeviceGuard g(s->device);
+  Weight w;
+  w.kind = W_INT8;
+  w.K = K;
+  w.N = N;
+  shard_cols(N, s->rank, s->world, &w.n0, &w.nl, &w.ns);
+  w.i8_signed = b_signed ? 1 : 0;
+  w.kpitch = (K + 15) / 16 * 16;
+  const int64_t nl = w.nl;
+  auto cleanup = [&](int rc) {
+    free_weight(w);
+    return rc;
+  };
+  if (nl > 0) {
+    // B [K][N] -> this rank's columns K-major, with their sums
+    const uint8_t* b = static_cast<const uint8_t*>(B);
+    std::vector<uint8_t> t((size_t)(nl * w.kpitch), 0);
+    std::vector<int32_t> cs((size_t)nl, 0), zp;
+    for (int64_t k = 0; k < K; k++) {
+      const uint8_t* row = b + k * N + w.n0;
+      for (int64_t c = 0; c < nl; c++) {
+        t[(size_t)(c * w.kpitch + k)] = row[c];
+        cs[(size_t)c] += b_signed ? (int32_t)(int8_t)row[c] : (int32_t)row[c];
+      }
+    }
+    if (b_zp) {
+      const uint8_t* z = static_cast<const uint8_t*>(b_zp);
+      zp.resize((size_t)nl);
+      for (int64_t c = 0; c < nl; c++) {
+        const uint8_t v = z[b_zp_len == 1 ? 0 : w.n0 + c];
+        zp[(size_t)c] = b_signed ? (int32_t)(int8_t)v : (int32_t)v;
+      }
+    }
+    cudaError_t e = cudaMalloc(&w.Wi8, t.size());
+    if (e == cudaSuccess) e = cudaMemcpy(w.Wi8, t.data(), t.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&w.colsum, cs.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(w.colsum, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && b_zp) e = cudaMalloc(&w.bzp, zp.size() * 4);
+    if (e == cudaSuccess && b_zp)
+      e = cudaMemcpy(w.bzp, zp.data(), zp.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "MatMulInteger weight upload"));
+    const int rc = prepare_int8_tc(w);
+    if (rc) return cleanup(rc);
+  }
+  auto it = s->weights.find(name);
+  if (it != s->weights.end()) {
+    free_weight(it->second);
+    s->weights.erase(it);
+  }
+  s->weights.emplace(name, w);
+  return ORT_CUDA_OK;
+}
+
 ORT_CUDA_API int ort_cuda_upload_dense(ort_cuda_session* s, const char* name, const float* B,
                                        int64_t rows, int64_t cols, int trans_b) {
   ORTC_CHECK(s && name && B, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
@@ -965,6 +1028,42 @@ ORT_CUDA_API int ort_cuda_argmax(ort_cuda_session* s, const float* X, int64_t ro
   return bounded_sync(s);
 }
 
+ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const float* X, int64_t n,
+                                                  uint8_t* Y, float* scale, uint8_t* zp,
+                                                  int flags) {
+  ORTC_CHECK(s && X && Y && scale && zp && n >= 0, ORT_CUDA_ERR_INVALID_ARG, "bad argument");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  DeviceGuard g(s->device);
+  if (!s->dqscratch) {
+    ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+               "a buffer would grow while a CUDA graph is being captured; run every "
+               "operation of the graph once before capturing it");
+    const size_t bytes = dynamic_quant_scratch_bytes(s->sm_count);
+    ORTC_CUDA(cudaMalloc(&s->dqscratch, bytes));
+    ORTC_CUDA(cudaMemsetAsync(s->dqscratch, 0, bytes, s->stream));
+  }
+  if (!host)
+    return launch_dynamic_quant(X, n, Y, scale, zp, s->dqscratch, s->sm_count, s->stream,
+                                &s->launches);
+  const size_t xb = (size_t)n * 4, off_y = (xb + 255) & ~(size_t)255;
+  const size_t off_s = (off_y + (size_t)n + 255) & ~(size_t)255;
+  int rc = ensure_ws(s, off_s + 256);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(s->ws);
+  ORTC_CUDA(cudaMemcpyAsync(ws, X, xb, cudaMemcpyHostToDevice, s->stream));
+  rc = launch_dynamic_quant(reinterpret_cast<float*>(ws), n, reinterpret_cast<uint8_t*>(ws + off_y),
+                            reinterpret_cast<float*>(ws + off_s),
+                            reinterpret_cast<uint8_t*>(ws + off_s + 16), s->dqscratch,
+                            s->sm_count, s->stream, &s->launches);
+  if (rc) return rc;
+  ORTC_CUDA(cudaMemcpyAsync(Y, ws + off_y, (size_t)n, cudaMemcpyDeviceToHost, s->stream));
+  ORTC_CUDA(cudaMemcpyAsync(scale, ws + off_s, 4, cudaMemcpyDeviceToHost, s->stream));
+  ORTC_CUDA(cudaMemcpyAsync(zp, ws + off_s + 16, 1, cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
+}
+
 // ---- the hot ops --------------------------------------------------------------
 
 }  // extern "C"
@@ -981,8 +1080,8 @@ size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 // all-gathers across ranks, writes back.  `compute` gets device A, C, the
 // local output pointer and its leading dimension.
 template <typename F>
-int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems, const float* C,
-           int64_t c_elems, float* Y, int64_t M, int flags, F&& compute) {
+int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, const void* C,
+           size_t c_bytes, float* Y, int64_t M, int flags, F&& compute) {
   const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
@@ -992,9 +1091,9 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
   size_t off = 0;
   if (host) {
     L.a = off;
-    off += al256((size_t)a_elems * 4);
+    off += al256(a_bytes);
     L.c = off;
-    off += al256((size_t)c_elems * 4);
+    off += al256(c_bytes);
     L.y = off;
     off += al256((size_t)(M * N) * 4);
   }
@@ -1008,19 +1107,19 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
   int rc = ensure_ws(s, L.total);
   if (rc) return rc;
   char* ws = (char*)s->ws;
-  const float* dA = A;
-  const float* dC = C;
+  const float* dA = static_cast<const float*>(A);
+  const float* dC = static_cast<const float*>(C);
   float* dY = Y;
   bool y_pinned = false;
   if (host) {
-    size_t pin_need = (size_t)(a_elems + c_elems + M * N) * 4 + 512;
+    size_t pin_need = a_bytes + c_bytes + (size_t)(M * N) * 4 + 768;
     rc = ensure_pinned(s, pin_need);
     if (rc) return rc;
-    rc = stage_in(s, ws + L.a, A, (size_t)a_elems * 4, 0);
+    rc = stage_in(s, ws + L.a, A, a_bytes, 0);
     if (rc) return rc;
     dA = (const float*)(ws + L.a);
-    if (C && c_elems) {
-      rc = stage_in(s, ws + L.c, C, (size_t)c_elems * 4, al256((size_t)a_elems * 4));
+    if (C && c_bytes) {
+      rc = stage_in(s, ws + L.c, C, c_bytes, al256(a_bytes));
       if (rc) return rc;
       dC = (const float*)(ws + L.c);
     }
@@ -1048,7 +1147,7 @@ int run_op(ort_cuda_session* s, const Weight& w, const float* A, int64_t a_elems
       ORTC_CUDA(cudaMemcpyAsync(Y, dY, yb, cudaMemcpyDeviceToHost, s->stream));
       return bounded_sync(s);
     }
-    const size_t pin_y = al256((size_t)(a_elems + c_elems) * 4 + 256);
+    const size_t pin_y = al256(al256(a_bytes) + c_bytes + 256);
     ORTC_CUDA(cudaMemcpyAsync((char*)s->pinned + pin_y, dY, yb, cudaMemcpyDeviceToHost,
                               s->stream));
     rc = bounded_sync(s);
@@ -1077,7 +1176,7 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
   const int mode = mode_of(s, flags);
   ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
   DeviceGuard g(s->device);
-  return run_op(s, w, A, M * w.K, nullptr, 0, Y, M, flags,
+  return run_op(s, w, A, (size_t)(M * w.K) * 4, nullptr, 0, Y, M, flags,
                 [&](const float* dA, const float*, float* yl, int64_t ldy) -> int {
                   if (mode == ORT_CUDA_MODE_STRICT)
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
@@ -1130,6 +1229,58 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                 });
 }
 
+}  // extern "C"
+
+static int matmul_integer_op(ort_cuda_session* s, const char* name, const void* A, int64_t M,
+                             int a_signed, const void* a_zp, int64_t a_zp_len, int32_t* Y,
+                             int flags) {
+  ORTC_CHECK(s && name && A && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 0 && M < (1ll << 30), ORT_CUDA_ERR_INVALID_ARG, "bad M");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  const Weight& w = it->second;
+  ORTC_CHECK(w.kind == W_INT8, ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + name + "' is not a MatMulInteger weight");
+  ORTC_CHECK(a_zp == nullptr || a_zp_len == 1 || a_zp_len == M, ORT_CUDA_ERR_UNSUPPORTED,
+             "MatMulInteger: a_zp must be scalar or per-row [M]");
+  if (M == 0) return ORT_CUDA_OK;
+  DeviceGuard g(s->device);
+  const size_t zbytes = a_zp ? (size_t)a_zp_len : 0;
+  return run_op(s, w, A, (size_t)(M * w.K), a_zp, zbytes, reinterpret_cast<float*>(Y), M, flags,
+                [&](const float* dA, const float* dC, float* yl, int64_t ldy) -> int {
+                  const uint8_t* a8 = reinterpret_cast<const uint8_t*>(dA);
+                  int64_t lda = w.K;
+                  // A rows 16-byte aligned for TMA, padded copy otherwise;
+                  // then the row sums the zero-point correction needs
+                  const bool pad = (w.K % 16) != 0 || (reinterpret_cast<uintptr_t>(a8) & 15);
+                  const size_t pad_bytes = pad ? (size_t)(M * w.kpitch) : 0;
+                  int rc = ensure_kscratch(s, ((pad_bytes + 255) & ~(size_t)255) + (size_t)M * 4);
+                  if (rc) return rc;
+                  if (pad) {
+                    ORTC_CUDA(cudaMemcpy2DAsync(s->kscratch, (size_t)w.kpitch, a8, (size_t)w.K,
+                                                (size_t)w.K, (size_t)M, cudaMemcpyDeviceToDevice,
+                                                s->stream));
+                    a8 = static_cast<const uint8_t*>(s->kscratch);
+                    lda = w.kpitch;
+                  }
+                  int32_t* rowsum = reinterpret_cast<int32_t*>(
+                      static_cast<char*>(s->kscratch) + ((pad_bytes + 255) & ~(size_t)255));
+                  return launch_matmul_i8(w, a8, lda, M, a_signed ? 1 : 0,
+                                          reinterpret_cast<const uint8_t*>(dC), a_zp_len,
+                                          reinterpret_cast<int32_t*>(yl), ldy, rowsum,
+                                          s->err_dev, s->sm_count, s->stream, &s->launches);
+                });
+}
+
+extern "C" {
+
+ORT_CUDA_API int ort_cuda_matmul_integer(ort_cuda_session* s, const char* name, const void* A,
+                                         int64_t M, int a_signed, const void* a_zp,
+                                         int64_t a_zp_len, int32_t* Y, int flags) {
+  return matmul_integer_op(s, name, A, M, a_signed, a_zp, a_zp_len, Y, flags);
+}
+
 static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64_t M,
                     const float* C, int64_t c_rows, int64_t c_cols, float alpha, float beta,
                     float* Y, int flags) {
@@ -1154,7 +1305,8 @@ static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64
   ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
   const bool transA = (flags & ORT_CUDA_TRANS_A) != 0;
   DeviceGuard g(s->device);
-  return run_op(s, w, A, M * w.K, C, C ? c_rows * c_cols : 0, Y, M, flags,
+  return run_op(s, w, A, (size_t)(M * w.K) * 4, C, C ? (size_t)(c_rows * c_cols) * 4 : 0, Y, M,
+                flags,
                 [&](const float* dA, const float* dC, float* yl, int64_t ldy) -> int {
                   const bool mma = mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16;
                   if (mma && mma_supported_shape(M, w.K))

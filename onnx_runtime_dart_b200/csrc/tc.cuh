@@ -70,6 +70,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);          // M / 16
 }
 
+// kind::i8 instruction descriptor with the signedness of each operand
+// (format 0: unsigned 8-bit, 1: signed 8-bit), s32 accumulator, K-major.
+__host__ __device__ constexpr uint32_t idesc_i8_signs(int a_signed, int b_signed, int M, int N) {
+  return (2u << 4)                              // D format: S32
+         | ((uint32_t)(a_signed & 1) << 7)      // A format
+         | ((uint32_t)(b_signed & 1) << 10)     // B format
+         | ((uint32_t)(N >> 3) << 17)           // N / 8
+         | ((uint32_t)(M >> 4) << 24);          // M / 16
+}
+
 // One lane of a converged warp (elect.sync); the MMA issuer uses it so the
 // warp issues tcgen05.mma from a uniform context.
 __device__ __forceinline__ bool elect_one() {
@@ -102,6 +112,17 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] x B[smem]^T, 8-bit integer operands, s32 accumulate.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

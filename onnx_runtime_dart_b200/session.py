@@ -222,6 +222,78 @@ class CudaSession:
             "ort_cuda_upload_nbits_file")
         self.weights[name] = ("nbits", k, n)
 
+    def upload_int8(self, name: str, b: np.ndarray, b_zp=None) -> None:
+        """MatMulInteger weight B [K, N] (int8 or uint8) with optional zero
+        points (scalar or per column, B's type)."""
+        b = np.ascontiguousarray(b)
+        if b.dtype not in (np.int8, np.uint8) or b.ndim != 2:
+            raise ValueError("MatMulInteger: B must be a 2-D int8 or uint8 array")
+        zp = None if b_zp is None else np.ascontiguousarray(b_zp, dtype=b.dtype).reshape(-1)
+        k, n = b.shape
+        check(_lib.load().ort_cuda_upload_int8(self.handle, name.encode(), b.ctypes.data, k, n,
+                                               int(b.dtype == np.int8), _ptr(zp),
+                                               0 if zp is None else zp.size),
+              "ort_cuda_upload_int8")
+        self.weights[name] = ("int8", k, n)
+
+    def matmul_integer(self, name: str, a, a_zp=None):
+        """Y = (A - a_zp) . (B - b_zp) as int32 (opMatMulInteger).  A numpy
+        array (host, synchronous) gives numpy; a torch CUDA tensor (with a_zp
+        a torch CUDA tensor or None) gives a torch int32 tensor."""
+        kind, k, n = self.weights[name]
+        if kind != "int8":
+            raise ValueError(f"weight '{name}' is not a MatMulInteger weight")
+        shape = tuple(a.shape)
+        if shape[-1] != k:
+            raise ValueError(f"MatMulInteger: A last dim {shape[-1]} != K {k}")
+        m = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        L = _lib.load()
+        if hasattr(a, "data_ptr"):
+            import torch
+            signed = a.dtype == torch.int8
+            a = a.contiguous()
+            zp = None if a_zp is None else a_zp.reshape(-1).contiguous()
+            y = torch.empty(shape[:-1] + (n,), dtype=torch.int32, device=a.device)
+            check(L.ort_cuda_matmul_integer(self.handle, name.encode(), a.data_ptr(), m,
+                                            int(signed), 0 if zp is None else zp.data_ptr(),
+                                            0 if zp is None else zp.numel(), y.data_ptr(), 0),
+                  "ort_cuda_matmul_integer")
+            return y
+        a = np.ascontiguousarray(a)
+        if a.dtype not in (np.int8, np.uint8):
+            raise ValueError("MatMulInteger: A must be int8 or uint8")
+        zp = None if a_zp is None else np.ascontiguousarray(a_zp, dtype=a.dtype).reshape(-1)
+        y = np.empty(shape[:-1] + (n,), np.int32)
+        check(L.ort_cuda_matmul_integer(self.handle, name.encode(), a.ctypes.data, m,
+                                        int(a.dtype == np.int8), _ptr(zp),
+                                        0 if zp is None else zp.size, y.ctypes.data,
+                                        _lib.HOST_IO), "ort_cuda_matmul_integer")
+        return y
+
+    def dynamic_quantize_linear(self, x):
+        """(y uint8, scale fp32, zero point uint8) of opDynamicQuantizeLinear.
+        A torch CUDA tensor gives torch tensors on its device (stream-ordered);
+        a numpy array gives (numpy uint8 array, float, int)."""
+        L = _lib.load()
+        if hasattr(x, "data_ptr"):
+            import torch
+            x = x.contiguous().float()
+            y = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+            sc = torch.empty((), dtype=torch.float32, device=x.device)
+            zp = torch.empty((), dtype=torch.uint8, device=x.device)
+            check(L.ort_cuda_dynamic_quantize_linear(self.handle, x.data_ptr(), x.numel(),
+                                                     y.data_ptr(), sc.data_ptr(), zp.data_ptr(),
+                                                     0), "ort_cuda_dynamic_quantize_linear")
+            return y, sc, zp
+        a = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(a.shape, np.uint8)
+        sc = np.zeros(1, np.float32)
+        zp = np.zeros(1, np.uint8)
+        check(L.ort_cuda_dynamic_quantize_linear(self.handle, a.ctypes.data, a.size, y.ctypes.data,
+                                                 sc.ctypes.data, zp.ctypes.data, _lib.HOST_IO),
+              "ort_cuda_dynamic_quantize_linear")
+        return y, float(sc[0]), int(zp[0])
+
     def upload_dense(self, name: str, b: np.ndarray, trans_b: bool = False) -> None:
         b = np.ascontiguousarray(b, dtype=np.float32)
         if b.ndim != 2:

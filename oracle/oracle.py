@@ -225,7 +225,10 @@ def matmul_integer(a, b, a_zp=None, b_zp=None) -> np.ndarray:
         raise ValueError("MatMulInteger: b_zp must be scalar or per-column [N]")
     ac = a - (az.reshape(-1, 1) if np.size(az) == m and m != 1 else np.reshape(az, ()))
     bc = b - (np.reshape(bz, ()) if np.size(bz) == 1 else bz)
-    return np.matmul(ac, bc)
+    # every product and partial sum is an integer of magnitude <= 255^2 K,
+    # exact in float64 below 2^53, so the float64 matmul is the exact one
+    assert 255 * 255 * a.shape[-1] < 2 ** 53
+    return np.rint(np.matmul(ac.astype(np.float64), bc.astype(np.float64))).astype(np.int64)
 
 
 def _round_even(v: float) -> int:

@@ -206,3 +206,17 @@ def test_oracle_dynamic_quantize_linear_fixture(golden):
     assert np.array_equal(y.astype(np.int64), g["expected_out0"])
     assert np.float32(scale) == np.float32(g["expected_out1"])
     assert zp == int(g["expected_out2"])
+
+
+def test_oracle_matmul_integer_float64_is_exact():
+    """The float64 form of the MatMulInteger oracle equals exact int64
+    arithmetic at an LLM-sized K with extreme operands."""
+    rng = np.random.default_rng(4)
+    K = 14336
+    a = rng.integers(0, 256, (3, K)).astype(np.uint8)
+    b = rng.integers(-128, 128, (K, 5)).astype(np.int8)
+    a[0] = 255
+    b[:, 0] = -128
+    az, bz = np.array([0], np.uint8), np.array([127], np.int8)
+    want = (a.astype(np.int64) - 0) @ (b.astype(np.int64) - 127)
+    assert np.array_equal(O.matmul_integer(a, b, az, bz), want)
