@@ -261,3 +261,157 @@ def dynamic_quantize_linear(x):
         q = zp if scale == 0 else _round_even(float(np.float32(v / scale))) + zp
         out[k] = 0 if q < 0 else (255 if q > 255 else q)
     return out.reshape(np.shape(x)), np.float32(scale), zp
+
+
+# ---- attention (the decoder step around the MatMulNBits projections) --------
+
+def rotary_embedding(x, position_ids, cos_cache, sin_cache, interleaved: bool = False,
+                     num_heads: int = 0, rotary_dim: int = 0) -> np.ndarray:
+    """RotaryEmbedding, restating opRotaryEmbedding (lib/src/onnx_ops.dart:
+    2121-2172): x [batch, seq, hidden] (or [batch, heads, seq, head]);
+    cos/sin [max_pos, rotary_dim/2] indexed by position_ids [batch, seq] (or
+    [seq], shared); the first rotary_dim features of each head are rotated
+    (GPT-NeoX halves, or GPT-J pairs when interleaved), the rest copied.  Each
+    output is x0*c -/+ x1*s in double, stored to float32, as in the
+    reference."""
+    x = np.asarray(x, np.float32)
+    cos = np.asarray(cos_cache, np.float32)
+    sin = np.asarray(sin_cache, np.float32)
+    pos = np.asarray(position_ids).astype(np.int64)
+    half_rot = cos.shape[-1]
+    rdim = rotary_dim if rotary_dim > 0 else 2 * half_rot
+    if x.ndim == 4:
+        xs = np.transpose(x, (0, 2, 1, 3))  # -> [b, s, h, d]
+    else:
+        b, s, hidden = x.shape
+        head = hidden // num_heads if num_heads > 0 else rdim
+        xs = x.reshape(b, s, hidden // head, head)
+    batch, seq = xs.shape[:2]
+    p = pos.reshape(1, seq) if pos.ndim == 1 else pos.reshape(batch, seq)
+    p = np.broadcast_to(p, (batch, seq))
+    c = cos.reshape(-1, half_rot)[p][:, :, None, :rdim // 2].astype(np.float64)
+    sn = sin.reshape(-1, half_rot)[p][:, :, None, :rdim // 2].astype(np.float64)
+    out = xs.copy()
+    x64 = xs.astype(np.float64)
+    if interleaved:
+        x0, x1 = x64[..., 0:rdim:2], x64[..., 1:rdim:2]
+        out[..., 0:rdim:2] = (x0 * c - x1 * sn).astype(np.float32)
+        out[..., 1:rdim:2] = (x1 * c + x0 * sn).astype(np.float32)
+    else:
+        h = rdim // 2
+        x0, x1 = x64[..., :h], x64[..., h:rdim]
+        out[..., :h] = (x0 * c - x1 * sn).astype(np.float32)
+        out[..., h:rdim] = (x1 * c + x0 * sn).astype(np.float32)
+    if x.ndim == 4:
+        return np.ascontiguousarray(np.transpose(out, (0, 2, 1, 3)))
+    return out.reshape(x.shape)
+
+
+def _softmax_rows(sc64, stored32):
+    """The reference's row softmax after the scale/bias pass
+    (onnx_ops.dart:1604-1621): the maximum is taken over the unrounded double
+    scores, exp(float32 score - max) is stored to float32 while its double
+    value is summed in index order, and each stored exp is multiplied by
+    1/sum (double) and stored to float32."""
+    mx = np.max(sc64, axis=-1, keepdims=True)
+    e = np.exp(stored32.astype(np.float64) - mx)
+    e32 = e.astype(np.float32)
+    total = np.cumsum(e, axis=-1)[..., -1:]
+    return (e32.astype(np.float64) * (1.0 / total)).astype(np.float32)
+
+
+def group_query_attention(q, k, v, num_heads: int, kv_num_heads: int, scale=None,
+                          do_rotary: bool = False, rotary_interleaved: bool = False,
+                          cos_cache=None, sin_cache=None, past_key=None, past_value=None,
+                          attention_bias=None):
+    """GroupQueryAttention (com.microsoft), restating opGroupQueryAttention
+    (lib/src/onnx_ops.dart:1507-1650): q [batch, seq, H*D], k/v [batch, seq,
+    Hkv*D], optional past [batch, Hkv, P, D]; RoPE on q and k at positions
+    P..P+seq-1 when do_rotary; present = past ++ (roped k, raw v); query
+    token i attends causally to keys 0..P+i; scores = QK^T (matmulKernel,
+    fp32) * scale + bias, the reference's row softmax, then P.V
+    (matmulKernel).  Returns (out [batch, seq, H*D], present_key,
+    present_value [batch, Hkv, P+seq, D])."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    batch, seq = q.shape[:2]
+    D = q.shape[2] // num_heads
+    group = num_heads // kv_num_heads
+    P = past_key.shape[2] if past_key is not None and np.ndim(past_key) == 4 else 0
+    T = P + seq
+    if do_rotary:
+        pos = np.arange(P, P + seq, dtype=np.int64).reshape(1, seq)
+        q = rotary_embedding(q, pos, cos_cache, sin_cache, rotary_interleaved, num_heads)
+        k = rotary_embedding(k, pos, cos_cache, sin_cache, rotary_interleaved, kv_num_heads)
+    s = float(scale) if scale is not None else 1.0 / np.sqrt(D)
+    kn = k.reshape(batch, seq, kv_num_heads, D).transpose(0, 2, 1, 3)
+    vn = v.reshape(batch, seq, kv_num_heads, D).transpose(0, 2, 1, 3)
+    if P:
+        pk = np.asarray(past_key, np.float32)
+        pv = np.asarray(past_value, np.float32)
+        present_k = np.concatenate([pk, kn], axis=2)
+        present_v = np.concatenate([pv, vn], axis=2)
+    else:
+        present_k, present_v = np.ascontiguousarray(kn), np.ascontiguousarray(vn)
+    bias = None if attention_bias is None else np.asarray(attention_bias, np.float32)
+    bias_heads = 0 if bias is None else bias.shape[1]
+    out = np.empty((batch, seq, num_heads * D), np.float32)
+    for b in range(batch):
+        for h in range(num_heads):
+            kvh = h // group
+            qh = np.ascontiguousarray(q[b, :, h * D:(h + 1) * D])
+            scores = matmul_kernel(qh, np.ascontiguousarray(present_k[b, kvh].T))
+            probs = np.zeros((seq, T), np.float32)
+            for i in range(seq):
+                last = P + i
+                sc = scores[i, :last + 1].astype(np.float64) * s
+                if bias is not None:
+                    sc = sc + bias[b, h % bias_heads, i, :last + 1].astype(np.float64)
+                probs[i, :last + 1] = _softmax_rows(sc, sc.astype(np.float32))
+            out[b, :, h * D:(h + 1) * D] = matmul_kernel(probs, np.ascontiguousarray(present_v[b, kvh]))
+    return out, np.ascontiguousarray(present_k), np.ascontiguousarray(present_v)
+
+
+def multi_head_attention(q, k, v, num_heads: int, scale=None, attention_bias=None):
+    """MultiHeadAttention (com.microsoft), restating opMultiHeadAttention
+    (lib/src/onnx_ops.dart:1656-1725): q [batch, seq, hidden], k/v [batch,
+    kv_seq, hidden], no mask beyond the optional additive bias [batch,
+    bias_heads, seq, kv_seq]."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    batch, seq, hidden = q.shape
+    D = hidden // num_heads
+    s = float(scale) if scale is not None else 1.0 / np.sqrt(D)
+    bias = None if attention_bias is None else np.asarray(attention_bias, np.float32)
+    out = np.empty_like(q)
+    for b in range(batch):
+        for h in range(num_heads):
+            sl = slice(h * D, (h + 1) * D)
+            scores = matmul_kernel(np.ascontiguousarray(q[b, :, sl]),
+                                   np.ascontiguousarray(k[b, :, sl].T))
+            sc = scores.astype(np.float64) * s
+            if bias is not None:
+                sc = sc + bias[b, h % bias.shape[1]].astype(np.float64)
+            probs = _softmax_rows(sc, sc.astype(np.float32))
+            out[b, :, sl] = matmul_kernel(probs, np.ascontiguousarray(v[b, :, sl]))
+    return out
+
+
+def fused_sdpa(a, b, v, mask, scale: float):
+    """_FusedSDPA, restating opFusedSDPA (lib/src/onnx_ops.dart:1733-1774):
+    s = MatMul(a, b) (b is K already transposed), val = s*scale + mask
+    (mask broadcast numpy-style, stored to float32), exp(val - max) stored,
+    divided by the double sum, then MatMul(s, v).  `scale` is the fused
+    node's float32 attribute (onnx_graph.dart:355-386 folds Div(c) as
+    1/c)."""
+    s = matmul(a, b)
+    m = np.broadcast_to(np.asarray(mask, np.float32), s.shape)
+    val = s.astype(np.float64) * float(scale) + m.astype(np.float64)
+    mx = np.max(val, axis=-1, keepdims=True)
+    e = np.exp(val.astype(np.float32).astype(np.float64) - mx)
+    e32 = e.astype(np.float32)
+    total = np.cumsum(e, axis=-1)[..., -1:]
+    p = (e32.astype(np.float64) / total).astype(np.float32)
+    return matmul(p, v)

@@ -40,6 +40,15 @@ CASES = [
     "matmulinteger_percol_bzp",
     "matmulinteger_u8i8",
     "matmulinteger_batched",
+    # the attention ops around the projections of a decoder step
+    "gqa_causal",
+    "gqa_kvcache",
+    "gqa_kvcache_bias",
+    "gqa_kvcache_rotary",
+    "mha_no_bias",
+    "mha_with_bias",
+    "rotary_embedding",
+    "sdpa_pattern",  # MatMul/Div/Add/Softmax/MatMul, fused to _FusedSDPA
 ]
 
 _ONNX_DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 6: np.int32, 7: np.int64,
@@ -171,7 +180,6 @@ def main(ref_root):
     for case in CASES:
         d = os.path.join(ref_root, "test", "fixtures", case)
         nodes, inits = parse_model(os.path.join(d, "model.onnx"))
-        assert len(nodes) == 1, case
         cj = json.load(open(os.path.join(d, "case.json")))
         arrays = {}
         for k, v in cj["inputs"].items():
@@ -184,11 +192,12 @@ def main(ref_root):
             arrays["expected_" + ok] = arr
             if len(outs) == 1:
                 arrays["expected"] = arr
-        meta = dict(nodes[0])
+        # one node, or (a pattern the reference fuses) the whole node list
+        meta = dict(nodes[0]) if len(nodes) == 1 else {"nodes": nodes, "op_type": "pattern"}
         meta["source"] = f"test/fixtures/{case}"
         arrays["meta"] = np.array(json.dumps(meta))
         np.savez(os.path.join(out_dir, case + ".npz"), **arrays)
-        print(case, {k: v.shape for k, v in arrays.items()}, meta["attrs"])
+        print(case, {k: v.shape for k, v in arrays.items()}, meta.get("attrs"))
 
 
 if __name__ == "__main__":

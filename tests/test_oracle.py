@@ -220,3 +220,67 @@ def test_oracle_matmul_integer_float64_is_exact():
     az, bz = np.array([0], np.uint8), np.array([127], np.int8)
     want = (a.astype(np.int64) - 0) @ (b.astype(np.int64) - 127)
     assert np.array_equal(O.matmul_integer(a, b, az, bz), want)
+
+
+@pytest.mark.parametrize("case", ["gqa_causal", "gqa_kvcache", "gqa_kvcache_bias",
+                                  "gqa_kvcache_rotary"])
+def test_oracle_group_query_attention_fixtures(golden, case):
+    """GroupQueryAttention restatement (causal, KV cache, additive bias,
+    RoPE) against the reference's ORT fixtures: output and present K/V."""
+    from tests.attn_fixtures import gqa_args
+    g = golden(case)
+    q, k, v, kw = gqa_args(g)
+    out, pk, pv = O.group_query_attention(q, k, v, **kw)
+    _fixture_check(g["expected_out0"], out)
+    outs = [key for key in g if key.startswith("expected_") and key != "expected_out0"]
+    if len(outs) == 2:
+        _fixture_check(g[sorted(outs)[0]], pk)
+        _fixture_check(g[sorted(outs)[1]], pv)
+
+
+@pytest.mark.parametrize("case", ["mha_no_bias", "mha_with_bias"])
+def test_oracle_multi_head_attention_fixtures(golden, case):
+    from tests.attn_fixtures import mha_args
+    g = golden(case)
+    q, k, v, kw = mha_args(g)
+    _fixture_check(g["expected"], O.multi_head_attention(q, k, v, **kw))
+
+
+def test_oracle_rotary_embedding_fixture(golden):
+    from tests.attn_fixtures import rotary_args
+    g = golden("rotary_embedding")
+    args, kw = rotary_args(g)
+    _fixture_check(g["expected"], O.rotary_embedding(*args, **kw))
+
+
+def test_oracle_fused_sdpa_fixture(golden):
+    """The MatMul/Div/Add/Softmax/MatMul pattern as the reference fuses it
+    (scale = float32(1/c), mask broadcast over heads and rows)."""
+    from tests.attn_fixtures import sdpa_args
+    g = golden("sdpa_pattern")
+    a, b, v, mask, scale = sdpa_args(g)
+    _fixture_check(g["expected"], O.fused_sdpa(a, b, v, mask, scale))
+
+
+def test_oracle_gqa_present_is_past_then_current():
+    """present K/V = past followed by the step's (roped) K and raw V, and a
+    decode step over the present cache equals the last row of the same
+    sequence run as one prefill (the causal mask makes them the same
+    computation)."""
+    rng = np.random.default_rng(3)
+    H, Hkv, D, S = 4, 2, 8, 6
+    q = rng.standard_normal((1, S, H * D)).astype(np.float32)
+    k = rng.standard_normal((1, S, Hkv * D)).astype(np.float32)
+    v = rng.standard_normal((1, S, Hkv * D)).astype(np.float32)
+    cos = rng.standard_normal((16, D // 2)).astype(np.float32)
+    sin = rng.standard_normal((16, D // 2)).astype(np.float32)
+    full, pk, pv = O.group_query_attention(q, k, v, H, Hkv, do_rotary=True, cos_cache=cos,
+                                           sin_cache=sin)
+    part, pk1, pv1 = O.group_query_attention(q[:, :S - 1], k[:, :S - 1], v[:, :S - 1], H, Hkv,
+                                             do_rotary=True, cos_cache=cos, sin_cache=sin)
+    step, pk2, pv2 = O.group_query_attention(q[:, S - 1:], k[:, S - 1:], v[:, S - 1:], H, Hkv,
+                                             do_rotary=True, cos_cache=cos, sin_cache=sin,
+                                             past_key=pk1, past_value=pv1)
+    assert np.array_equal(pk2, pk) and np.array_equal(pv2, pv)
+    assert np.allclose(step[0, 0], full[0, S - 1], rtol=1e-6, atol=1e-6)
+    assert np.allclose(part, full[:, :S - 1], rtol=1e-6, atol=1e-6)
