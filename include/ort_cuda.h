@@ -306,6 +306,78 @@ ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const flo
 ORT_CUDA_API int ort_cuda_argmax(ort_cuda_session* s, const float* X, int64_t rows, int64_t cols,
                                  int64_t ldx, int64_t* out, int flags);
 
+/* ---- attention of a decoder step --------------------------------------
+ * fp32 on the device (exact mode's rounding: fp32 dot products, expf, the
+ * reference's double scale step); the device counterparts of the
+ * reference's GroupQueryAttention, MultiHeadAttention, fused SDPA and
+ * RotaryEmbedding cases of OnnxGraphExecutor._dispatch
+ * (lib/src/onnx_graph.dart:978-1005, :1029-1033).  Head sizes up to 128.
+ * All pointers are device pointers (stream-ordered) unless ORT_CUDA_HOST_IO
+ * is set.  `scale` <= 0 selects 1/sqrt(head_size) (GQA and MHA). */
+#define ORT_CUDA_ROTARY 0x80              /* GQA do_rotary=1                   */
+#define ORT_CUDA_ROTARY_INTERLEAVED 0x200 /* rotary_interleaved / interleaved=1 */
+#define ORT_CUDA_ROTARY_BHSD 0x400        /* RotaryEmbedding X is [b, h, s, d]  */
+
+/* GroupQueryAttention (opGroupQueryAttention, lib/src/onnx_ops.dart:
+ * 1507-1650): Q [batch, seq, num_heads*head], K/V [batch, seq,
+ * kv_num_heads*head], past K/V [batch, kv_num_heads, past_len, head] (NULL
+ * when past_len is 0); with ORT_CUDA_ROTARY, RoPE from cos/sin caches
+ * [max_pos, rotary_half] at positions past_len..past_len+seq-1 (GPT-J pairs
+ * with ORT_CUDA_ROTARY_INTERLEAVED); query token i attends to keys
+ * 0..past_len+i, plus bias [bias_batch (1 or batch), bias_heads, seq,
+ * past_len+seq] (head h reads bias head h % bias_heads) or NULL.  Writes out
+ * [batch, seq, num_heads*head] and, unless both are NULL, present K/V
+ * [batch, kv_num_heads, past_len+seq, head] = past then this step's (roped)
+ * K and V.  kv_capacity > 0 (device buffers): past and present rows are
+ * kv_capacity apart, and present may be the past buffer itself (only this
+ * step's rows are then written: an in-place KV cache).  softcap and
+ * local_window_size are not supported (the reference raises too). */
+ORT_CUDA_API int ort_cuda_group_query_attention(
+    ort_cuda_session* s, const float* Q, const float* K, const float* V, const float* past_key,
+    const float* past_value, int64_t batch, int64_t seq, int64_t past_len, int num_heads,
+    int kv_num_heads, int64_t head_size, double scale, const float* cos_cache,
+    const float* sin_cache, int64_t rotary_half, int64_t max_pos, const float* bias,
+    int64_t bias_batch, int64_t bias_heads, int64_t kv_capacity, float* out, float* present_key,
+    float* present_value, int flags);
+
+/* MultiHeadAttention (opMultiHeadAttention, lib/src/onnx_ops.dart:
+ * 1656-1725): Q [batch, seq, hidden], K/V [batch, kv_seq, hidden], no causal
+ * mask, optional bias [bias_batch, bias_heads, seq, kv_seq]; out [batch,
+ * seq, hidden]. */
+ORT_CUDA_API int ort_cuda_multi_head_attention(ort_cuda_session* s, const float* Q,
+                                               const float* K, const float* V, int64_t batch,
+                                               int64_t seq, int64_t kv_seq, int num_heads,
+                                               int64_t hidden, double scale, const float* bias,
+                                               int64_t bias_batch, int64_t bias_heads, float* out,
+                                               int flags);
+
+/* _FusedSDPA (opFusedSDPA, lib/src/onnx_ops.dart:1733-1774; the
+ * MatMul -> Div/Mul -> Add -> Softmax -> MatMul pattern that
+ * onnx_graph.dart:332-386 fuses): out = softmax(A.B * scale + mask) . V with
+ * A [n0, n1, seq, head], B [n0, n1, head, kv_seq] (K already transposed),
+ * V [n0, n1, kv_seq, v_head]; mask element (i0, i1, r, c) at
+ * mask[i0*ms[0] + i1*ms[1] + r*ms[2] + c*ms[3]] (stride 0 broadcasts; the
+ * host array mask_strides holds ms), or mask NULL. */
+ORT_CUDA_API int ort_cuda_fused_sdpa(ort_cuda_session* s, const float* A, const float* B,
+                                     const float* V, const float* mask,
+                                     const int64_t* mask_strides, int64_t n0, int64_t n1,
+                                     int64_t seq, int64_t kv_seq, int64_t head_size,
+                                     int64_t v_head_size, double scale, float* out, int flags);
+
+/* RotaryEmbedding (opRotaryEmbedding, lib/src/onnx_ops.dart:2121-2172): X
+ * [batch, seq, heads*head] (or [batch, heads, seq, head] with
+ * ORT_CUDA_ROTARY_BHSD), int64 position_ids [batch, seq] (pos_per_batch 1)
+ * or [seq] shared, cos/sin [max_pos, rotary_half]; the first rotary_dim
+ * features of each head (0: 2*rotary_half) are rotated, the rest copied.
+ * A position outside [0, max_pos) yields NaN for that row (the reference
+ * raises). */
+ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
+                                           const int64_t* position_ids, int pos_per_batch,
+                                           const float* cos_cache, const float* sin_cache,
+                                           int64_t max_pos, int64_t rotary_half, int64_t batch,
+                                           int64_t seq, int64_t heads, int64_t head_size,
+                                           int64_t rotary_dim, float* Y, int flags);
+
 /* Kernel launches issued by this session since it was opened (all of
  * them this library's own kernels; a graph launch counts the kernels it
  * holds). */

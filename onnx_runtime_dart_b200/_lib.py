@@ -47,6 +47,9 @@ ZP_FLAT = 0x0
 ZP_PER_COLUMN = 0x10
 ARG_MIN = 0x20  # ort_cuda_argmax flags
 ARG_SELECT_LAST = 0x40
+ROTARY = 0x80  # attention flags
+ROTARY_INTERLEAVED = 0x200
+ROTARY_BHSD = 0x400
 
 # Every symbol include/ort_cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -88,6 +91,15 @@ SIGNATURES = {
     "ort_cuda_dynamic_quantize_linear": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _int]),
     "ort_cuda_matmul_integer": (_int, [_vp, _cp, _vp, _i64, _int, _vp, _i64, _vp, _int]),
     "ort_cuda_launch_count": (_int, [_vp, ctypes.POINTER(_i64)]),
+    "ort_cuda_group_query_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                              _int, _int, _i64, ctypes.c_double, _vp, _vp, _i64,
+                                              _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _int]),
+    "ort_cuda_multi_head_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _i64,
+                                             ctypes.c_double, _vp, _i64, _i64, _vp, _int]),
+    "ort_cuda_fused_sdpa": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                   _i64, ctypes.c_double, _vp, _int]),
+    "ort_cuda_rotary_embedding": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _i64, _i64, _i64, _i64,
+                                         _i64, _i64, _i64, _vp, _int]),
     "ort_cuda_graph_begin": (_int, [_vp]),
     "ort_cuda_graph_end": (_int, [_vp, ctypes.POINTER(_int)]),
     "ort_cuda_graph_launch": (_int, [_vp, _int]),

@@ -132,6 +132,10 @@ struct ort_cuda_session {
   // DynamicQuantizeLinear scratch (ticket, scale and zero point, per-CTA
   // ranges); zeroed once, every call returns the ticket to zero
   void* dqscratch = nullptr;
+  // attention split-key scratch: tickets (zeroed when allocated, returned
+  // to zero by every call) then partials
+  void* attnscratch = nullptr;
+  size_t attn_bytes = 0;
   // N-sharded sessions: peer-memory exchange of Y (csrc/p2p.cu).  xbuf holds
   // a 256-byte flag area (8 peer flags, epoch counter, CTA counter) then two
   // halves of xcap floats; xpeer[r] is rank r's xbuf mapped into this
@@ -249,6 +253,62 @@ int launch_argminmax(const float* X, int64_t rows, int64_t cols, int64_t ldx, bo
 size_t dynamic_quant_scratch_bytes(int sm_count);
 int launch_dynamic_quant(const float* X, int64_t n, uint8_t* Y, float* scale, uint8_t* zp,
                          void* scratch, int sm_count, cudaStream_t st, int64_t* launches);
+// Attention over one (batch, KV head) sequence per CTA group, in fp32
+// (csrc/attn.cu): the body of GroupQueryAttention, MultiHeadAttention and
+// the fused SDPA pattern.  Element (b, i, h, d) of Q is
+// q[b*qsb + i*qsi + h*qsh + d]; key j of KV head g is a past row
+// (j < past: pk/pv[b*psb + g*psh + j*D + d]) or a row of this call
+// (k[b*ksb + g*ksh + (j-past)*ksj + d*ksd], v[b*vsb + g*vsh + (j-past)*vsj + d]);
+// query head h reads KV head h / group.
+struct AttnArgs {
+  const float* q = nullptr;
+  int64_t qsb = 0, qsi = 0, qsh = 0;
+  const float* k = nullptr;
+  int64_t ksb = 0, ksh = 0, ksj = 0, ksd = 1;
+  const float* v = nullptr;
+  int64_t vsb = 0, vsh = 0, vsj = 0;
+  const float* pk = nullptr;
+  const float* pv = nullptr;
+  int64_t psb = 0, psh = 0;
+  // present K/V (GQA): prk[b*rsb + g*rsh + j*D + d] for j < T; rows j < past
+  // are copied only when write_past (present does not alias past)
+  float* prk = nullptr;
+  float* prv = nullptr;
+  int64_t rsb = 0, rsh = 0;
+  int write_past = 0;
+  // additive bias: bias[b*bsb + (h % bh)*bsh + i*bsi + j*bsj]
+  const float* bias = nullptr;
+  int64_t bsb = 0, bsh = 0, bsi = 0, bsj = 0;
+  int bh = 1;
+  float* out = nullptr;
+  int64_t osb = 0, osi = 0, osh = 0;
+  int batch = 0, seq = 0, heads_kv = 0, group = 1, D = 0, Dv = 0, past = 0, T = 0;
+  // keys j < cached come from pk/pv (normally the past; all keys once a
+  // pre-pass has written this call's rows to the present cache); query
+  // token i is at position past + i either way
+  int cached = -1;
+  int causal = 0;
+  double scale = 1.0;
+  // RoPE of Q (position past+i) and of this call's K rows (position j)
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  int half_rot = 0, interleaved = 0, rotary = 0;
+  // filled by launch_attention
+  int rows_total = 0, nqt = 0, nsplit = 1, vec = 0;
+  float* part = nullptr;
+  unsigned* tickets = nullptr;
+  int* err = nullptr;  // host-mapped error word for a bounded wait that expired
+};
+// Scratch the launch needs (0 when no split of the keys is used); the
+// tickets at its start must be zero on entry and are zero again at exit.
+size_t attention_scratch_bytes(const AttnArgs& a, int sm_count);
+int launch_attention(AttnArgs a, void* scratch, int sm_count, cudaStream_t st, int64_t* launches);
+// RotaryEmbedding of X laid out [batch][seq][heads][head] (x_bhsd = 0) or
+// [batch][heads][seq][head] (1); positions pos[(pos_per_batch ? b : 0)*seq + s]
+int launch_rotary(const float* X, float* Y, const int64_t* pos, int pos_per_batch,
+                  const float* cos, const float* sin, int64_t max_pos, int half_rot, int rdim,
+                  int64_t batch, int64_t seq, int64_t heads, int64_t head, int x_bhsd,
+                  int interleaved, cudaStream_t st, int64_t* launches);
 int prepare_int8_tc(Weight& w);
 int launch_matmul_i8(const Weight& w, const uint8_t* A, int64_t lda, int64_t M, int a_signed,
                      const uint8_t* azp, int64_t az_len, int32_t* Y, int64_t ldy,

@@ -11,6 +11,8 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <climits>
+#include <cmath>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
@@ -426,6 +428,7 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->kscratch) cudaFree(s->kscratch);
   if (s->argscratch) cudaFree(s->argscratch);
   if (s->dqscratch) cudaFree(s->dqscratch);
+  if (s->attnscratch) cudaFree(s->attnscratch);
   if (s->pinned) cudaFreeHost(s->pinned);
   if (s->err_host) cudaFreeHost(s->err_host);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second.exec);
@@ -1062,6 +1065,380 @@ ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const flo
   ORTC_CUDA(cudaMemcpyAsync(scale, ws + off_s, 4, cudaMemcpyDeviceToHost, s->stream));
   ORTC_CUDA(cudaMemcpyAsync(zp, ws + off_s + 16, 1, cudaMemcpyDeviceToHost, s->stream));
   return bounded_sync(s);
+}
+
+// ---- attention of a decoder step -------------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+// Copies for an ORT_CUDA_HOST_IO call: each host input gets a 256-aligned
+// slot in the session workspace, each output a slot copied back afterwards.
+struct HostStage {
+  struct In {
+    const void* src;
+    size_t bytes, off;
+  };
+  struct Out {
+    void* dst;
+    size_t bytes, off;
+  };
+  std::vector<In> ins;
+  std::vector<Out> outs;
+  size_t total = 0;
+  size_t slot(size_t bytes) {
+    const size_t off = total;
+    total += (bytes + 255) & ~(size_t)255;
+    return off;
+  }
+  size_t in(const void* src, size_t bytes) {
+    const size_t off = slot(bytes);
+    if (src && bytes) ins.push_back({src, bytes, off});
+    return off;
+  }
+  size_t out(void* dst, size_t bytes) {
+    const size_t off = slot(bytes);
+    if (dst && bytes) outs.push_back({dst, bytes, off});
+    return off;
+  }
+};
+
+template <typename T>
+T* ws_at(ort_cuda_session* s, size_t off, const void* host) {
+  return host ? reinterpret_cast<T*>(static_cast<char*>(s->ws) + off) : nullptr;
+}
+
+int host_stage_in(ort_cuda_session* s, const HostStage& st) {
+  int rc = ensure_ws(s, st.total + 256);
+  if (rc) return rc;
+  for (const auto& i : st.ins)
+    ORTC_CUDA(cudaMemcpyAsync(static_cast<char*>(s->ws) + i.off, i.src, i.bytes,
+                              cudaMemcpyHostToDevice, s->stream));
+  return ORT_CUDA_OK;
+}
+
+int host_stage_out(ort_cuda_session* s, const HostStage& st) {
+  for (const auto& o : st.outs)
+    ORTC_CUDA(cudaMemcpyAsync(o.dst, static_cast<char*>(s->ws) + o.off, o.bytes,
+                              cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
+}
+
+// Split-key scratch for launch_attention; tickets zero when allocated.
+int run_attention(ort_cuda_session* s, ortc::AttnArgs& a) {
+  const size_t need = ortc::attention_scratch_bytes(a, s->sm_count);
+  if (need > s->attn_bytes) {
+    ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+               "a buffer would grow while a CUDA graph is being captured; run every "
+               "operation of the graph once before capturing it");
+    if (s->attnscratch) {
+      ORTC_CUDA(cudaStreamSynchronize(s->stream));
+      ORTC_CUDA(cudaFree(s->attnscratch));
+      s->attnscratch = nullptr;
+      s->attn_bytes = 0;
+    }
+    const size_t want = std::max<size_t>(need, 1 << 20);
+    ORTC_CUDA(cudaMalloc(&s->attnscratch, want));
+    ORTC_CUDA(cudaMemsetAsync(s->attnscratch, 0, want, s->stream));
+    s->attn_bytes = want;
+  }
+  a.err = s->err_dev;
+  return ortc::launch_attention(a, s->attnscratch, s->sm_count, s->stream, &s->launches);
+}
+
+}  // namespace
+
+extern "C" {
+
+ORT_CUDA_API int ort_cuda_group_query_attention(
+    ort_cuda_session* s, const float* Q, const float* K, const float* V, const float* past_key,
+    const float* past_value, int64_t batch, int64_t seq, int64_t past_len, int num_heads,
+    int kv_num_heads, int64_t head_size, double scale, const float* cos_cache,
+    const float* sin_cache, int64_t rotary_half, int64_t max_pos, const float* bias,
+    int64_t bias_batch, int64_t bias_heads, int64_t kv_capacity, float* out, float* present_key,
+    float* present_value, int flags) {
+  ORTC_CHECK(s && Q && K && V && out, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(batch >= 0 && seq >= 0 && past_len >= 0 && num_heads >= 1 && kv_num_heads >= 1 &&
+                 num_heads % kv_num_heads == 0 && head_size >= 1,
+             ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: need num_heads a multiple of kv_num_heads, sizes >= 0");
+  ORTC_CHECK(head_size <= 128, ORT_CUDA_ERR_UNSUPPORTED,
+             "GroupQueryAttention: head sizes above 128 are not supported");
+  ORTC_CHECK(past_len == 0 || (past_key && past_value), ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: past_len > 0 needs past_key and past_value");
+  ORTC_CHECK((present_key == nullptr) == (present_value == nullptr), ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: give both present outputs or neither");
+  const int64_t T = past_len + seq;
+  ORTC_CHECK(kv_capacity == 0 || kv_capacity >= T, ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: kv_capacity below past_len + seq");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  ORTC_CHECK(!(host && kv_capacity), ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: kv_capacity needs device buffers");
+  const bool rotary = (flags & ORT_CUDA_ROTARY) != 0;
+  ORTC_CHECK(!rotary || (cos_cache && sin_cache && rotary_half >= 1 &&
+                         2 * rotary_half <= head_size && max_pos >= T),
+             ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: rotary needs cos/sin caches of max_pos >= past_len + seq "
+             "rows of rotary_half <= head_size / 2 values");
+  ORTC_CHECK(!bias || ((bias_batch == 1 || bias_batch == batch) && bias_heads >= 1),
+             ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: attention bias must be [1 or batch, heads, seq, total]");
+  const int64_t H = num_heads, Hkv = kv_num_heads, D = head_size;
+  ORTC_CHECK(batch * seq * H <= INT_MAX && T <= INT_MAX && batch * Hkv <= INT_MAX,
+             ORT_CUDA_ERR_INVALID_ARG, "GroupQueryAttention: sizes too large");
+  if (batch == 0 || T == 0) return ORT_CUDA_OK;
+  DeviceGuard guard(s->device);
+  const int64_t pcap = kv_capacity ? kv_capacity : past_len;
+  const int64_t rcap = kv_capacity ? kv_capacity : T;
+
+  HostStage st;
+  const size_t o_q = st.in(Q, sizeof(float) * batch * seq * H * D);
+  const size_t o_k = st.in(K, sizeof(float) * batch * seq * Hkv * D);
+  const size_t o_v = st.in(V, sizeof(float) * batch * seq * Hkv * D);
+  const size_t o_pk = st.in(past_len ? past_key : nullptr, sizeof(float) * batch * Hkv * pcap * D);
+  const size_t o_pv = st.in(past_len ? past_value : nullptr, sizeof(float) * batch * Hkv * pcap * D);
+  const size_t o_c = st.in(rotary ? cos_cache : nullptr, sizeof(float) * max_pos * rotary_half);
+  const size_t o_s = st.in(rotary ? sin_cache : nullptr, sizeof(float) * max_pos * rotary_half);
+  const size_t o_b = st.in(bias, sizeof(float) * bias_batch * bias_heads * seq * T);
+  const size_t o_o = st.out(out, sizeof(float) * batch * seq * H * D);
+  const size_t o_rk = st.out(present_key, sizeof(float) * batch * Hkv * rcap * D);
+  const size_t o_rv = st.out(present_value, sizeof(float) * batch * Hkv * rcap * D);
+  if (host) {
+    int rc = host_stage_in(s, st);
+    if (rc) return rc;
+    Q = ws_at<const float>(s, o_q, Q);
+    K = ws_at<const float>(s, o_k, K);
+    V = ws_at<const float>(s, o_v, V);
+    past_key = ws_at<const float>(s, o_pk, past_len ? past_key : nullptr);
+    past_value = ws_at<const float>(s, o_pv, past_len ? past_value : nullptr);
+    cos_cache = ws_at<const float>(s, o_c, rotary ? cos_cache : nullptr);
+    sin_cache = ws_at<const float>(s, o_s, rotary ? sin_cache : nullptr);
+    bias = ws_at<const float>(s, o_b, bias);
+    out = ws_at<float>(s, o_o, out);
+    present_key = ws_at<float>(s, o_rk, present_key);
+    present_value = ws_at<float>(s, o_rv, present_value);
+  }
+  const bool alias = present_key && present_key == past_key;
+  ORTC_CHECK(!alias || (present_value == past_value && pcap == rcap), ORT_CUDA_ERR_INVALID_ARG,
+             "GroupQueryAttention: an in-place cache needs present = past for K and V and "
+             "kv_capacity");
+  if (seq == 0) {  // present = past
+    if (present_key && !alias && past_len) {
+      ORTC_CUDA(cudaMemcpy2DAsync(present_key, rcap * D * 4, past_key, pcap * D * 4,
+                                  past_len * D * 4, batch * Hkv, cudaMemcpyDeviceToDevice,
+                                  s->stream));
+      ORTC_CUDA(cudaMemcpy2DAsync(present_value, rcap * D * 4, past_value, pcap * D * 4,
+                                  past_len * D * 4, batch * Hkv, cudaMemcpyDeviceToDevice,
+                                  s->stream));
+    }
+    return host ? host_stage_out(s, st) : ORT_CUDA_OK;
+  }
+  ortc::AttnArgs a;
+  a.q = Q;
+  a.qsb = seq * H * D, a.qsi = H * D, a.qsh = D;
+  a.k = K;
+  a.ksb = seq * Hkv * D, a.ksh = D, a.ksj = Hkv * D, a.ksd = 1;
+  a.v = V;
+  a.vsb = seq * Hkv * D, a.vsh = D, a.vsj = Hkv * D;
+  a.pk = past_key, a.pv = past_value;
+  a.psb = Hkv * pcap * D, a.psh = pcap * D;
+  a.prk = present_key, a.prv = present_value;
+  a.rsb = Hkv * rcap * D, a.rsh = rcap * D;
+  a.write_past = alias ? 0 : 1;
+  a.bias = bias;
+  if (bias) {
+    a.bsb = bias_batch == 1 ? 0 : bias_heads * seq * T;
+    a.bsh = seq * T, a.bsi = T, a.bsj = 1, a.bh = (int)bias_heads;
+  }
+  a.out = out;
+  a.osb = seq * H * D, a.osi = H * D, a.osh = D;
+  a.batch = (int)batch, a.seq = (int)seq, a.heads_kv = (int)Hkv, a.group = (int)(H / Hkv);
+  a.D = a.Dv = (int)D, a.past = (int)past_len, a.T = (int)T, a.causal = 1;
+  a.scale = scale > 0 ? scale : 1.0 / std::sqrt((double)D);
+  if (rotary) {
+    a.rotary = 1, a.cos = cos_cache, a.sin = sin_cache, a.half_rot = (int)rotary_half;
+    a.interleaved = (flags & ORT_CUDA_ROTARY_INTERLEAVED) ? 1 : 0;
+  }
+  int rc = run_attention(s, a);
+  if (rc) return rc;
+  return host ? host_stage_out(s, st) : ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_multi_head_attention(ort_cuda_session* s, const float* Q,
+                                               const float* K, const float* V, int64_t batch,
+                                               int64_t seq, int64_t kv_seq, int num_heads,
+                                               int64_t hidden, double scale, const float* bias,
+                                               int64_t bias_batch, int64_t bias_heads, float* out,
+                                               int flags) {
+  ORTC_CHECK(s && Q && K && V && out, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(batch >= 0 && seq >= 0 && kv_seq >= 0 && num_heads >= 1 && hidden >= 1 &&
+                 hidden % num_heads == 0,
+             ORT_CUDA_ERR_INVALID_ARG,
+             "MultiHeadAttention: need hidden a multiple of num_heads, sizes >= 0");
+  const int64_t H = num_heads, D = hidden / H;
+  ORTC_CHECK(D <= 128, ORT_CUDA_ERR_UNSUPPORTED,
+             "MultiHeadAttention: head sizes above 128 are not supported");
+  ORTC_CHECK(!bias || ((bias_batch == 1 || bias_batch == batch) && bias_heads >= 1),
+             ORT_CUDA_ERR_INVALID_ARG,
+             "MultiHeadAttention: attention bias must be [1 or batch, heads, seq, kv_seq]");
+  ORTC_CHECK(seq == 0 || kv_seq >= 1, ORT_CUDA_ERR_INVALID_ARG, "MultiHeadAttention: no keys");
+  ORTC_CHECK(batch * seq * H <= INT_MAX && kv_seq <= INT_MAX && batch * H <= INT_MAX,
+             ORT_CUDA_ERR_INVALID_ARG, "MultiHeadAttention: sizes too large");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  if (batch == 0 || seq == 0) return ORT_CUDA_OK;
+  DeviceGuard guard(s->device);
+  HostStage st;
+  const size_t o_q = st.in(Q, sizeof(float) * batch * seq * hidden);
+  const size_t o_k = st.in(K, sizeof(float) * batch * kv_seq * hidden);
+  const size_t o_v = st.in(V, sizeof(float) * batch * kv_seq * hidden);
+  const size_t o_b = st.in(bias, sizeof(float) * bias_batch * bias_heads * seq * kv_seq);
+  const size_t o_o = st.out(out, sizeof(float) * batch * seq * hidden);
+  if (host) {
+    int rc = host_stage_in(s, st);
+    if (rc) return rc;
+    Q = ws_at<const float>(s, o_q, Q);
+    K = ws_at<const float>(s, o_k, K);
+    V = ws_at<const float>(s, o_v, V);
+    bias = ws_at<const float>(s, o_b, bias);
+    out = ws_at<float>(s, o_o, out);
+  }
+  ortc::AttnArgs a;
+  a.q = Q;
+  a.qsb = seq * hidden, a.qsi = hidden, a.qsh = D;
+  a.k = K;
+  a.ksb = kv_seq * hidden, a.ksh = D, a.ksj = hidden, a.ksd = 1;
+  a.v = V;
+  a.vsb = kv_seq * hidden, a.vsh = D, a.vsj = hidden;
+  a.bias = bias;
+  if (bias) {
+    a.bsb = bias_batch == 1 ? 0 : bias_heads * seq * kv_seq;
+    a.bsh = seq * kv_seq, a.bsi = kv_seq, a.bsj = 1, a.bh = (int)bias_heads;
+  }
+  a.out = out;
+  a.osb = seq * hidden, a.osi = hidden, a.osh = D;
+  a.batch = (int)batch, a.seq = (int)seq, a.heads_kv = (int)H, a.group = 1;
+  a.D = a.Dv = (int)D, a.past = 0, a.T = (int)kv_seq, a.causal = 0;
+  a.scale = scale > 0 ? scale : 1.0 / std::sqrt((double)D);
+  int rc = run_attention(s, a);
+  if (rc) return rc;
+  return host ? host_stage_out(s, st) : ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_fused_sdpa(ort_cuda_session* s, const float* A, const float* B,
+                                     const float* V, const float* mask,
+                                     const int64_t* mask_strides, int64_t n0, int64_t n1,
+                                     int64_t seq, int64_t kv_seq, int64_t head_size,
+                                     int64_t v_head_size, double scale, float* out, int flags) {
+  ORTC_CHECK(s && A && B && V && out && (!mask || mask_strides), ORT_CUDA_ERR_INVALID_ARG,
+             "NULL argument");
+  ORTC_CHECK(n0 >= 0 && n1 >= 0 && seq >= 0 && kv_seq >= 0 && head_size >= 1 &&
+                 v_head_size >= 1,
+             ORT_CUDA_ERR_INVALID_ARG, "fused SDPA: sizes must be >= 0");
+  ORTC_CHECK(head_size <= 128 && v_head_size <= 128, ORT_CUDA_ERR_UNSUPPORTED,
+             "fused SDPA: head sizes above 128 are not supported");
+  ORTC_CHECK(seq == 0 || kv_seq >= 1, ORT_CUDA_ERR_INVALID_ARG, "fused SDPA: no keys");
+  int64_t mask_elems = 0;
+  if (mask) {
+    const int64_t dims[4] = {n0, n1, seq, kv_seq};
+    mask_elems = 1;
+    for (int i = 0; i < 4; i++) {
+      ORTC_CHECK(mask_strides[i] >= 0, ORT_CUDA_ERR_INVALID_ARG,
+                 "fused SDPA: mask strides must be >= 0 (0 broadcasts)");
+      if (dims[i] > 0) mask_elems += (dims[i] - 1) * mask_strides[i];
+    }
+  }
+  ORTC_CHECK(n0 * n1 <= INT_MAX && seq <= INT_MAX && kv_seq <= INT_MAX, ORT_CUDA_ERR_INVALID_ARG,
+             "fused SDPA: sizes too large");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  if (n0 == 0 || n1 == 0 || seq == 0) return ORT_CUDA_OK;
+  DeviceGuard guard(s->device);
+  const int64_t D = head_size, Dv = v_head_size;
+  HostStage st;
+  const size_t o_a = st.in(A, sizeof(float) * n0 * n1 * seq * D);
+  const size_t o_b = st.in(B, sizeof(float) * n0 * n1 * D * kv_seq);
+  const size_t o_v = st.in(V, sizeof(float) * n0 * n1 * kv_seq * Dv);
+  const size_t o_m = st.in(mask, sizeof(float) * mask_elems);
+  const size_t o_o = st.out(out, sizeof(float) * n0 * n1 * seq * Dv);
+  if (host) {
+    int rc = host_stage_in(s, st);
+    if (rc) return rc;
+    A = ws_at<const float>(s, o_a, A);
+    B = ws_at<const float>(s, o_b, B);
+    V = ws_at<const float>(s, o_v, V);
+    mask = ws_at<const float>(s, o_m, mask);
+    out = ws_at<float>(s, o_o, out);
+  }
+  ortc::AttnArgs a;  // (n0, n1) as (batch, head); B is K transposed: [D][kv_seq]
+  a.q = A;
+  a.qsb = n1 * seq * D, a.qsh = seq * D, a.qsi = D;
+  a.k = B;
+  a.ksb = n1 * D * kv_seq, a.ksh = D * kv_seq, a.ksj = 1, a.ksd = kv_seq;
+  a.v = V;
+  a.vsb = n1 * kv_seq * Dv, a.vsh = kv_seq * Dv, a.vsj = Dv;
+  a.bias = mask;
+  if (mask) {
+    a.bsb = mask_strides[0], a.bsh = mask_strides[1], a.bsi = mask_strides[2];
+    a.bsj = mask_strides[3], a.bh = (int)n1;
+  }
+  a.out = out;
+  a.osb = n1 * seq * Dv, a.osh = seq * Dv, a.osi = Dv;
+  a.batch = (int)n0, a.seq = (int)seq, a.heads_kv = (int)n1, a.group = 1;
+  a.D = (int)D, a.Dv = (int)Dv, a.past = 0, a.T = (int)kv_seq, a.causal = 0;
+  a.scale = scale;
+  int rc = run_attention(s, a);
+  if (rc) return rc;
+  return host ? host_stage_out(s, st) : ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
+                                           const int64_t* position_ids, int pos_per_batch,
+                                           const float* cos_cache, const float* sin_cache,
+                                           int64_t max_pos, int64_t rotary_half, int64_t batch,
+                                           int64_t seq, int64_t heads, int64_t head_size,
+                                           int64_t rotary_dim, float* Y, int flags) {
+  ORTC_CHECK(s && X && position_ids && cos_cache && sin_cache && Y, ORT_CUDA_ERR_INVALID_ARG,
+             "NULL argument");
+  const int64_t rdim = rotary_dim > 0 ? rotary_dim : 2 * rotary_half;
+  ORTC_CHECK(batch >= 0 && seq >= 0 && heads >= 0 && head_size >= 1 && rotary_half >= 1 &&
+                 max_pos >= 1 && rdim % 2 == 0 && rdim <= head_size && rdim / 2 <= rotary_half,
+             ORT_CUDA_ERR_INVALID_ARG,
+             "RotaryEmbedding: need an even rotary_dim <= head_size with rotary_dim / 2 <= the "
+             "cache row length");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  const int64_t n = batch * seq * heads * head_size;
+  if (n == 0) return ORT_CUDA_OK;
+  DeviceGuard guard(s->device);
+  HostStage st;
+  const size_t o_x = st.in(X, sizeof(float) * n);
+  const size_t o_p = st.in(position_ids, sizeof(int64_t) * (pos_per_batch ? batch : 1) * seq);
+  const size_t o_c = st.in(cos_cache, sizeof(float) * max_pos * rotary_half);
+  const size_t o_s = st.in(sin_cache, sizeof(float) * max_pos * rotary_half);
+  const size_t o_y = st.out(Y, sizeof(float) * n);
+  if (host) {
+    int rc = host_stage_in(s, st);
+    if (rc) return rc;
+    X = ws_at<const float>(s, o_x, X);
+    position_ids = ws_at<const int64_t>(s, o_p, position_ids);
+    cos_cache = ws_at<const float>(s, o_c, cos_cache);
+    sin_cache = ws_at<const float>(s, o_s, sin_cache);
+    Y = ws_at<float>(s, o_y, Y);
+  }
+  int rc = ortc::launch_rotary(X, Y, position_ids, pos_per_batch ? 1 : 0, cos_cache, sin_cache,
+                               max_pos, (int)rotary_half, (int)rdim, batch, seq, heads, head_size,
+                               (flags & ORT_CUDA_ROTARY_BHSD) ? 1 : 0,
+                               (flags & ORT_CUDA_ROTARY_INTERLEAVED) ? 1 : 0, s->stream,
+                               &s->launches);
+  if (rc) return rc;
+  return host ? host_stage_out(s, st) : ORT_CUDA_OK;
 }
 
 // ---- the hot ops --------------------------------------------------------------

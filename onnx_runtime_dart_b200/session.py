@@ -106,6 +106,8 @@ class CudaSession:
         self.device, self.rank, self.world, self.mode = device, rank, world, mode
         # initializer name -> ("nbits" | "dense", K, N)
         self.weights: Dict[str, tuple] = {}
+        self._explicit_stream = False  # set_stream() chose the launch stream
+        self._followed: Optional[int] = None
 
     @staticmethod
     def nccl_unique_id() -> bytes:
@@ -135,11 +137,29 @@ class CudaSession:
         """Launch on an existing cudaStream_t.  0 is the legacy default
         stream (torch's default stream), passed as cudaStreamLegacy; None
         restores the session's own stream."""
+        self._explicit_stream = stream_ptr is not None
+        self._followed = None
+        self._set_stream_raw(stream_ptr)
+
+    def _set_stream_raw(self, stream_ptr: Optional[int]) -> None:
         if stream_ptr is None:
             arg = None
         else:
             arg = stream_ptr if stream_ptr else 1  # cudaStreamLegacy == (cudaStream_t)0x1
         check(_lib.load().ort_cuda_set_stream(self.handle, arg), "ort_cuda_set_stream")
+
+    def _follow_torch_stream(self) -> None:
+        """Calls on torch CUDA tensors launch on torch's current stream
+        (unless set_stream() chose one), so they are ordered after the
+        kernels that produced their inputs and before those that read their
+        outputs, as torch ops are."""
+        if self._explicit_stream:
+            return
+        import torch
+        cur = torch.cuda.current_stream().cuda_stream
+        if cur != self._followed:
+            self._set_stream_raw(cur)
+            self._followed = cur
 
     def sync(self) -> None:
         check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")
@@ -250,6 +270,7 @@ class CudaSession:
         L = _lib.load()
         if hasattr(a, "data_ptr"):
             import torch
+            self._follow_torch_stream()
             signed = a.dtype == torch.int8
             a = a.contiguous()
             zp = None if a_zp is None else a_zp.reshape(-1).contiguous()
@@ -277,6 +298,7 @@ class CudaSession:
         L = _lib.load()
         if hasattr(x, "data_ptr"):
             import torch
+            self._follow_torch_stream()
             x = x.contiguous().float()
             y = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
             sc = torch.empty((), dtype=torch.float32, device=x.device)
@@ -317,6 +339,7 @@ class CudaSession:
             check(fn(self.handle, name.encode(), a.ptr, m, *extra, y.ptr, flags), fn.__name__)
             return y
         if hasattr(a, "data_ptr"):  # torch CUDA tensor: device pointers
+            self._follow_torch_stream()
             y = out
             if y is None:
                 import torch
@@ -353,6 +376,7 @@ class CudaSession:
         flags = (_lib.ARG_MIN if is_min else 0) | (_lib.ARG_SELECT_LAST if select_last else 0)
         if hasattr(x, "data_ptr"):  # torch CUDA tensor
             import torch
+            self._follow_torch_stream()
             x = x.contiguous().float()
             out = torch.empty(out_shape, dtype=torch.int64, device=x.device)
             check(L.ort_cuda_argmax(self.handle, x.data_ptr(), rows, cols, cols, out.data_ptr(),
@@ -375,6 +399,182 @@ class CudaSession:
         check(L.ort_cuda_argmax(self.handle, a.ctypes.data, rows, cols, cols, out.ctypes.data,
                                 flags | _lib.HOST_IO), "ort_cuda_argmax")
         return out
+
+    # -- attention of a decoder step ---------------------------------------
+    @staticmethod
+    def _is_torch(x) -> bool:
+        return hasattr(x, "data_ptr")
+
+    def _vals(self, xs):
+        """(pointers, host flag) for a call whose tensors are all numpy
+        arrays (ORT_CUDA_HOST_IO) or all torch CUDA tensors (device)."""
+        present = [x for x in xs if x is not None]
+        dev = [self._is_torch(x) for x in present]
+        if any(dev) and not all(dev):
+            raise ValueError("attention: mix of host and device tensors")
+        if dev and all(dev):
+            import torch
+            self._follow_torch_stream()
+            ts = [None if x is None else x.contiguous().to(torch.float32) if x.dtype.is_floating_point
+                  else x.contiguous() for x in xs]
+            return ts, [0 if t is None else t.data_ptr() for t in ts], 0
+        arrs = [None if x is None else np.ascontiguousarray(x) for x in xs]
+        arrs = [a if a is None or a.dtype == np.int64 else a.astype(np.float32, copy=False)
+                for a in arrs]
+        return arrs, [0 if a is None else a.ctypes.data for a in arrs], _lib.HOST_IO
+
+    def group_query_attention(self, q, k, v, num_heads: int, kv_num_heads: int, scale=None,
+                              do_rotary: bool = False, rotary_interleaved: bool = False,
+                              cos_cache=None, sin_cache=None, past_key=None, past_value=None,
+                              attention_bias=None, *, past_len: Optional[int] = None,
+                              present_key=None, present_value=None):
+        """GroupQueryAttention (opGroupQueryAttention, lib/src/onnx_ops.dart:
+        1507-1650) -> (out, present_key, present_value).  numpy inputs run
+        through host buffers; torch CUDA tensors stay on the device.  With
+        device ``present_key/present_value`` of shape [batch, kv_heads,
+        capacity, head] (an in-place KV cache: they may be past_key /
+        past_value themselves) ``past_len`` rows are taken as the past and
+        this step's rows are appended at past_len."""
+        L = _lib.load()
+        batch, seq = int(q.shape[0]), int(q.shape[1])
+        D = int(q.shape[2]) // num_heads
+        cap = 0
+        if present_key is not None:
+            if not self._is_torch(present_key) or past_len is None:
+                raise ValueError("an in-place KV cache needs device tensors and past_len")
+            cap = int(present_key.shape[2])
+        if past_len is None:
+            past_len = int(past_key.shape[2]) if past_key is not None and past_key.ndim == 4 else 0
+        T = past_len + seq
+        if not past_len:
+            past_key = past_value = None
+        flags = (_lib.ROTARY if do_rotary else 0) | (_lib.ROTARY_INTERLEAVED if rotary_interleaved else 0)
+        ts, ptrs, hflag = self._vals([q, k, v, past_key, past_value,
+                                      cos_cache if do_rotary else None,
+                                      sin_cache if do_rotary else None, attention_bias])
+        cos_t = ts[5]
+        max_pos = int(cos_t.shape[0]) if do_rotary else 0
+        half = int(cos_t.shape[-1]) if do_rotary else 0
+        bias_t = ts[7]
+        bb, bh = (int(bias_t.shape[0]), int(bias_t.shape[1])) if bias_t is not None else (0, 0)
+        if hflag:
+            out = np.empty((batch, seq, num_heads * D), np.float32)
+            pk = np.empty((batch, kv_num_heads, T, D), np.float32)
+            pv = np.empty_like(pk)
+            outp, pkp, pvp = out.ctypes.data, pk.ctypes.data, pv.ctypes.data
+        else:
+            import torch
+            out = torch.empty((batch, seq, num_heads * D), dtype=torch.float32, device=q.device)
+            if present_key is None:
+                pk = torch.empty((batch, kv_num_heads, T, D), dtype=torch.float32, device=q.device)
+                pv = torch.empty_like(pk)
+            else:
+                pk, pv = present_key, present_value
+            outp, pkp, pvp = out.data_ptr(), pk.data_ptr(), pv.data_ptr()
+        check(L.ort_cuda_group_query_attention(
+            self.handle, ptrs[0], ptrs[1], ptrs[2], ptrs[3], ptrs[4], batch, seq, past_len,
+            num_heads, kv_num_heads, D, 0.0 if scale is None else float(scale), ptrs[5],
+            ptrs[6], half, max_pos, ptrs[7], bb, bh, cap, outp, pkp, pvp, flags | hflag),
+            "ort_cuda_group_query_attention")
+        return out, pk, pv
+
+    def multi_head_attention(self, q, k, v, num_heads: int, scale=None, attention_bias=None):
+        """MultiHeadAttention (opMultiHeadAttention, lib/src/onnx_ops.dart:
+        1656-1725) over already-projected [batch, seq, hidden] Q/K/V."""
+        L = _lib.load()
+        batch, seq, hidden = (int(d) for d in q.shape)
+        kv_seq = int(k.shape[1])
+        ts, ptrs, hflag = self._vals([q, k, v, attention_bias])
+        bias_t = ts[3]
+        bb, bh = (int(bias_t.shape[0]), int(bias_t.shape[1])) if bias_t is not None else (0, 0)
+        if hflag:
+            out = np.empty((batch, seq, hidden), np.float32)
+            outp = out.ctypes.data
+        else:
+            import torch
+            out = torch.empty((batch, seq, hidden), dtype=torch.float32, device=q.device)
+            outp = out.data_ptr()
+        check(L.ort_cuda_multi_head_attention(
+            self.handle, ptrs[0], ptrs[1], ptrs[2], batch, seq, kv_seq, num_heads, hidden,
+            0.0 if scale is None else float(scale), ptrs[3], bb, bh, outp, hflag),
+            "ort_cuda_multi_head_attention")
+        return out
+
+    def fused_sdpa(self, a, b, v, mask, scale: float):
+        """_FusedSDPA (opFusedSDPA, lib/src/onnx_ops.dart:1733-1774):
+        softmax(a.b * scale + mask) . v for a [..., seq, D], b [..., D,
+        kv_seq] (K transposed), v [..., kv_seq, Dv] with equal leading dims
+        (at most two); mask broadcasts numpy-style (or None)."""
+        L = _lib.load()
+        lead = tuple(int(d) for d in a.shape[:-2])
+        if len(lead) > 2 or tuple(b.shape[:-2]) != lead or tuple(v.shape[:-2]) != lead:
+            raise UnsupportedError("fused SDPA: A, B and V need the same (at most two) batch dims")
+        n0, n1 = ((1, 1) + lead)[-2:]
+        seq, D = int(a.shape[-2]), int(a.shape[-1])
+        kv_seq, Dv = int(b.shape[-1]), int(v.shape[-1])
+        ts, ptrs, hflag = self._vals([a, b, v, mask])
+        strides = (ctypes.c_int64 * 4)(0, 0, 0, 0)
+        if ts[3] is not None:
+            m = ts[3]
+            mshape = (1,) * (4 - m.ndim) + tuple(int(d) for d in m.shape)
+            if m.ndim > 4:
+                raise UnsupportedError("fused SDPA: mask of rank > 4")
+            full = (n0, n1, seq, kv_seq)
+            st, acc = [0, 0, 0, 0], 1
+            for i in range(3, -1, -1):
+                if mshape[i] not in (1, full[i]):
+                    raise ValueError(f"fused SDPA: mask shape {tuple(m.shape)} does not broadcast")
+                st[i] = 0 if mshape[i] == 1 else acc
+                acc *= mshape[i]
+            for i in range(4):
+                strides[i] = st[i]
+        if hflag:
+            out = np.empty(lead + (seq, Dv), np.float32)
+            outp = out.ctypes.data
+        else:
+            import torch
+            out = torch.empty(lead + (seq, Dv), dtype=torch.float32, device=a.device)
+            outp = out.data_ptr()
+        check(L.ort_cuda_fused_sdpa(self.handle, ptrs[0], ptrs[1], ptrs[2], ptrs[3], strides,
+                                    n0, n1, seq, kv_seq, D, Dv, float(scale), outp, hflag),
+              "ort_cuda_fused_sdpa")
+        return out
+
+    def rotary_embedding(self, x, position_ids, cos_cache, sin_cache, interleaved: bool = False,
+                         num_heads: int = 0, rotary_dim: int = 0):
+        """RotaryEmbedding (opRotaryEmbedding, lib/src/onnx_ops.dart:
+        2121-2172); x [batch, seq, hidden] or [batch, heads, seq, head]."""
+        L = _lib.load()
+        half = int(cos_cache.shape[-1])
+        rdim = rotary_dim if rotary_dim > 0 else 2 * half
+        if x.ndim == 4:
+            batch, heads, seq, head = (int(d) for d in x.shape)
+            layout = _lib.ROTARY_BHSD
+        else:
+            batch, seq, hidden = (int(d) for d in x.shape)
+            head = hidden // num_heads if num_heads > 0 else rdim
+            heads = hidden // head
+            layout = 0
+        per_batch = 1 if np.ndim(position_ids) == 2 and int(position_ids.shape[0]) == batch and batch > 1 else 0
+        if self._is_torch(x):
+            import torch
+            position_ids = position_ids.to(torch.int64)
+        else:
+            position_ids = np.asarray(position_ids).astype(np.int64)
+        ts, ptrs, hflag = self._vals([x, position_ids, cos_cache, sin_cache])
+        if hflag:
+            y = np.empty(tuple(x.shape), np.float32)
+            yp = y.ctypes.data
+        else:
+            import torch
+            y = torch.empty(tuple(x.shape), dtype=torch.float32, device=x.device)
+            yp = y.data_ptr()
+        check(L.ort_cuda_rotary_embedding(
+            self.handle, ptrs[0], ptrs[1], per_batch, ptrs[2], ptrs[3], int(ts[2].shape[0]),
+            half, batch, seq, heads, head, rotary_dim,
+            yp, layout | (_lib.ROTARY_INTERLEAVED if interleaved else 0) | hflag),
+            "ort_cuda_rotary_embedding")
+        return y
 
     def matmul_nbits(self, name: str, a: Tensorish, flags: int = 0, out=None):
         kind, k, n = self.weights[name]
@@ -477,6 +677,29 @@ class CudaSession:
             if ins[1] in self.weights:
                 return [self.matmul(ins[1], a)]
             return [self.matmul_batched(np.asarray(a), np.asarray(values[ins[1]]))]
+        if op == "GroupQueryAttention":  # onnx_graph.dart:978-993
+            if attrs.get("softcap", 0) or attrs.get("local_window_size", -1) > 0:
+                raise UnsupportedError("GroupQueryAttention: softcap / local_window not supported")
+            opt = lambda i: values.get(ins[i]) if len(ins) > i and ins[i] else None  # noqa: E731
+            return list(self.group_query_attention(
+                a, values[ins[1]], values[ins[2]], attrs["num_heads"], attrs["kv_num_heads"],
+                scale=attrs.get("scale"), do_rotary=bool(attrs.get("do_rotary", 0)),
+                rotary_interleaved=bool(attrs.get("rotary_interleaved", 0)),
+                cos_cache=opt(7), sin_cache=opt(8), past_key=opt(3), past_value=opt(4),
+                attention_bias=opt(10)))
+        if op == "MultiHeadAttention":  # onnx_graph.dart:994-1000
+            bias = values.get(ins[5]) if len(ins) > 5 and ins[5] else None
+            return [self.multi_head_attention(a, values[ins[1]], values[ins[2]],
+                                              attrs["num_heads"], scale=attrs.get("scale"),
+                                              attention_bias=bias)]
+        if op == "RotaryEmbedding":  # onnx_graph.dart:1001-1005
+            return [self.rotary_embedding(a, values[ins[1]], values[ins[2]], values[ins[3]],
+                                          interleaved=bool(attrs.get("interleaved", 0)),
+                                          num_heads=attrs.get("num_heads", 0),
+                                          rotary_dim=attrs.get("rotary_embedding_dim", 0))]
+        if op == "_FusedSDPA":  # onnx_graph.dart:1029-1033
+            return [self.fused_sdpa(a, values[ins[1]], values[ins[2]], values[ins[3]],
+                                    attrs["scale"])]
         raise UnsupportedError(f"op {op} is not on the CUDA matmul path")
 
 

@@ -341,7 +341,12 @@ def group_query_attention(q, k, v, num_heads: int, kv_num_heads: int, scale=None
     P = past_key.shape[2] if past_key is not None and np.ndim(past_key) == 4 else 0
     T = P + seq
     if do_rotary:
-        pos = np.arange(P, P + seq, dtype=np.int64).reshape(1, seq)
+        # The reference builds these positions as a [1, seq] tensor
+        # (onnx_ops.dart:1533-1536), which opRotaryEmbedding indexes with
+        # b*seq + s (:2147): batch > 1 raises a RangeError there.  The same
+        # positions for every batch row (ORT's definition; a rank-1 tensor)
+        # is what batch 1 computes and what the restatement uses.
+        pos = np.arange(P, P + seq, dtype=np.int64)
         q = rotary_embedding(q, pos, cos_cache, sin_cache, rotary_interleaved, num_heads)
         k = rotary_embedding(k, pos, cos_cache, sin_cache, rotary_interleaved, kv_num_heads)
     s = float(scale) if scale is not None else 1.0 / np.sqrt(D)
@@ -366,8 +371,9 @@ def group_query_attention(q, k, v, num_heads: int, kv_num_heads: int, scale=None
             for i in range(seq):
                 last = P + i
                 sc = scores[i, :last + 1].astype(np.float64) * s
-                if bias is not None:
-                    sc = sc + bias[b, h % bias_heads, i, :last + 1].astype(np.float64)
+                if bias is not None:  # batch-1 bias broadcasts (as in MHA)
+                    bb = b if bias.shape[0] > 1 else 0
+                    sc = sc + bias[bb, h % bias_heads, i, :last + 1].astype(np.float64)
                 probs[i, :last + 1] = _softmax_rows(sc, sc.astype(np.float32))
             out[b, :, h * D:(h + 1) * D] = matmul_kernel(probs, np.ascontiguousarray(present_v[b, kvh]))
     return out, np.ascontiguousarray(present_k), np.ascontiguousarray(present_v)
@@ -392,8 +398,9 @@ def multi_head_attention(q, k, v, num_heads: int, scale=None, attention_bias=Non
             scores = matmul_kernel(np.ascontiguousarray(q[b, :, sl]),
                                    np.ascontiguousarray(k[b, :, sl].T))
             sc = scores.astype(np.float64) * s
-            if bias is not None:
-                sc = sc + bias[b, h % bias.shape[1]].astype(np.float64)
+            if bias is not None:  # a batch-1 bias broadcasts (ORT; the reference
+                # indexes b * bias_heads and raises for b > 0)
+                sc = sc + bias[b if bias.shape[0] > 1 else 0, h % bias.shape[1]].astype(np.float64)
             probs = _softmax_rows(sc, sc.astype(np.float32))
             out[b, :, sl] = matmul_kernel(probs, np.ascontiguousarray(v[b, :, sl]))
     return out
