@@ -125,13 +125,14 @@ __device__ void take_ticket_and_merge(const AttnArgs& p, int x, int RT, int nrow
   const int64_t ngrp = (int64_t)p.nqt * p.batch * p.heads_kv;
   const float* po = p.part;                                  // [grp][split][RT][Dv]
   const float* pml = p.part + ngrp * p.nsplit * RT * p.Dv;   // [grp][split][RT][2]
-  __threadfence();
+  // the CTA's partial writes, ordered by the barrier, are released by
+  // thread 0's acquire-release ticket (cumulative); the last CTA's thread 0
+  // acquires every split's writes, which the barrier passes on to its CTA
   __syncthreads();
   __shared__ bool last;
-  if (tid == 0) last = atomicAdd(&p.tickets[x], 1u) == (unsigned)(p.nsplit - 1);
+  if (tid == 0) last = atom_add_acq_rel_gpu(&p.tickets[x], 1u) == (unsigned)(p.nsplit - 1);
   __syncthreads();
   if (!last) return;
-  __threadfence();
   const int64_t gbase = (int64_t)x * p.nsplit * RT;
   float* mm = smem;                    // [nsplit][RT] maxima, then weights
   float* ll = smem + p.nsplit * RT;    // [nsplit][RT] sums
@@ -681,6 +682,24 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const AttnA
         }
     __syncwarp();
   }
+  float* rM = ow + kDecWarps * RTP * D;  // [RTP] CTA maximum, then [RTP] sum
+  float* rL = rM + RTP;
+  __syncthreads();
+  for (int r = tid; r < nrows; r += NT) {  // per row: the warps' weights, once
+    float M = -INFINITY;
+#pragma unroll
+    for (int w2 = 0; w2 < kDecWarps; w2++) M = fmaxf(M, mw[w2 * RTP + r]);
+    float L = 0.0f;
+#pragma unroll
+    for (int w2 = 0; w2 < kDecWarps; w2++) {
+      const float ms = mw[w2 * RTP + r];
+      const float wt = ms == -INFINITY ? 0.0f : expf(ms - M);
+      mw[w2 * RTP + r] = wt;
+      L = fmaf(wt, lw[w2 * RTP + r], L);
+    }
+    rM[r] = M;
+    rL[r] = L;
+  }
   __syncthreads();
   const int64_t base = ((int64_t)x * p.nsplit + split) * RTP;
   const int64_t ngrp = (int64_t)p.batch * p.heads_kv;
@@ -688,19 +707,11 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const AttnA
   float* pml = p.part ? p.part + ngrp * p.nsplit * RTP * D : nullptr;
   for (int e = tid; e < nrows * D; e += NT) {
     const int r = e / D, d = e % D;
-    float M = -INFINITY;
+    const float M = rM[r], L = rL[r];
+    float acc = 0.0f;
 #pragma unroll
-    for (int w2 = 0; w2 < kDecWarps; w2++) M = fmaxf(M, mw[w2 * RTP + r]);
-    float L = 0.0f, acc = 0.0f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w2 = 0; w2 < kDecWarps; w2++) {
-        const float ms = mw[w2 * RTP + r];
-        const float wt = ms == -INFINITY ? 0.0f : expf(ms - M);
-        L = fmaf(wt, lw[w2 * RTP + r], L);
-        acc = fmaf(wt, ow[(w2 * RTP + r) * D + d], acc);
-      }
-    }
+    for (int w2 = 0; w2 < kDecWarps; w2++)
+      acc = fmaf(mw[w2 * RTP + r], ow[(w2 * RTP + r) * D + d], acc);
     if (p.nsplit == 1) {
       const int h = g * p.group + r % p.group;
       p.out[b * p.osb + (int64_t)(r / p.group) * p.osi + (int64_t)h * p.osh + d] = acc / L;

@@ -242,3 +242,18 @@ def test_gqa_partial_rotary(sess, shape, interleaved):
     out, pk, pv = sess.group_query_attention(q, k, v, **kw)
     assert max_rel(want_o, out) <= TOL
     assert np.array_equal(pk, want_k) and np.array_equal(pv, want_v)
+
+
+@pytest.mark.parametrize("case", GQA_CASES + MHA_CASES + ["rotary_embedding"])
+def test_dispatch_attention_fixture_nodes(sess, golden, case):
+    """The fixture's node through CudaSession.dispatch, as the reference's
+    OnnxGraphExecutor._dispatch would route it (onnx_graph.dart:978-1005):
+    every output against the ORT-computed fixture."""
+    g = golden(case)
+    node = g["meta"]
+    values = {k[3:]: v for k, v in g.items() if k.startswith("in_")}
+    values.update({k[5:]: v for k, v in g.items() if k.startswith("init_")})
+    outs = sess.dispatch(node, values)
+    names = sorted(k for k in g if k.startswith("expected_"))
+    for name, got in zip(names, outs):
+        _fixture_ok(g[name], np.asarray(got))
