@@ -384,6 +384,56 @@ def main():
     big_flops = 2 * PREFILL_M * big.K * (bb - ba)
     del Ap, Yp
 
+    # ---- cfg4: one decode step of the Llama-3.2-1B matmul stream at M=4 ----
+    # 16 distinct layers x (q, k, v, o, gate, up, down) + lm_head, about
+    # 0.6 GB of int4 weights per step (larger than L2), in a CUDA graph
+    from onnx_runtime_dart_b200.workloads import LLAMA32_1B, LLAMA32_1B_LM_HEAD, make_nbits_weight
+    M4 = 4
+    c4 = [(f"c4.l{layer}.{p.name}", p) for layer in range(16) for p in LLAMA32_1B]
+    c4.append(("c4.lm_head", LLAMA32_1B_LM_HEAD))
+    rng4 = np.random.default_rng(SEED + 4)
+    for name, p in c4:
+        B4, s4, _ = make_nbits_weight(rng4, p.K, p.N, BS, zero_points=False,
+                                      scale_dtype=np.float16)
+        sess.upload_nbits(name, B4, s4, None, k=p.K, n=p.N, block_size=BS)
+    A4 = {K: torch.randn(M4, K, device=dev, generator=gen) for K in sorted({p.K for _, p in c4})}
+    Y4 = {name: torch.empty(M4, p.N, device=dev) for name, p in c4}
+
+    def step4():
+        for name, p in c4:
+            sess.matmul_nbits(name, A4[p.K], out=Y4[name])
+
+    for _ in range(args.warmup):
+        step4()
+    barrier()
+    g4 = None
+    if not args.eager:
+        sess.graph_begin()
+        step4()
+        g4 = sess.graph_end()
+        sess.graph_launch(g4)  # one untimed replay
+        barrier()
+    d4_steps = max(1, min(args.steps, 20))
+    e0.record(stream)
+    for _ in range(d4_steps):
+        if g4 is not None:
+            sess.graph_launch(g4)
+        else:
+            step4()
+    e1.record(stream)
+    barrier()
+    if g4 is not None:
+        sess.graph_drop(g4)
+    sess.sync()
+    d4_ms = e0.elapsed_time(e1) / d4_steps
+    rank_bytes4 = 0
+    for name, p in c4:
+        a, b = shard_range(p.N, rank, world)
+        rank_bytes4 += nbits_bytes(p.K, b - a, BS, M4, 2, False)
+    for name, _ in c4:
+        sess.drop_weight(name)
+    del A4, Y4
+
     # ---- end to end through the C ABI with host buffers -----------------
     hostA = {K: torch.randn(M, K, generator=torch.Generator().manual_seed(K)).pin_memory().numpy()
              for K in A}
@@ -404,13 +454,13 @@ def main():
     h2d = sum(4 * M * p.K for p in projs)
     d2h = sum(4 * M * p.N for p in projs)
 
-    stats = torch.tensor([ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms], dtype=torch.float64)
-    tot = torch.tensor([rank_bytes, launches, rank_flops], dtype=torch.float64)
+    stats = torch.tensor([ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms, d4_ms], dtype=torch.float64)
+    tot = torch.tensor([rank_bytes, launches, rank_flops, rank_bytes4], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-    ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms = stats.tolist()
-    job_bytes, launches, job_flops = tot.tolist()
+    ms_step, e2e_ms, big_ms, pf_ms, pf_big_ms, d4_ms = stats.tolist()
+    job_bytes, launches, job_flops, job_bytes4 = tot.tolist()
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -467,6 +517,15 @@ def main():
                              "frac": big_flops / (pf_big_ms * 1e-3) / 1e12 / tpk,
                              "peak_kind": tpk_kind},
             },
+            "decode_m4": {
+                "value": job_bytes4 / (d4_ms * 1e-3) / 1e9, "unit": "GB/s", "M": M4,
+                "mode": args.mode, "ms_per_step": d4_ms, "steps": d4_steps,
+                "frac": job_bytes4 / (d4_ms * 1e-3) / 1e9 / peak, "peak_kind": peak_kind,
+                "workload": "cfg4 decode step: Llama-3.2-1B int4 matmul stream, 16 layers x "
+                            "(q 2048x2048, k/v 2048x512, o 2048x2048, gate/up 2048x8192, "
+                            "down 8192x2048) + lm_head 2048x128256 at M=4; bits 4, block 128, "
+                            "fp16 scales, no zero points; CUDA graph of one step, weights "
+                            f"{job_bytes4 / 1e6:.0f} MB per step (larger than L2)"},
         }
         print(json.dumps(line), flush=True)
     sess.close()
