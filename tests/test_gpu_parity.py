@@ -503,17 +503,22 @@ def test_cluster_plans_parity_and_slice_invariance(sess, K, N, M, bs, zp):
     sess.drop_weight("cl1")
 
 
-@pytest.mark.parametrize("K,N,M", [(4096, 6144, 1), (14336, 1024, 2), (1536, 5000, 4)])
-def test_every_gemv_plan_gives_the_same_bits(sess, K, N, M):
+@pytest.mark.parametrize("K,N,M,bs", [(4096, 6144, 1, 128), (14336, 1024, 2, 128),
+                                      (1536, 5000, 4, 128), (2048, 512, 4, 128),
+                                      (2048, 2048, 5, 32), (2048, 1024, 8, 128),
+                                      (1000, 300, 3, 32),
+                                      (4096, 777, 5, 256), (3072, 1000, 2, 512)])
+def test_every_gemv_plan_gives_the_same_bits(sess, K, N, M, bs):
     """Every candidate decomposition of the decode GEMV (tile-major, the
-    cluster sizes that fit, split-K), set through ort_cuda_gemv_plan_set,
+    cluster sizes that fit, split-K), over block sizes 32-512, ragged K and
+    M up to 8, set through ort_cuda_gemv_plan_set,
     gives bit-identical results that match the oracle; plans outside the
     candidate range are refused and -1 restores the automatic choice."""
     rng = np.random.default_rng(K + N + M)
-    B, s, z = O.make_nbits_weight(rng, K, N, 128, zero_points=True)
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True)
     A = rng.standard_normal((M, K)).astype(np.float32)
-    sess.upload_nbits("pl", B, s, z, k=K, n=N, block_size=128)
-    ref = O.matmul_nbits(A, B, s, z, K, N, 4, 128, threads=8)
+    sess.upload_nbits("pl", B, s, z, k=K, n=N, block_size=bs)
+    ref = O.matmul_nbits(A, B, s, z, K, N, 4, bs, threads=8)
     first = None
     plan = 0
     while True:
