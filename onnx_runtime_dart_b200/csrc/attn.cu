@@ -77,20 +77,20 @@ __device__ __forceinline__ void rope_pair(float* row, int i, int half, int inter
   row[a1] = (float)(x1 * c + x0 * s);
 }
 
-// K/V tile [j0, j0 + 64) of (b, g) into shared memory, rows of PD / PDV
+// K/V tile [j0, j0 + KT) of (b, g) into shared memory, rows of PD / PDV
 // floats; rows j >= T and the columns up to the next multiple of 4 are zero.
-template <int NT>
+template <int NT, int KT>
 __device__ __forceinline__ void load_kv_tile(const AttnArgs& p, int b, int g, int j0, float* ks,
                                              float* vs, int PD, int PDV) {
   const int D4 = (p.D + 3) & ~3, Dv4 = (p.Dv + 3) & ~3;
   if (p.vec) {  // 16-byte rows chunks, asynchronous
     const int kq = D4 >> 2, vq = Dv4 >> 2;
-    for (int e = threadIdx.x; e < kKT * kq; e += NT) {
+    for (int e = threadIdx.x; e < KT * kq; e += NT) {
       const int jj = e / kq, c = e - jj * kq, j = j0 + jj;
       const bool in = j < p.T;
       cp_async16(ks + jj * PD + 4 * c, in ? k_row(p, b, g, j) + 4 * c : p.q, in ? 16 : 0);
     }
-    for (int e = threadIdx.x; e < kKT * vq; e += NT) {
+    for (int e = threadIdx.x; e < KT * vq; e += NT) {
       const int jj = e / vq, c = e - jj * vq, j = j0 + jj;
       const bool in = j < p.T;
       cp_async16(vs + jj * PDV + 4 * c, in ? v_row(p, b, g, j) + 4 * c : p.q, in ? 16 : 0);
@@ -100,13 +100,13 @@ __device__ __forceinline__ void load_kv_tile(const AttnArgs& p, int b, int g, in
   // element loads: feature-fastest when K rows are contiguous, else
   // key-fastest (K given transposed)
   const bool dfast = p.ksd == 1;
-  for (int e = threadIdx.x; e < kKT * D4; e += NT) {
-    const int jj = dfast ? e / D4 : e % kKT, d = dfast ? e % D4 : e / kKT, j = j0 + jj;
+  for (int e = threadIdx.x; e < KT * D4; e += NT) {
+    const int jj = dfast ? e / D4 : e % KT, d = dfast ? e % D4 : e / KT, j = j0 + jj;
     float x = 0.0f;
     if (j < p.T && d < p.D) x = j < p.cached ? k_row(p, b, g, j)[d] : k_row(p, b, g, j)[d * p.ksd];
     ks[jj * PD + d] = x;
   }
-  for (int e = threadIdx.x; e < kKT * Dv4; e += NT) {
+  for (int e = threadIdx.x; e < KT * Dv4; e += NT) {
     const int jj = e / Dv4, d = e % Dv4, j = j0 + jj;
     vs[jj * PDV + d] = (j < p.T && d < p.Dv) ? v_row(p, b, g, j)[d] : 0.0f;
   }
@@ -169,18 +169,19 @@ __device__ void take_ticket_and_merge(const AttnArgs& p, int x, int RT, int nrow
 }
 
 // TX lanes share a query row (TX = 16: a half warp; 32: a warp); TY groups
-// of them; RM rows per thread, KC keys per thread (key tx + TX*c).
+// of them; RM rows per thread, KC keys per thread (key tx + TX*c): tiles of
+// TX*KC keys (32 for heads above 64 in 64-row tiles, so that two CTAs fit
+// an SM; else 64).
 template <int TX, int TY, int RM, int KC>
 __global__ void __launch_bounds__(TX* TY) attn_kernel(const AttnArgs p) {
-  constexpr int NT = TX * TY, RT = TY * RM, DQ = (32 + TX - 1) / TX;
-  static_assert(TX * KC == kKT, "a tile is 64 keys");
+  constexpr int NT = TX * TY, RT = TY * RM, DQ = (32 + TX - 1) / TX, KT = TX * KC;
   extern __shared__ __align__(16) float smem[];
   const int D4 = (p.D + 3) & ~3, Dv4 = (p.Dv + 3) & ~3;
-  const int PD = D4 + 4, PDV = Dv4 + 4, PP = kKT + 4;
+  const int PD = D4 + 4, PDV = Dv4 + 4, PP = KT + 4;
   float* qs = smem;                 // RT x PD
-  float* ks = qs + RT * PD;         // 2 x kKT x PD
-  float* vs = ks + 2 * kKT * PD;    // 2 x kKT x PDV
-  float* ps = vs + 2 * kKT * PDV;   // RT x PP
+  float* ks = qs + RT * PD;         // 2 x KT x PD
+  float* vs = ks + 2 * KT * PD;    // 2 x KT x PDV
+  float* ps = vs + 2 * KT * PDV;   // RT x PP
 
   int x = blockIdx.x;
   const int split = x % p.nsplit;
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(TX* TY) attn_kernel(const AttnArgs p) {
 
   int limit = p.T;  // keys [0, limit) are read by this row tile
   if (p.causal) limit = min(p.T, p.past + (row0 + nrows - 1) / p.group + 1);
-  const int ntiles = (limit + kKT - 1) / kKT;
+  const int ntiles = (limit + KT - 1) / KT;
   const int tps = (ntiles + p.nsplit - 1) / p.nsplit;
   const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
   const bool writer = p.prk != nullptr && qt == p.nqt - 1;
@@ -232,24 +233,24 @@ __global__ void __launch_bounds__(TX* TY) attn_kernel(const AttnArgs p) {
   }
 
   if (t0 < t1) {
-    load_kv_tile<NT>(p, b, g, t0 * kKT, ks, vs, PD, PDV);
+    load_kv_tile<NT, KT>(p, b, g, t0 * KT, ks, vs, PD, PDV);
     cp_async_commit();
   }
   for (int t = t0; t < t1; t++) {
     const int stg = (t - t0) & 1;
     if (t + 1 < t1) {
-      load_kv_tile<NT>(p, b, g, (t + 1) * kKT, ks + (stg ^ 1) * kKT * PD,
-                       vs + (stg ^ 1) * kKT * PDV, PD, PDV);
+      load_kv_tile<NT, KT>(p, b, g, (t + 1) * KT, ks + (stg ^ 1) * KT * PD,
+                       vs + (stg ^ 1) * KT * PDV, PD, PDV);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    float* kt = ks + stg * kKT * PD;
-    float* vt = vs + stg * kKT * PDV;
-    const int j0 = t * kKT;
-    const int jn0 = max(j0, p.cached), jn1 = min(j0 + kKT, p.T);  // this call's keys
+    float* kt = ks + stg * KT * PD;
+    float* vt = vs + stg * KT * PDV;
+    const int j0 = t * KT;
+    const int jn0 = max(j0, p.cached), jn1 = min(j0 + KT, p.T);  // this call's keys
     if (p.rotary && jn0 < jn1) {  // RoPE at position j
       for (int e = tid; e < (jn1 - jn0) * p.half_rot; e += NT) {
         const int j = jn0 + e / p.half_rot, i = e % p.half_rot;
@@ -350,7 +351,7 @@ __global__ void __launch_bounds__(TX* TY) attn_kernel(const AttnArgs p) {
     __syncthreads();
 
     // O += P . V
-    for (int j = 0; j < kKT; j += 4) {
+    for (int j = 0; j < KT; j += 4) {
       float4 pv[RM];
 #pragma unroll
       for (int a = 0; a < RM; a++)
@@ -810,19 +811,20 @@ __global__ void rotary_kernel(const float* __restrict__ X, float* __restrict__ Y
 }
 
 struct AttnCfg {
-  int tx, ty, rm, rows;
+  int tx, ty, rm, rows, kt;
 };
 
-AttnCfg pick_cfg(int rows_total) {
-  if (rows_total <= 4) return {32, 4, 1, 4};
-  if (rows_total <= 8) return {32, 8, 1, 8};
-  if (rows_total <= 16) return {16, 16, 1, 16};
-  return {16, 16, 4, 64};
+AttnCfg pick_cfg(int rows_total, int D) {
+  if (rows_total <= 4) return {32, 4, 1, 4, 64};
+  if (rows_total <= 8) return {32, 8, 1, 8, 64};
+  if (rows_total <= 16) return {16, 16, 1, 16, 64};
+  return {16, 16, 4, 64, D > 64 ? 32 : 64};
 }
 
 size_t attn_smem_bytes(const AttnArgs& a, const AttnCfg& c) {
   const int PD = ((a.D + 3) & ~3) + 4, PDV = ((a.Dv + 3) & ~3) + 4;
-  return sizeof(float) * ((size_t)c.rows * PD + 2 * kKT * PD + 2 * kKT * PDV + c.rows * (kKT + 4));
+  return sizeof(float) *
+         ((size_t)c.rows * PD + 2 * c.kt * PD + 2 * c.kt * PDV + c.rows * (c.kt + 4));
 }
 
 size_t decode_smem_bytes(const AttnArgs& a, int rows) {
@@ -895,7 +897,7 @@ struct AttnPlan {
 AttnPlan plan_attention(AttnArgs& a, int sm_count) {
   AttnPlan pl;
   if (a.cached < 0) a.cached = a.past;
-  pl.c = pick_cfg(a.seq * a.group);
+  pl.c = pick_cfg(a.seq * a.group, std::max(a.D, a.Dv));
   a.rows_total = a.seq * a.group;
   a.nqt = (a.rows_total + pl.c.rows - 1) / pl.c.rows;
   a.vec = vec_ok(a);
@@ -988,6 +990,8 @@ int launch_attention(AttnArgs a, void* scratch, int sm_count, cudaStream_t st, i
       rc = launch_cfg<32, 8, 1, 2>(a, smem, grid, st);
     else if (c.rows == 16)
       rc = launch_cfg<16, 16, 1, 4>(a, smem, grid, st);
+    else if (c.kt == 32)
+      rc = launch_cfg<16, 16, 4, 2>(a, smem, grid, st);
     else
       rc = launch_cfg<16, 16, 4, 4>(a, smem, grid, st);
   }
