@@ -378,6 +378,25 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
                                            int64_t seq, int64_t heads, int64_t head_size,
                                            int64_t rotary_dim, float* Y, int flags);
 
+/* TopK (opTopK, lib/src/onnx_ops.dart:2261-2303) over the last axis of X,
+ * a [rows x cols] fp32 matrix with row stride ldx: values[r][0..k) and
+ * indices[r][0..k) (int64) in the reference's order -- value descending
+ * (ascending with ORT_CUDA_TOPK_SMALLEST), ties to the smaller index, NaN
+ * ranked above every number, -0.0 equal to 0.0.  1 <= k <= min(cols, 1024).
+ * The candidates of top-k sampling after lm_head stay on the device.  All
+ * pointers device (stream-ordered) unless ORT_CUDA_HOST_IO is set. */
+#define ORT_CUDA_TOPK_SMALLEST 0x800
+ORT_CUDA_API int ort_cuda_topk(ort_cuda_session* s, const float* X, int64_t rows, int64_t cols,
+                               int64_t ldx, int64_t k, float* values, int64_t* indices, int flags);
+
+/* _SliceLastSeq (onnx_graph.dart:456-473, inserted before the vocab
+ * projection by the lastTokenLogits rewrite, :398-451): Y[o][i] =
+ * X[o][seq-1][i] for X [outer][seq][inner], device pointers (a strided copy
+ * on the session stream), so that lm_head runs on the last position of a
+ * device-resident prefill. */
+ORT_CUDA_API int ort_cuda_slice_last_seq(ort_cuda_session* s, const float* X, int64_t outer,
+                                         int64_t seq, int64_t inner, float* Y, int flags);
+
 /* Kernel launches issued by this session since it was opened (all of
  * them this library's own kernels; a graph launch counts the kernels it
  * holds). */

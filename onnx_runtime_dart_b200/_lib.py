@@ -50,6 +50,7 @@ ARG_SELECT_LAST = 0x40
 ROTARY = 0x80  # attention flags
 ROTARY_INTERLEAVED = 0x200
 ROTARY_BHSD = 0x400
+TOPK_SMALLEST = 0x800
 
 # Every symbol include/ort_cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -91,6 +92,8 @@ SIGNATURES = {
     "ort_cuda_dynamic_quantize_linear": (_int, [_vp, _vp, _i64, _vp, _vp, _vp, _int]),
     "ort_cuda_matmul_integer": (_int, [_vp, _cp, _vp, _i64, _int, _vp, _i64, _vp, _int]),
     "ort_cuda_launch_count": (_int, [_vp, ctypes.POINTER(_i64)]),
+    "ort_cuda_topk": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _int]),
+    "ort_cuda_slice_last_seq": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _int]),
     "ort_cuda_group_query_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                               _int, _int, _i64, ctypes.c_double, _vp, _vp, _i64,
                                               _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _int]),

@@ -249,6 +249,10 @@ int launch_argminmax(const float* X, int64_t rows, int64_t cols, int64_t ldx, bo
 // MatMulInteger (int32 Y[M][ldy] over this rank's columns) on tensor cores;
 // A rows 16-byte aligned with lda % 16 == 0; rowsum holds M int32 when the
 // weight has zero points.
+// TopK over the last axis of X [rows][ldx]: vals/idx [rows][k], k <= 1024
+size_t topk_scratch_bytes(int64_t rows, int64_t cols, int64_t k);
+int launch_topk(const float* X, int64_t rows, int64_t cols, int64_t ldx, int64_t k, bool largest,
+                float* vals, int64_t* idx, void* scratch, cudaStream_t st, int64_t* launches);
 // DynamicQuantizeLinear of X[n] into Y[n] (uint8), *scale, *zp (device)
 size_t dynamic_quant_scratch_bytes(int sm_count);
 int launch_dynamic_quant(const float* X, int64_t n, uint8_t* Y, float* scale, uint8_t* zp,

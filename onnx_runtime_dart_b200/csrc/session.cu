@@ -1067,6 +1067,60 @@ ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const flo
   return bounded_sync(s);
 }
 
+ORT_CUDA_API int ort_cuda_topk(ort_cuda_session* s, const float* X, int64_t rows, int64_t cols,
+                               int64_t ldx, int64_t k, float* values, int64_t* indices,
+                               int flags) {
+  ORTC_CHECK(s && X && values && indices, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(rows >= 0 && cols >= 0 && ldx >= cols && k >= 0, ORT_CUDA_ERR_INVALID_ARG,
+             "TopK: need rows, cols, k >= 0 and ldx >= cols");
+  ORTC_CHECK(k <= cols, ORT_CUDA_ERR_INVALID_ARG, "TopK: k exceeds the axis length");
+  ORTC_CHECK(k <= 1024, ORT_CUDA_ERR_UNSUPPORTED, "TopK: k above 1024 is not supported");
+  if (rows == 0 || k == 0) return ORT_CUDA_OK;
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
+  DeviceGuard g(s->device);
+  const bool largest = (flags & ORT_CUDA_TOPK_SMALLEST) == 0;
+  const size_t sb = topk_scratch_bytes(rows, cols, k);
+  if (sb) {
+    int rc0 = ensure_kscratch(s, sb);
+    if (rc0) return rc0;
+  }
+  if (!host)
+    return launch_topk(X, rows, cols, ldx, k, largest, values, indices, s->kscratch, s->stream,
+                       &s->launches);
+  const size_t xb = (size_t)(rows * cols) * 4, vb = (size_t)(rows * k) * 4,
+               ib = (size_t)(rows * k) * 8;
+  const size_t ov = (xb + 255) & ~(size_t)255, oi = (ov + vb + 255) & ~(size_t)255;
+  int rc = ensure_ws(s, oi + ib + 256);
+  if (rc) return rc;
+  char* ws = static_cast<char*>(s->ws);
+  ORTC_CUDA(cudaMemcpy2DAsync(ws, (size_t)cols * 4, X, (size_t)ldx * 4, (size_t)cols * 4,
+                              (size_t)rows, cudaMemcpyHostToDevice, s->stream));
+  rc = launch_topk(reinterpret_cast<float*>(ws), rows, cols, cols, k, largest,
+                   reinterpret_cast<float*>(ws + ov), reinterpret_cast<int64_t*>(ws + oi),
+                   s->kscratch, s->stream, &s->launches);
+  if (rc) return rc;
+  ORTC_CUDA(cudaMemcpyAsync(values, ws + ov, vb, cudaMemcpyDeviceToHost, s->stream));
+  ORTC_CUDA(cudaMemcpyAsync(indices, ws + oi, ib, cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
+}
+
+ORT_CUDA_API int ort_cuda_slice_last_seq(ort_cuda_session* s, const float* X, int64_t outer,
+                                         int64_t seq, int64_t inner, float* Y, int flags) {
+  ORTC_CHECK(s && X && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(outer >= 0 && seq >= 1 && inner >= 0, ORT_CUDA_ERR_INVALID_ARG,
+             "slice_last_seq: need outer, inner >= 0 and seq >= 1");
+  ORTC_CHECK((flags & ORT_CUDA_HOST_IO) == 0, ORT_CUDA_ERR_INVALID_ARG,
+             "slice_last_seq takes device tensors (on the host it is the caller's copy)");
+  if (outer == 0 || inner == 0) return ORT_CUDA_OK;
+  DeviceGuard g(s->device);
+  ORTC_CUDA(cudaMemcpy2DAsync(Y, (size_t)inner * 4, X + (seq - 1) * inner, (size_t)(seq * inner) * 4,
+                              (size_t)inner * 4, (size_t)outer, cudaMemcpyDeviceToDevice,
+                              s->stream));
+  return ORT_CUDA_OK;
+}
+
 // ---- attention of a decoder step -------------------------------------------
 
 }  // extern "C"

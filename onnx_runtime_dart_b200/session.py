@@ -400,6 +400,48 @@ class CudaSession:
                                 flags | _lib.HOST_IO), "ort_cuda_argmax")
         return out
 
+    def topk(self, x, k: int, *, largest: bool = True):
+        """TopK over the last axis (opTopK, lib/src/onnx_ops.dart:2261-2303):
+        (values, int64 indices) of shape x.shape[:-1] + (k,), the
+        reference's ordering.  A torch CUDA tensor stays on its device
+        (stream-ordered); a numpy array runs through host buffers."""
+        L = _lib.load()
+        shape = tuple(int(d) for d in x.shape)
+        cols = shape[-1] if shape else 1
+        rows = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        flags = 0 if largest else _lib.TOPK_SMALLEST
+        out_shape = shape[:-1] + (k,)
+        if hasattr(x, "data_ptr"):
+            import torch
+            self._follow_torch_stream()
+            x = x.contiguous().float()
+            v = torch.empty(out_shape, dtype=torch.float32, device=x.device)
+            i = torch.empty(out_shape, dtype=torch.int64, device=x.device)
+            check(L.ort_cuda_topk(self.handle, x.data_ptr(), rows, cols, cols, k, v.data_ptr(),
+                                  i.data_ptr(), flags), "ort_cuda_topk")
+            return v, i
+        a = np.ascontiguousarray(x, dtype=np.float32)
+        v = np.empty(out_shape, np.float32)
+        i = np.empty(out_shape, np.int64)
+        check(L.ort_cuda_topk(self.handle, a.ctypes.data, rows, cols, cols, k, v.ctypes.data,
+                              i.ctypes.data, flags | _lib.HOST_IO), "ort_cuda_topk")
+        return v, i
+
+    def slice_last_seq(self, x):
+        """_SliceLastSeq (onnx_graph.dart:456-473) of a torch CUDA tensor
+        [..., seq, inner]: the last position, [..., 1, inner], on the device."""
+        import torch
+        self._follow_torch_stream()
+        x = x.contiguous().float()
+        seq, inner = int(x.shape[-2]), int(x.shape[-1])
+        if seq <= 1:
+            return x
+        outer = int(np.prod(x.shape[:-2], dtype=np.int64)) if x.dim() > 2 else 1
+        y = torch.empty(tuple(x.shape[:-2]) + (1, inner), dtype=torch.float32, device=x.device)
+        check(_lib.load().ort_cuda_slice_last_seq(self.handle, x.data_ptr(), outer, seq, inner,
+                                                  y.data_ptr(), 0), "ort_cuda_slice_last_seq")
+        return y
+
     # -- attention of a decoder step ---------------------------------------
     @staticmethod
     def _is_torch(x) -> bool:
@@ -697,6 +739,12 @@ class CudaSession:
                                           interleaved=bool(attrs.get("interleaved", 0)),
                                           num_heads=attrs.get("num_heads", 0),
                                           rotary_dim=attrs.get("rotary_embedding_dim", 0))]
+        if op == "TopK":  # onnx_graph.dart:1514-1517 (last axis)
+            k = int(np.asarray(values[ins[1]]).ravel()[0])
+            axis = attrs.get("axis", -1)
+            if axis not in (-1, np.ndim(a) - 1):
+                raise UnsupportedError("TopK: the device path takes the last axis")
+            return list(self.topk(a, k, largest=bool(attrs.get("largest", 1))))
         if op == "_FusedSDPA":  # onnx_graph.dart:1029-1033
             return [self.fused_sdpa(a, values[ins[1]], values[ins[2]], values[ins[3]],
                                     attrs["scale"])]

@@ -422,3 +422,37 @@ def fused_sdpa(a, b, v, mask, scale: float):
     total = np.cumsum(e, axis=-1)[..., -1:]
     p = (e32.astype(np.float64) / total).astype(np.float32)
     return matmul(p, v)
+
+
+# ---- selection after lm_head ------------------------------------------------
+
+def topk(x, k: int, axis: int = -1, largest: bool = True):
+    """TopK, restating opTopK (lib/src/onnx_ops.dart:2261-2303): along
+    `axis`, the indices ordered by value (descending when largest, else
+    ascending) with ties to the smaller index; Dart's compareTo ranks NaN
+    above every number, and -0.0 == 0.0 is a tie.  Returns (values float32,
+    indices int64) of shape x.shape with axis -> k.  Plain Python sort."""
+    x = np.asarray(x, np.float32)
+    ax = axis + x.ndim if axis < 0 else axis
+    xm = np.moveaxis(x, ax, -1)
+    flat = xm.reshape(-1, xm.shape[-1])
+    vals = np.empty((flat.shape[0], k), np.float32)
+    idx = np.empty((flat.shape[0], k), np.int64)
+    for r in range(flat.shape[0]):
+        row = flat[r].tolist()
+        if largest:
+            order = sorted(range(len(row)),
+                           key=lambda d: (0 if row[d] != row[d] else 1, -row[d] if row[d] == row[d] else 0.0, d))
+        else:
+            order = sorted(range(len(row)),
+                           key=lambda d: (1 if row[d] != row[d] else 0, row[d] if row[d] == row[d] else 0.0, d))
+        idx[r] = order[:k]
+        vals[r] = flat[r][order[:k]]
+    shape = xm.shape[:-1] + (k,)
+    return (np.moveaxis(vals.reshape(shape), -1, ax), np.moveaxis(idx.reshape(shape), -1, ax))
+
+
+def slice_last_seq(x):
+    """_SliceLastSeq (onnx_graph.dart:456-473): x[..., seq-1:seq, :]."""
+    x = np.asarray(x)
+    return np.ascontiguousarray(x[..., -1:, :]) if x.shape[-2] > 1 else x

@@ -49,6 +49,9 @@ CASES = [
     "mha_with_bias",
     "rotary_embedding",
     "sdpa_pattern",  # MatMul/Div/Add/Softmax/MatMul, fused to _FusedSDPA
+    # candidate selection after lm_head (top-k sampling)
+    "topk_largest",
+    "topk_smallest_axis0",
 ]
 
 _ONNX_DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 6: np.int32, 7: np.int64,

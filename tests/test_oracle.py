@@ -284,3 +284,27 @@ def test_oracle_gqa_present_is_past_then_current():
     assert np.array_equal(pk2, pk) and np.array_equal(pv2, pv)
     assert np.allclose(step[0, 0], full[0, S - 1], rtol=1e-6, atol=1e-6)
     assert np.allclose(part, full[:, :S - 1], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["topk_largest", "topk_smallest_axis0"])
+def test_oracle_topk_fixtures(golden, case):
+    """TopK restatement against the reference's ORT fixtures: values and
+    int64 indices exactly."""
+    g = golden(case)
+    a = g["meta"]["attrs"]
+    vals, idx = O.topk(g["in_x"], int(g["init_k"].ravel()[0]), axis=int(a.get("axis", -1)),
+                       largest=bool(a.get("largest", 1)))
+    assert np.array_equal(vals, g["expected_out0"])
+    assert np.array_equal(idx, g["expected_out1"])
+
+
+def test_oracle_topk_ties_nan_and_signed_zero():
+    """Ties keep index order, NaN ranks above every number (first when
+    largest, last when smallest), -0.0 ties with 0.0."""
+    x = np.array([[1.0, np.nan, 3.0, 3.0, -0.0, 0.0, np.inf, -np.inf]], np.float32)
+    v, i = O.topk(x, 8)
+    assert i.tolist() == [[1, 6, 2, 3, 0, 4, 5, 7]]
+    v, i = O.topk(x, 8, largest=False)
+    assert i.tolist() == [[7, 4, 5, 0, 2, 3, 6, 1]]
+    assert np.array_equal(O.slice_last_seq(np.arange(24.0).reshape(2, 3, 4)),
+                          np.arange(24.0).reshape(2, 3, 4)[:, 2:3])
