@@ -1141,17 +1141,21 @@ struct HostStage {
   std::vector<In> ins;
   std::vector<Out> outs;
   size_t total = 0;
+  bool enabled;  // device-pointer calls stage nothing
+  explicit HostStage(bool host) : enabled(host) {}
   size_t slot(size_t bytes) {
     const size_t off = total;
     total += (bytes + 255) & ~(size_t)255;
     return off;
   }
   size_t in(const void* src, size_t bytes) {
+    if (!enabled) return 0;
     const size_t off = slot(bytes);
     if (src && bytes) ins.push_back({src, bytes, off});
     return off;
   }
   size_t out(void* dst, size_t bytes) {
+    if (!enabled) return 0;
     const size_t off = slot(bytes);
     if (dst && bytes) outs.push_back({dst, bytes, off});
     return off;
@@ -1248,7 +1252,7 @@ ORT_CUDA_API int ort_cuda_group_query_attention(
   const int64_t pcap = kv_capacity ? kv_capacity : past_len;
   const int64_t rcap = kv_capacity ? kv_capacity : T;
 
-  HostStage st;
+  HostStage st(host);
   const size_t o_q = st.in(Q, sizeof(float) * batch * seq * H * D);
   const size_t o_k = st.in(K, sizeof(float) * batch * seq * Hkv * D);
   const size_t o_v = st.in(V, sizeof(float) * batch * seq * Hkv * D);
@@ -1346,7 +1350,7 @@ ORT_CUDA_API int ort_cuda_multi_head_attention(ort_cuda_session* s, const float*
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   if (batch == 0 || seq == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
-  HostStage st;
+  HostStage st(host);
   const size_t o_q = st.in(Q, sizeof(float) * batch * seq * hidden);
   const size_t o_k = st.in(K, sizeof(float) * batch * kv_seq * hidden);
   const size_t o_v = st.in(V, sizeof(float) * batch * kv_seq * hidden);
@@ -1414,7 +1418,7 @@ ORT_CUDA_API int ort_cuda_fused_sdpa(ort_cuda_session* s, const float* A, const 
   if (n0 == 0 || n1 == 0 || seq == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
   const int64_t D = head_size, Dv = v_head_size;
-  HostStage st;
+  HostStage st(host);
   const size_t o_a = st.in(A, sizeof(float) * n0 * n1 * seq * D);
   const size_t o_b = st.in(B, sizeof(float) * n0 * n1 * D * kv_seq);
   const size_t o_v = st.in(V, sizeof(float) * n0 * n1 * kv_seq * Dv);
@@ -1471,7 +1475,7 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
   const int64_t n = batch * seq * heads * head_size;
   if (n == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
-  HostStage st;
+  HostStage st(host);
   const size_t o_x = st.in(X, sizeof(float) * n);
   const size_t o_p = st.in(position_ids, sizeof(int64_t) * (pos_per_batch ? batch : 1) * seq);
   const size_t o_c = st.in(cos_cache, sizeof(float) * max_pos * rotary_half);
