@@ -210,14 +210,20 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
  * ort_cuda_matmul_nbits may grow session scratch with cudaMalloc; this
  * call runs the same exact-mode decode GEMV with its split-K scratch in a
  * static device array of this library: 4 MiB of partial sums, held by every
- * GPU that loads the library until the process exits.  Shapes whose
- * scratch would exceed that are rejected with ORT_CUDA_ERR_INVALID_ARG
- * (only few-column, very long-K weights need split-K scratch at all).
+ * GPU that loads the library until the process exits.  When the work plan
+ * the regular entry point uses would need more scratch than that, the call
+ * runs the fastest-estimated plan that fits (the tile-major plan needs
+ * none); every plan gives the same bits, so Y equals the regular entry
+ * point's Y bit for bit and only the speed can differ.
  *   A, Y   DEVICE pointers ([M,K] and [M,N] fp32); the call is
  *          stream-ordered on the session stream
- *   M      1..4; 32 <= block_size <= 512; single-GPU sessions only
+ *   M      1..4 (else ORT_CUDA_ERR_INVALID_ARG); 32 <= block_size <= 512;
+ *          single-GPU sessions whose mode is not STRICT (the call always
+ *          runs the exact-mode GEMV; a STRICT session gets
+ *          ORT_CUDA_ERR_UNSUPPORTED)
  * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * (cudaGetSymbolAddress); make that first call before any stream capture
+ * (a first call during a capture returns ORT_CUDA_ERR_INVALID_ARG).
  * All calls share the array, so calls that overlap on the GPU (other
  * streams, other sessions on the same device) race. */
 ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, const char* name,
@@ -382,7 +388,13 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
  * a [rows x cols] fp32 matrix with row stride ldx: values[r][0..k) and
  * indices[r][0..k) (int64) in the reference's order -- value descending
  * (ascending with ORT_CUDA_TOPK_SMALLEST), ties to the smaller index, NaN
- * ranked above every number, -0.0 equal to 0.0.  1 <= k <= min(cols, 1024).
+ * ranked above every number, -0.0 equal to 0.0.  1 <= k <= min(cols, 1024);
+ * rows above 40960 columns are split into segments of at most 40960
+ * columns, at most floor(4096 / k) of them, so such rows also need
+ * cols <= 40960 * floor(4096 / k) (a 128256-column vocabulary takes every
+ * k <= 1024, a 256000-column one k <= 585); beyond that the call returns
+ * ORT_CUDA_ERR_UNSUPPORTED.  Among equal NaNs the smaller index comes first
+ * (the reference's sort leaves that order unspecified).
  * The candidates of top-k sampling after lm_head stay on the device.  All
  * pointers device (stream-ordered) unless ORT_CUDA_HOST_IO is set. */
 #define ORT_CUDA_TOPK_SMALLEST 0x800
@@ -401,6 +413,30 @@ ORT_CUDA_API int ort_cuda_slice_last_seq(ort_cuda_session* s, const float* X, in
  * them this library's own kernels; a graph launch counts the kernels it
  * holds). */
 ORT_CUDA_API int ort_cuda_launch_count(ort_cuda_session* s, int64_t* count);
+
+/* ---- per-op-type profile --------------------------------------------- */
+/* The device-side counterpart of ExecutionProfile (onnx_graph.dart:22-47):
+ * while enabled, every call of an op entry point records a CUDA event pair
+ * on the session stream around its work, under its ONNX op type
+ * ("MatMulNBits", "Gemm", "MatMul", "MatMulInteger", "GroupQueryAttention",
+ * "TopK", ...).  Events between kernels end their programmatic overlap, so
+ * a profiled sequence runs somewhat slower; calls captured into a CUDA
+ * graph are not recorded.  Enabling keeps earlier totals; reset clears
+ * them (both synchronise the session stream). */
+ORT_CUDA_API int ort_cuda_profile_enable(ort_cuda_session* s, int on);
+ORT_CUDA_API int ort_cuda_profile_reset(ort_cuda_session* s);
+/* Entry `index` of the report, sorted by cumulative device time, longest
+ * first (ExecutionProfile.report's order): op type (NUL-terminated,
+ * truncated to op_type_cap), call count and device microseconds.
+ * Synchronises the session stream; ORT_CUDA_ERR_NOT_FOUND past the end. */
+ORT_CUDA_API int ort_cuda_profile_read(ort_cuda_session* s, int index, char* op_type,
+                                       int op_type_cap, int64_t* calls, double* device_us);
+
+/* ---- diagnostics ------------------------------------------------------ */
+/* Measured fp32 FFMA throughput (TFLOP/s) of the session's GPU, the
+ * CUDA-core roofline of the exact and strict modes' dense Gemm/MatMul.  No
+ * counterpart in the reference.  Runs one probe kernel for a few ms. */
+ORT_CUDA_API int ort_cuda_probe_ffma(ort_cuda_session* s, double* tflops);
 
 #ifdef __cplusplus
 }

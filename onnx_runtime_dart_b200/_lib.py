@@ -107,6 +107,11 @@ SIGNATURES = {
     "ort_cuda_graph_end": (_int, [_vp, ctypes.POINTER(_int)]),
     "ort_cuda_graph_launch": (_int, [_vp, _int]),
     "ort_cuda_graph_drop": (_int, [_vp, _int]),
+    "ort_cuda_profile_enable": (_int, [_vp, _int]),
+    "ort_cuda_profile_reset": (_int, [_vp]),
+    "ort_cuda_profile_read": (_int, [_vp, _int, _cp, _int, ctypes.POINTER(_i64),
+                                     ctypes.POINTER(ctypes.c_double)]),
+    "ort_cuda_probe_ffma": (_int, [_vp, ctypes.POINTER(ctypes.c_double)]),
 }
 
 _lib = None

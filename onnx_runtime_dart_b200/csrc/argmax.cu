@@ -15,6 +15,7 @@
 // the last CTA of a row (an atomic ticket) combines the row's candidates in
 // segment order and writes the index.
 #include <algorithm>
+#include <atomic>
 #include <climits>
 
 #include "common.cuh"
@@ -331,6 +332,16 @@ int topk_segments(int64_t cols, int64_t k) {
   return (int)std::max<int64_t>(1, nseg);
 }
 
+// Largest k a row of `cols` columns takes: a segment holds at most
+// kTkMaxKeyBytes / 4 = 40960 columns and a row at most kTkMaxCand / k
+// segments, so cols <= 40960 * floor(4096 / k).
+int64_t topk_max_k(int64_t cols) {
+  const int64_t seg_cols = kTkMaxKeyBytes / 4;
+  if (cols <= 2 * kTkSeg || cols <= seg_cols) return std::min<int64_t>(cols, kTkMaxK);
+  const int64_t nseg_needed = (cols + seg_cols - 1) / seg_cols;
+  return std::min<int64_t>({cols, (int64_t)kTkMaxK, kTkMaxCand / nseg_needed});
+}
+
 size_t topk_scratch_bytes(int64_t rows, int64_t cols, int64_t k) {
   const int nseg = topk_segments(cols, k);
   return nseg > 1 ? (size_t)rows * nseg * k * 8 : 0;
@@ -343,15 +354,18 @@ int launch_topk(const float* X, int64_t rows, int64_t cols, int64_t ldx, int64_t
                  rows <= INT_MAX,
              ORT_CUDA_ERR_INVALID_ARG, "TopK: need 1 <= k <= min(cols, 1024) and cols < 2^31");
   const int nseg = topk_segments(cols, k);
-  static unsigned long long attr_set = 0;  // per device: keys above 48 KB of shared memory
+  // per device: keys above 48 KB of shared memory.  Sessions may run on
+  // several host threads; setting the attribute twice is harmless, so an
+  // atomic bit per device only saves the repeated calls.
+  static std::atomic<unsigned long long> attr_set{0};
   int dev = 0;
   ORTC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set >> dev & 1ull)) {
+  if (dev >= 64 || !(attr_set.load(std::memory_order_acquire) >> dev & 1ull)) {
     ORTC_CUDA(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kTkMaxKeyBytes));
     ORTC_CUDA(cudaFuncSetAttribute(topk_seg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    kTkMaxKeyBytes));
-    attr_set |= 1ull << dev;
+    if (dev < 64) attr_set.fetch_or(1ull << dev, std::memory_order_acq_rel);
   }
   if (nseg == 1) {
     topk_kernel<<<(unsigned)rows, kTkThreads, (size_t)cols * 4, st>>>(
@@ -364,7 +378,9 @@ int launch_topk(const float* X, int64_t rows, int64_t cols, int64_t ldx, int64_t
   ORTC_CHECK(rows * nseg <= INT_MAX, ORT_CUDA_ERR_INVALID_ARG, "TopK: too many rows");
   const int seg = (int)((cols + nseg - 1) / nseg);
   ORTC_CHECK((size_t)seg * 4 <= (size_t)kTkMaxKeyBytes, ORT_CUDA_ERR_UNSUPPORTED,
-             "TopK: row segment too long for shared memory");
+             "TopK: rows of " + std::to_string(cols) + " columns take k <= " +
+                 std::to_string(topk_max_k(cols)) + " (each of at most 4096 / k segments "
+                 "holds 40960 columns), got k = " + std::to_string(k));
   unsigned long long* cand = static_cast<unsigned long long*>(scratch);
   topk_seg_kernel<<<(unsigned)(rows * nseg), kTkThreads, (size_t)seg * 4, st>>>(
       X, ldx, (int)cols, seg, nseg, (int)k, largest ? 1 : 0, cand);

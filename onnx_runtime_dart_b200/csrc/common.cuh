@@ -104,6 +104,8 @@ __host__ __device__ __forceinline__ uint32_t nbits_zp(const uint8_t* zp, int64_t
 
 }  // namespace ortc
 
+struct ort_cuda_profile;  // per-op-type device times (csrc/profile.cu)
+
 struct ort_cuda_session {
   int device = 0;
   int mode = ORT_CUDA_MODE_EXACT;
@@ -146,6 +148,17 @@ struct ort_cuda_session {
   bool p2p_ok = false;
   bool xsel_offer = false;  // run_op offers the exchange half to the producer
   bool xsel_taken = false;  // the producer wrote its slice there
+  size_t llcap = 0;          // 64-bit words per half of the tagged (push) area
+  float* push_y = nullptr;   // run_op offers push mode: the gathered Y [M, N]
+  bool push_taken = false;   // the producer pushed (p2p_land completes the op)
+  // run_op offers the NCCL exchange to the producer, which may run it in
+  // row chunks overlapped with its own compute (prefill): the gathered Y,
+  // the [G, M, Ns] landing area; `gathered` says the producer did it
+  float* chunk_y = nullptr;
+  float* chunk_gath = nullptr;
+  bool gathered = false;
+  cudaStream_t comm_stream = nullptr;  // the chunks' all-gathers and re-layouts
+  cudaEvent_t chunk_ev[17] = {};       // chunk c computed; [16]: exchange done
   // CUDA graphs captured from the session stream (ort_cuda_graph_*)
   struct Graph {
     cudaGraphExec_t exec;
@@ -155,6 +168,11 @@ struct ort_cuda_session {
   int next_graph = 1;
   bool capturing = false;
   int64_t capture_launch0 = 0;
+  // ort_cuda_profile_*: event pairs around each call while profiling
+  ort_cuda_profile* prof = nullptr;
+  bool profiling = false;
+  // event bounded_sync records and polls (created on first use)
+  cudaEvent_t sync_ev = nullptr;
   // host-mapped error word kernels write when a bounded wait gives up
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -163,21 +181,71 @@ struct ort_cuda_session {
 
 namespace ortc {
 
+// Records a CUDA event pair on the session stream around one call of an
+// entry point while the session profiles (ort_cuda_profile_enable); does
+// nothing otherwise or while a graph is being captured.
+class OpTimer {
+ public:
+  OpTimer(ort_cuda_session* s, const char* op);
+  ~OpTimer();
+  OpTimer(const OpTimer&) = delete;
+  OpTimer& operator=(const OpTimer&) = delete;
+
+ private:
+  ort_cuda_session* s_ = nullptr;
+  const char* op_ = nullptr;
+  cudaEvent_t e0_ = nullptr;
+};
+void profile_free(ort_cuda_session* s);
+
 // Scratch helpers (session-owned, stream-ordered reuse).
 int ensure_ws(ort_cuda_session* s, size_t bytes);
 int ensure_pinned(ort_cuda_session* s, size_t bytes);
-// Output redirected to the half of a peer-exchange buffer that a device
-// resident epoch counter selects (half (ctr + 1) & 1, N-sharded sessions);
-// inactive when ctr is null.
+// Where an N-sharded producer puts its outputs (inactive when ctr is null).
+// The device-resident epoch counter ctr gives this operation's epoch
+// e = ctr + 1.
+//  - pull mode: the outputs go to half (e & 1) of this rank's exchange
+//    buffer (half0, cap floats a half); p2p_gather then reads every rank's
+//    half over peer memory.
+//  - push mode: the outputs go to the caller's Y (the gathered [M, N]
+//    layout, at this rank's columns) and, each as one 64-bit word
+//    (e << 32 | float bits), to half (e & 1) of every peer's tagged
+//    exchange area ll[r] (llcap words a half, row pitch N, row row0 + m,
+//    column n0 + n); p2p_land on each peer waits for the tags and copies
+//    the values into its own Y.  A 64-bit store is single-copy atomic, so
+//    a word whose tag reads e holds this epoch's value: no fence and no
+//    flag is needed between producer and consumer.
 struct YSel {
   float* half0 = nullptr;
   int64_t cap = 0;
   const unsigned long long* ctr = nullptr;
+  bool push = false;
+  int rank = 0, world = 0, row0 = 0;
+  int64_t n0 = 0, N = 0, llcap = 0;
+  unsigned long long* ll[8] = {};
 };
+__device__ __forceinline__ unsigned long long ysel_epoch(const YSel& s) {
+  return s.ctr ? *reinterpret_cast<const volatile unsigned long long*>(s.ctr) + 1 : 0ull;
+}
 __device__ __forceinline__ float* ysel_base(float* Y, const YSel& s) {
-  if (!s.ctr) return Y;
-  const unsigned long long e = *reinterpret_cast<const volatile unsigned long long*>(s.ctr) + 1;
-  return s.half0 + (int64_t)(e & 1) * s.cap;
+  if (!s.ctr || s.push) return Y;
+  return s.half0 + (int64_t)(ysel_epoch(s) & 1) * s.cap;
+}
+// Yb[m * ldy + n] = v (Yb from ysel_base) and, in push mode, the tagged
+// copy of v for every peer; e = ysel_epoch(s), read after the grid's
+// dependency wait.
+__device__ __forceinline__ void ysel_store(float* Yb, int64_t ldy, const YSel& s,
+                                           unsigned long long e, int m, int n, float v) {
+  Yb[m * ldy + n] = v;
+  if (s.push) {
+    const unsigned long long word = (e << 32) | (unsigned long long)__float_as_uint(v);
+    const int64_t off = (int64_t)(e & 1) * s.llcap + (int64_t)(s.row0 + m) * s.N + s.n0 + n;
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+      if (r < s.world && r != s.rank)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(s.ll[r] + off), "l"(word)
+                     : "memory");
+  }
 }
 
 int ensure_kscratch(ort_cuda_session* s, size_t bytes);
@@ -191,6 +259,14 @@ int p2p_setup(ort_cuda_session* s);
 void p2p_teardown(ort_cuda_session* s);
 bool p2p_fits(ort_cuda_session* s, int64_t floats);
 YSel p2p_ysel(ort_cuda_session* s);
+// Push mode for a producer of rows [row0, row0 + m) of an [M, N] output
+// whose local column 0 is global column n0 (see YSel).
+bool p2p_push_fits(ort_cuda_session* s, int64_t M, int64_t N);
+YSel p2p_ysel_push(ort_cuda_session* s, int64_t n0, int64_t N, int row0);
+// Completes a push-mode operation: waits (bounded) for every peer's tagged
+// words of this epoch and copies them into Y [M, N] (row pitch N); this
+// rank's columns [n0, n0 + nl) are already there.  Advances the epoch.
+int p2p_land(ort_cuda_session* s, int64_t M, int64_t N, int64_t n0, int64_t nl, float* Y);
 // `local` null: the producer already wrote the slice with p2p_ysel().
 int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, int64_t N,
                float* Y);
@@ -209,9 +285,12 @@ int encode_tma_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, ui
 // tc_gemv_partial_floats(.., plan) floats (no initial value needed).
 int prepare_nbits_tc(Weight& w);
 bool tc_gemv_ok(const Weight& w, int64_t M);
+// tc_gemv_ok without the rank's own column count: the same answer on every
+// rank of an N-sharded group (a rank holding no columns launches nothing).
+bool tc_gemv_shape_ok(const Weight& w, int64_t M);
 // The work plan a call uses: the one tune_tc_gemv chose for (w, M) when its
-// partial sums fit in max_partial_floats, else the heuristic's; -1 if
-// neither fits.
+// partial sums fit in max_partial_floats, else the heuristic's choice among
+// the candidates that fit; -1 if none fits.
 int tc_gemv_plan(const Weight& w, int64_t M, int sm_count,
                  size_t max_partial_floats = (size_t)-1);
 // Number of candidate plans for (w, M) on this device.

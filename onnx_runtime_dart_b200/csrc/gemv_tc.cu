@@ -708,6 +708,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (lane == 0 && egrp == 0)
       for (int e = 0; e < p.nd; e++) mbar_arrive(&ready[e]);
     griddep_wait();  // outputs and split-K scratch may still be in use upstream
+    const unsigned long long ep = ysel_epoch(p.ysel);  // push mode's tag
     __syncwarp();    // .aligned cluster barrier: the whole warp, converged
     if (clustered) cluster_wait();
     const int set = (int)blockIdx.x / p.csize;
@@ -806,7 +807,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int m = 0; m < M; m++) {
           const float acc = chunk == 0 ? 0.0f + part[m] : ya[m * kTile + nl] + part[m];
           ya[m * kTile + nl] = acc;
-          if (chunk == p.nch - 1 && n < p.N) ysel_base(p.Y, p.ysel)[m * p.ldy + n] = acc;
+          if (chunk == p.nch - 1 && n < p.N)
+            ysel_store(ysel_base(p.Y, p.ysel), p.ldy, p.ysel, ep, m, n, acc);
         }
       } else if (clustered) {
         // into the inbox of the CTA that sums this tile: rank ti % csize,
@@ -863,7 +865,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               for (int u = 0; u < 8; u++) acc = acc + v[u];
             }
             for (; c < p.nch; c++) acc = acc + col[(size_t)c * per];
-            if (n < p.N) Yb[m * p.ldy + n] = acc;
+            if (n < p.N) ysel_store(Yb, p.ldy, p.ysel, ep, m, n, acc);
           }
         }
       }
@@ -890,6 +892,7 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
   griddep_launch_dependents();
   griddep_wait();
   Y = ysel_base(Y, ysel);
+  const unsigned long long ep = ysel_epoch(ysel);
   const int64_t total = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -907,7 +910,7 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
       for (int c = 0; c < 32; c++)
         if (c0 + c < nch) acc = acc + v[c];
     }
-    Y[m * ldy + n] = acc;
+    ysel_store(Y, ldy, ysel, ep, m, n, acc);
   }
 }
 
@@ -1055,11 +1058,16 @@ std::vector<Plan> plan_candidates(const Weight& w, int64_t M, int sm_count) {
   return out;
 }
 
-int heuristic_plan(const std::vector<Plan>& c) {
-  int best = 0;
-  for (int i = 1; i < (int)c.size(); i++)
-    if (c[i].cost2 < c[best].cost2 || (c[i].cost2 == c[best].cost2 && c[i].grid > c[best].grid))
+// The heuristic's choice among the candidates whose partial sums fit in
+// `max_partial_floats` (-1: none fits).
+int heuristic_plan(const std::vector<Plan>& c, size_t max_partial_floats = (size_t)-1) {
+  int best = -1;
+  for (int i = 0; i < (int)c.size(); i++) {
+    if (c[i].partial_floats > max_partial_floats) continue;
+    if (best < 0 || c[i].cost2 < c[best].cost2 ||
+        (c[i].cost2 == c[best].cost2 && c[i].grid > c[best].grid))
       best = i;
+  }
   return best;
 }
 
@@ -1130,12 +1138,17 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
 }  // namespace
 
 // TMA views of a MatMulNBits weight for the tensor-core GEMV.
+// Shape conditions of the tensor-core GEMV that hold on every rank of an
+// N-sharded group alike (they do not depend on the rank's column count).
+static bool tc_layout_ok(const Weight& w) {
+  const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
+  return w.bs >= kMinBs && w.bs <= kChunkK && (w.bs & (w.bs - 1)) == 0 && col_bytes % 16 == 0;
+}
+
 int prepare_nbits_tc(Weight& w) {
   w.tc_ok = false;
   const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
-  if (w.bs < kMinBs || w.bs > kChunkK || (w.bs & (w.bs - 1)) != 0 || col_bytes % 16 != 0 ||
-      w.nl == 0)
-    return ORT_CUDA_OK;
+  if (!tc_layout_ok(w) || w.nl == 0) return ORT_CUDA_OK;
   const int bpi = kChunkK / w.bs;
   int rc = encode_tma_2d(&w.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes,
                          (uint64_t)w.nl, (uint64_t)col_bytes, 128, kTile,
@@ -1164,6 +1177,11 @@ int prepare_nbits_tc(Weight& w) {
 // beside the A ring (384 columns).
 bool tc_gemv_ok(const Weight& w, int64_t M) {
   if (!w.tc_ok || M < 1 || M > 8) return false;
+  return d_plan(M, w.bs).nd > 0;
+}
+
+bool tc_gemv_shape_ok(const Weight& w, int64_t M) {
+  if (w.kind != W_NBITS || !tc_layout_ok(w) || M < 1 || M > 8) return false;
   return d_plan(M, w.bs).nd > 0;
 }
 
@@ -1241,8 +1259,7 @@ int tc_gemv_plan(const Weight& w, int64_t M, int sm_count, size_t max_partial_fl
   const std::vector<Plan> c = plan_candidates(w, M, sm_count);
   const int t = (M >= 1 && M <= 8) ? w.gemv_plan[M] : -1;
   if (t >= 0 && t < (int)c.size() && c[t].partial_floats <= max_partial_floats) return t;
-  const int h = heuristic_plan(c);
-  return c[h].partial_floats <= max_partial_floats ? h : -1;
+  return heuristic_plan(c, max_partial_floats);
 }
 
 int tc_gemv_plan_count(const Weight& w, int64_t M, int sm_count) {

@@ -33,12 +33,19 @@ struct Slot {
 std::mutex g_mu;
 Slot g_slots[64];
 
-// Device address of the array on `device` (which must be current).
-int slot_for(int device, Slot** out) {
+// Device address of the array on `device` (which must be current).  The
+// lookup can load the module lazily, which would invalidate a stream
+// capture in progress, so a session that is capturing gets an error
+// instead when the address is not known yet.
+int slot_for(int device, bool capturing, Slot** out) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (device < 0 || device >= 64) return fail(ORT_CUDA_ERR_INVALID_ARG, "device index >= 64");
   Slot& sl = g_slots[device];
   if (!sl.ready) {
+    if (capturing)
+      return fail(ORT_CUDA_ERR_INVALID_ARG,
+                  "the first no-allocation MatMulNBits call on a device sets it up and cannot "
+                  "be captured; make one call before the capture");
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(partials)");
@@ -65,12 +72,17 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
              std::string("weight '") + name + "' is not a MatMulNBits weight");
   ORTC_CHECK(s->world == 1, ORT_CUDA_ERR_UNSUPPORTED,
              "no-allocation MatMulNBits runs on single-GPU sessions only");
+  ORTC_CHECK(s->mode != ORT_CUDA_MODE_STRICT, ORT_CUDA_ERR_UNSUPPORTED,
+             "no-allocation MatMulNBits runs the exact-mode GEMV; this session's mode is "
+             "STRICT, whose bit-for-bit reference rounding it does not reproduce");
   ORTC_CHECK(M >= 1 && M <= 4, ORT_CUDA_ERR_INVALID_ARG,
              "no-allocation MatMulNBits takes 1 <= M <= 4, got M=" + std::to_string(M));
   ORTC_CHECK(tc_gemv_ok(w, M), ORT_CUDA_ERR_UNSUPPORTED,
              "no-allocation MatMulNBits needs 32 <= block_size <= 512");
-  // the plan the regular entry point would use, unless its partial sums do
-  // not fit the static scratch (then the heuristic's, if that fits)
+  // The plan the regular entry point would use, unless its partial sums do
+  // not fit the static scratch; then the heuristic's choice among the plans
+  // that fit.  Every plan gives the same bits, and the tile-major plan
+  // needs no partial sums, so only a shape no plan fits is refused.
   const int plan = tc_gemv_plan(w, M, s->sm_count, kNoAllocPartialFloats);
   if (plan < 0) {
     const size_t pf = tc_gemv_partial_floats(w, M, s->sm_count, tc_gemv_plan(w, M, s->sm_count));
@@ -85,7 +97,7 @@ extern "C" ORT_CUDA_API int ort_cuda_matmul_nbits_noalloc(ort_cuda_session* s, c
   Slot* sl = nullptr;
   // The array keeps the previous call's contents; nothing in it needs a
   // starting value (every partial is written before it is read).
-  int rc = slot_for(s->device, &sl);
+  int rc = slot_for(s->device, s->capturing, &sl);
   if (rc == ORT_CUDA_OK)
     rc = launch_tc_gemv(w, plan, A, M, Y, w.nl, sl->partials, s->err_dev, s->sm_count,
                         s->stream, &s->launches, nullptr);

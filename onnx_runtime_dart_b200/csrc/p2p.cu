@@ -19,6 +19,7 @@
 // does only after its own read finished: two halves are enough.  The epoch
 // lives on the device, so the sequence replays unchanged from a CUDA graph.
 // No NCCL and no multicast is on the per-operation path.
+#include <climits>
 #include <cstring>
 #include <vector>
 
@@ -33,6 +34,8 @@ constexpr size_t kFlagBytes = 256;
 constexpr int kCtrSlot = 8, kDoneSlot = 9;  // 64-bit words in the flag area
 constexpr int kPull = 4;                    // elements per thread and round
 constexpr size_t kDefaultCapFloats = size_t(4) << 20;  // 16 MB per half
+constexpr size_t kDefaultLLWords = size_t(4) << 20;    // tagged area: 32 MB per half
+constexpr int kLand = 4;                               // words per thread and round
 
 struct P2PArgs {
   const float* src[8];            // rank r's half 0 (half 1 follows at + cap)
@@ -135,6 +138,71 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
   }
 }
 
+// Push mode's consumer (see YSel): copies the peers' columns of this
+// epoch's [M, N] output from this rank's tagged area into Y, waiting
+// (bounded) for each word's tag; the rank's own columns [n0, n0 + nl) are
+// in Y already.  Launched as a programmatic dependent of the producer: the
+// epoch is read and advanced only after the producer grid has finished
+// (it read the same counter).
+__global__ void __launch_bounds__(256) p2p_land_kernel(const unsigned long long* ll0,
+                                                       int64_t llcap, unsigned long long* mine,
+                                                       float* Y, int M, int N, int n0, int nl,
+                                                       int* err) {
+  __shared__ unsigned long long epoch;
+  griddep_launch_dependents();
+  griddep_wait();
+  if (threadIdx.x == 0) epoch = next_epoch(mine);
+  __syncthreads();
+  const unsigned long long e = epoch;
+  const unsigned tag = (unsigned)e;
+  const unsigned long long* src = ll0 + (int64_t)(e & 1) * llcap;
+  const int other = N - nl;  // peers' columns per row
+  const int total = M * other;
+  const int stride = (int)(gridDim.x * blockDim.x);
+  uint64_t t0 = 0;
+  bool ok = true;
+  for (int i0 = (int)(blockIdx.x * blockDim.x + threadIdx.x); i0 < total && ok;
+       i0 += stride * kLand) {
+    int64_t at[kLand];
+    unsigned long long w[kLand];
+#pragma unroll
+    for (int u = 0; u < kLand; u++) {
+      const int i = i0 + u * stride;
+      at[u] = -1;
+      if (i < total) {
+        const int m = i / other, j = i - m * other;
+        at[u] = (int64_t)m * N + (j < n0 ? j : j + nl);
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[u]) : "l"(src + at[u]) : "memory");
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kLand; u++) {
+      if (at[u] < 0 || !ok) continue;
+      while ((unsigned)(w[u] >> 32) != tag) {
+        if (t0 == 0) t0 = globaltimer();
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          record_error(err, KERR_WAIT_PEER);
+          ok = false;
+          break;
+        }
+        __nanosleep(32);
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[u]) : "l"(src + at[u]) : "memory");
+      }
+      if (ok) Y[at[u]] = __uint_as_float((unsigned)w[u]);
+    }
+  }
+  // the last CTA to finish advances the epoch counter (every CTA has read it)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(mine + kDoneSlot, 1ull) == gridDim.x - 1) {
+      mine[kDoneSlot] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(mine + kCtrSlot) = e;
+    }
+  }
+}
+
 // Bounded completion of a non-blocking NCCL call, then of the stream.
 int nccl_finish(ort_cuda_session* s, ncclResult_t r) {
   if (r != ncclSuccess && r != ncclInProgress)
@@ -172,9 +240,16 @@ int p2p_setup(ort_cuda_session* s) {
   if (s->world < 2 || s->world > 8 || !s->nccl) return ORT_CUDA_OK;
   size_t cap = kDefaultCapFloats;
   if (const char* env = std::getenv("ORT_CUDA_P2P_FLOATS")) cap = std::strtoull(env, nullptr, 10);
-  ORTC_CUDA(cudaMalloc(&s->xbuf, kFlagBytes + 2 * cap * 4));
+  cap = (cap + 63) / 64 * 64;  // keeps the tagged area 256-byte aligned
+  const size_t llcap = kDefaultLLWords;
+  // [flags][half 0, half 1: cap floats][tagged half 0, half 1: llcap words];
+  // the tagged area starts zeroed (tag 0 is never an epoch: e >= 1)
+  ORTC_CUDA(cudaMalloc(&s->xbuf, kFlagBytes + 2 * cap * 4 + 2 * llcap * 8));
   ORTC_CUDA(cudaMemset(s->xbuf, 0, kFlagBytes));
+  ORTC_CUDA(cudaMemset((char*)s->xbuf + kFlagBytes + 2 * cap * 4, 0, 2 * llcap * 8));
+  ORTC_CUDA(cudaDeviceSynchronize());
   s->xcap = cap;
+  s->llcap = llcap;
   cudaIpcMemHandle_t h;
   bool ok = cudaIpcGetMemHandle(&h, s->xbuf) == cudaSuccess;
   if (!ok) std::memset(&h, 0, sizeof(h));
@@ -223,6 +298,48 @@ void p2p_teardown(ort_cuda_session* s) {
 
 bool p2p_fits(ort_cuda_session* s, int64_t floats) {
   return s->p2p_ok && (size_t)floats <= s->xcap;
+}
+
+bool p2p_push_fits(ort_cuda_session* s, int64_t M, int64_t N) {
+  return s->p2p_ok && s->llcap > 0 && M * N <= (int64_t)s->llcap && N <= INT_MAX / 16 &&
+         M * N <= INT_MAX;
+}
+
+YSel p2p_ysel_push(ort_cuda_session* s, int64_t n0, int64_t N, int row0) {
+  YSel y;
+  y.ctr = (const unsigned long long*)s->xbuf + kCtrSlot;
+  y.push = true;
+  y.rank = s->rank;
+  y.world = s->world;
+  y.row0 = row0;
+  y.n0 = n0;
+  y.N = N;
+  y.llcap = (int64_t)s->llcap;
+  for (int r = 0; r < s->world; r++)
+    y.ll[r] = (unsigned long long*)((char*)s->xpeer[r] + kFlagBytes + 2 * s->xcap * 4);
+  return y;
+}
+
+int p2p_land(ort_cuda_session* s, int64_t M, int64_t N, int64_t n0, int64_t nl, float* Y) {
+  unsigned long long* mine = (unsigned long long*)s->xbuf;
+  const unsigned long long* ll0 =
+      (const unsigned long long*)((char*)s->xbuf + kFlagBytes + 2 * s->xcap * 4);
+  const int64_t total = M * (N - nl);
+  const unsigned blocks = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>((total + 256 * kLand - 1) / (256 * kLand), s->sm_count));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ORTC_CUDA(cudaLaunchKernelEx(&cfg, p2p_land_kernel, ll0, (int64_t)s->llcap, mine, Y, (int)M,
+                               (int)N, (int)n0, (int)nl, s->err_dev));
+  s->launches++;
+  return ORT_CUDA_OK;
 }
 
 YSel p2p_ysel(ort_cuda_session* s) {

@@ -180,43 +180,39 @@ int bounded_sync(ort_cuda_session* s) {
     ORTC_CUDA(cudaStreamSynchronize(s->stream));
     return check_kernel_error(s);
   }
-  cudaEvent_t ev;
-  ORTC_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  cudaError_t e = cudaEventRecord(ev, s->stream);
-  if (e != cudaSuccess) {
-    cudaEventDestroy(ev);
-    return cuda_fail(e, "cudaEventRecord");
-  }
+  // One event per session, recorded anew by every call.
+  if (!s->sync_ev) ORTC_CUDA(cudaEventCreateWithFlags(&s->sync_ev, cudaEventDisableTiming));
+  ORTC_CUDA(cudaEventRecord(s->sync_ev, s->stream));
+  // A decode-sized op finishes within tens of microseconds: poll without
+  // sleeping for the first 2 ms (a sleep granule would dominate such a
+  // call), then back off to 20 us sleeps.
   const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    e = cudaEventQuery(ev);
+  for (int polls = 0;; polls++) {
+    const cudaError_t e = cudaEventQuery(s->sync_ev);
     if (e == cudaSuccess) break;
-    if (e != cudaErrorNotReady) {
-      cudaEventDestroy(ev);
-      return cuda_fail(e, "cudaEventQuery");
-    }
-    ncclResult_t ar = ncclSuccess;
-    nccl()->CommGetAsyncError((ncclComm_t)s->nccl, &ar);
-    if (ar != ncclSuccess && ar != ncclInProgress) {
-      cudaEventDestroy(ev);
-      nccl()->CommAbort((ncclComm_t)s->nccl);
-      s->nccl = nullptr;
-      return fail(ORT_CUDA_ERR_NCCL, std::string("NCCL async error: ") + nccl()->GetErrorString(ar));
-    }
-    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+    if (e != cudaErrorNotReady) return cuda_fail(e, "cudaEventQuery");
+    const auto us = std::chrono::duration_cast<std::chrono::microseconds>(
                         std::chrono::steady_clock::now() - t0)
                         .count();
-    if (ms > s->timeout_ms) {
+    if ((polls & 63) == 0 || us > 2000) {
+      ncclResult_t ar = ncclSuccess;
+      nccl()->CommGetAsyncError((ncclComm_t)s->nccl, &ar);
+      if (ar != ncclSuccess && ar != ncclInProgress) {
+        nccl()->CommAbort((ncclComm_t)s->nccl);
+        s->nccl = nullptr;
+        return fail(ORT_CUDA_ERR_NCCL,
+                    std::string("NCCL async error: ") + nccl()->GetErrorString(ar));
+      }
+    }
+    if (us > (int64_t)s->timeout_ms * 1000) {
       nccl()->CommAbort((ncclComm_t)s->nccl);
       s->nccl = nullptr;
-      cudaEventDestroy(ev);
       return fail(ORT_CUDA_ERR_TIMEOUT, "collective did not complete within " +
                                             std::to_string(s->timeout_ms) +
                                             " ms; communicator aborted");
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (us > 2000) std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
-  cudaEventDestroy(ev);
   return check_kernel_error(s);
 }
 
@@ -433,6 +429,13 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->err_host) cudaFreeHost(s->err_host);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second.exec);
   s->graphs.clear();
+  profile_free(s);
+  if (s->sync_ev) cudaEventDestroy(s->sync_ev);
+  for (cudaEvent_t& e : s->chunk_ev)
+    if (e) cudaEventDestroy(e);
+  if (s->comm_stream) cudaStreamDestroy(s->comm_stream);
+  s->comm_stream = nullptr;
+  s->sync_ev = nullptr;
   p2p_teardown(s);
   if (s->nccl) {
     nccl()->CommFinalize((ncclComm_t)s->nccl);
@@ -989,6 +992,7 @@ ORT_CUDA_API int ort_cuda_argmax(ort_cuda_session* s, const float* X, int64_t ro
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   DeviceGuard g(s->device);
+  OpTimer timer(s, "ArgMax");
   const int64_t ncand = argminmax_candidates(rows, cols);
   if (ncand > 0 && (rows > s->arg_rows_cap || ncand > s->arg_cand_cap)) {
     ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
@@ -1039,6 +1043,7 @@ ORT_CUDA_API int ort_cuda_dynamic_quantize_linear(ort_cuda_session* s, const flo
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   DeviceGuard g(s->device);
+  OpTimer timer(s, "DynamicQuantizeLinear");
   if (!s->dqscratch) {
     ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
                "a buffer would grow while a CUDA graph is being captured; run every "
@@ -1080,6 +1085,7 @@ ORT_CUDA_API int ort_cuda_topk(ort_cuda_session* s, const float* X, int64_t rows
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   DeviceGuard g(s->device);
+  OpTimer timer(s, "TopK");
   const bool largest = (flags & ORT_CUDA_TOPK_SMALLEST) == 0;
   const size_t sb = topk_scratch_bytes(rows, cols, k);
   if (sb) {
@@ -1115,6 +1121,7 @@ ORT_CUDA_API int ort_cuda_slice_last_seq(ort_cuda_session* s, const float* X, in
              "slice_last_seq takes device tensors (on the host it is the caller's copy)");
   if (outer == 0 || inner == 0) return ORT_CUDA_OK;
   DeviceGuard g(s->device);
+  OpTimer timer(s, "SliceLastSeq");
   ORTC_CUDA(cudaMemcpy2DAsync(Y, (size_t)inner * 4, X + (seq - 1) * inner, (size_t)(seq * inner) * 4,
                               (size_t)inner * 4, (size_t)outer, cudaMemcpyDeviceToDevice,
                               s->stream));
@@ -1249,6 +1256,7 @@ ORT_CUDA_API int ort_cuda_group_query_attention(
              ORT_CUDA_ERR_INVALID_ARG, "GroupQueryAttention: sizes too large");
   if (batch == 0 || T == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
+  OpTimer timer(s, "GroupQueryAttention");
   const int64_t pcap = kv_capacity ? kv_capacity : past_len;
   const int64_t rcap = kv_capacity ? kv_capacity : T;
 
@@ -1350,6 +1358,7 @@ ORT_CUDA_API int ort_cuda_multi_head_attention(ort_cuda_session* s, const float*
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   if (batch == 0 || seq == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
+  OpTimer timer(s, "MultiHeadAttention");
   HostStage st(host);
   const size_t o_q = st.in(Q, sizeof(float) * batch * seq * hidden);
   const size_t o_k = st.in(K, sizeof(float) * batch * kv_seq * hidden);
@@ -1417,6 +1426,7 @@ ORT_CUDA_API int ort_cuda_fused_sdpa(ort_cuda_session* s, const float* A, const 
              "ORT_CUDA_HOST_IO calls cannot be recorded into a CUDA graph");
   if (n0 == 0 || n1 == 0 || seq == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
+  OpTimer timer(s, "FusedSDPA");
   const int64_t D = head_size, Dv = v_head_size;
   HostStage st(host);
   const size_t o_a = st.in(A, sizeof(float) * n0 * n1 * seq * D);
@@ -1475,6 +1485,7 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
   const int64_t n = batch * seq * heads * head_size;
   if (n == 0) return ORT_CUDA_OK;
   DeviceGuard guard(s->device);
+  OpTimer timer(s, "RotaryEmbedding");
   HostStage st(host);
   const size_t o_x = st.in(X, sizeof(float) * n);
   const size_t o_p = st.in(position_ids, sizeof(int64_t) * (pos_per_batch ? batch : 1) * seq);
@@ -1505,11 +1516,61 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
 
 namespace {
 
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// N-sharded MatMulNBits in a tensor-core mode whose output is too large for
+// the peer exchange buffers (prefill): the rows are cut into chunks, and
+// while the session stream runs the GEMM of chunk c + 1, the exchange
+// stream all-gathers chunk c (NCCL) and re-lays it into Y, so the NVLink
+// transfer overlaps the tensor-core work instead of following it.  yloc is
+// [M, Ns], gath [G, M, Ns] (chunk c's gather lands at rows r0.. of every
+// rank's part, contiguous per chunk), Y [M, N].
+int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_t M,
+                          float* yloc, float* gath, float* Y, int mode) {
+  const int64_t N = w.N, ns = w.ns, G = s->world;
+  const int64_t mc = std::max<int64_t>(256, ((M + 3) / 4 + 127) / 128 * 128);
+  const int64_t nch = (M + mc - 1) / mc;
+  ORTC_CHECK(nch <= 16, ORT_CUDA_ERR_INVALID_ARG, "too many prefill chunks");
+  if (!s->comm_stream)
+    ORTC_CUDA(cudaStreamCreateWithFlags(&s->comm_stream, cudaStreamNonBlocking));
+  for (int i = 0; i <= 16; i++)
+    if (!s->chunk_ev[i])
+      ORTC_CUDA(cudaEventCreateWithFlags(&s->chunk_ev[i], cudaEventDisableTiming));
+  // the exchange stream starts after everything queued before this call
+  ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->stream));
+  ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[16], 0));
+  for (int64_t c = 0; c < nch; c++) {
+    const int64_t r0 = c * mc, m = std::min(mc, M - r0);
+    int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, yloc + r0 * ns, ns, mode, s->stream);
+    if (rc) return rc;
+    ORTC_CUDA(cudaEventRecord(s->chunk_ev[c], s->stream));
+    ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[c], 0));
+    float* g = gath + r0 * ns * G;
+    ncclResult_t r = nccl()->AllGather(yloc + r0 * ns, g, (size_t)(m * ns), ncclFloat,
+                                       (ncclComm_t)s->nccl, s->comm_stream);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return fail(ORT_CUDA_ERR_NCCL, std::string("ncclAllGather: ") + nccl()->GetErrorString(r));
+    if (r == ncclInProgress) {
+      rc = nccl_wait_ready((ncclComm_t)s->nccl, s->timeout_ms);
+      if (rc) {
+        nccl()->CommAbort((ncclComm_t)s->nccl);
+        s->nccl = nullptr;
+        return rc;
+      }
+    }
+    rc = launch_unshard(g, Y + r0 * N, G, m, ns, N, s->comm_stream, &s->launches);
+    if (rc) return rc;
+  }
+  // the session stream continues once every chunk has landed in Y
+  ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->comm_stream));
+  ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->chunk_ev[16], 0));
+  return ORT_CUDA_OK;
+}
+
 // Workspace layout for one op call (byte offsets into s->ws, 256-aligned).
 struct WsLayout {
   size_t a = 0, c = 0, yloc = 0, gath = 0, y = 0, total = 0;
 };
-size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Runs one matmul-family op: stages host IO, computes this rank's columns,
 // all-gathers across ranks, writes back.  `compute` gets device A, C, the
@@ -1568,12 +1629,28 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
   const bool p2p = sharded && p2p_fits(s, M * w.ns);
   s->xsel_offer = p2p;
   s->xsel_taken = false;
+  // a producer that can push its outputs to the peers (decode GEMV) writes
+  // straight into the gathered Y and p2p_land completes the exchange
+  s->push_y = (sharded && p2p_push_fits(s, M, N)) ? dY : nullptr;
+  s->push_taken = false;
+  const bool nccl_path = sharded && !p2p;
+  s->chunk_y = nccl_path ? dY : nullptr;
+  s->chunk_gath = nccl_path ? (float*)(ws + L.gath) : nullptr;
+  s->gathered = false;
   rc = compute(dA, dC, yloc, ldy);
+  const bool pushed = s->push_taken, gathered = s->gathered;
   s->xsel_offer = false;
+  s->push_y = nullptr;
+  s->push_taken = false;
+  s->chunk_y = s->chunk_gath = nullptr;
+  s->gathered = false;
   if (rc) return rc;
-  if (sharded) {
-    rc = p2p ? p2p_gather(s, s->xsel_taken ? nullptr : yloc, M, w.ns, N, dY)
-             : gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
+  if (sharded && !gathered) {
+    if (pushed)
+      rc = p2p_land(s, M, N, w.n0, w.nl, dY);
+    else
+      rc = p2p ? p2p_gather(s, s->xsel_taken ? nullptr : yloc, M, w.ns, N, dY)
+               : gather_y(s, yloc, (float*)(ws + L.gath), dY, M, w.ns, N);
     if (rc) return rc;
   }
   if (host) {
@@ -1611,6 +1688,7 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
   const int mode = mode_of(s, flags);
   ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
   DeviceGuard g(s->device);
+  OpTimer timer(s, "MatMulNBits");
   return run_op(s, w, A, (size_t)(M * w.K) * 4, nullptr, 0, Y, M, flags,
                 [&](const float* dA, const float*, float* yl, int64_t ldy) -> int {
                   if (mode == ORT_CUDA_MODE_STRICT)
@@ -1618,47 +1696,73 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                                             0, 0, 0, s->stream, &s->launches);
                   // tensor-core GEMV over rows [r, r + m): timed plan choice on
                   // the first eager call for (w, m), then the launch
-                  auto gemv_rows = [&](const float* a, int64_t m, float* y,
+                  auto gemv_rows = [&](const float* a, int64_t m, float* y, int64_t ly,
                                        const YSel* ysp) -> int {
+                    if (w.nl == 0) return ORT_CUDA_OK;  // a rank without columns
                     int rc;
                     if (w.gemv_plan[m] < 0 && !s->capturing && gemv_tuning_enabled()) {
                       rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, -1) * 4);
                       if (rc) return rc;
-                      rc = tune_tc_gemv(w, a, m, y, ldy, (float*)s->kscratch, s->err_dev,
+                      rc = tune_tc_gemv(w, a, m, y, ly, (float*)s->kscratch, s->err_dev,
                                         s->sm_count, s->stream, ysp);
                       if (rc) return rc;
                     }
                     const int plan = tc_gemv_plan(w, m, s->sm_count);
                     rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, plan) * 4);
                     if (rc) return rc;
-                    return launch_tc_gemv(w, plan, a, m, y, ldy, (float*)s->kscratch, s->err_dev,
+                    return launch_tc_gemv(w, plan, a, m, y, ly, (float*)s->kscratch, s->err_dev,
                                           s->sm_count, s->stream, &s->launches, ysp);
                   };
-                  if (tc_gemv_ok(w, M)) {
+                  // every rank takes the same path (the exchange that follows
+                  // depends on it), also a rank that holds no columns
+                  auto gemv_ok = [&](int64_t m) {
+                    return w.nl == 0 ? tc_gemv_shape_ok(w, m) : tc_gemv_ok(w, m);
+                  };
+                  if (gemv_ok(M)) {
+                    if (s->push_y) {  // N-sharded: outputs pushed to the peers
+                      YSel ys = p2p_ysel_push(s, w.n0, w.N, 0);
+                      s->push_taken = true;
+                      return gemv_rows(dA, M, s->push_y + w.n0, w.N, &ys);
+                    }
                     YSel ys;
                     if (s->xsel_offer) {
                       ys = p2p_ysel(s);
                       s->xsel_taken = true;
                     }
-                    return gemv_rows(dA, M, yl, s->xsel_offer ? &ys : nullptr);
+                    return gemv_rows(dA, M, yl, ldy, s->xsel_offer ? &ys : nullptr);
                   }
                   // Up to 8 passes of the GEMV over row chunks (each streams the
                   // weight again) still beat the CUDA-core GEMM at decode-sized
                   // M, and every row keeps the exact arithmetic.
                   int cmax = 0;
                   for (int m = 8; m >= 1 && !cmax; m--)
-                    if (tc_gemv_ok(w, m)) cmax = m;
+                    if (gemv_ok(m)) cmax = m;
                   if (cmax > 0 && M > cmax && M <= 8 * cmax) {
+                    const bool push = s->push_y != nullptr;
                     for (int64_t r = 0; r < M; r += cmax) {
                       const int64_t m = std::min<int64_t>(cmax, M - r);
-                      int rc = gemv_rows(dA + r * w.K, m, yl + r * ldy, nullptr);
+                      int rc;
+                      if (push) {
+                        YSel ys = p2p_ysel_push(s, w.n0, w.N, (int)r);
+                        s->push_taken = true;
+                        rc = gemv_rows(dA + r * w.K, m, s->push_y + r * w.N + w.n0, w.N, &ys);
+                      } else {
+                        rc = gemv_rows(dA + r * w.K, m, yl + r * ldy, ldy, nullptr);
+                      }
                       if (rc) return rc;
                     }
                     return ORT_CUDA_OK;
                   }
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
-                      mma_supported_shape(M, w.K))
+                      mma_supported_shape(M, w.K)) {
+                    // the same decision on every rank: it depends on shapes only
+                    if (s->chunk_gath && M >= 512 && !s->capturing && s->nccl) {
+                      s->gathered = true;
+                      return nbits_prefill_chunked(s, w, dA, M, yl, s->chunk_gath, s->chunk_y,
+                                                   mode);
+                    }
                     return launch_mma_nbits(s, w, dA, M, yl, ldy, mode, s->stream);
+                  }
                   return launch_simt_gemm(w, dA, M, false, yl, ldy, false, 1.0f, 1.0f, nullptr, 0,
                                           0, 0, s->stream, &s->launches);
                 });
@@ -1681,6 +1785,7 @@ static int matmul_integer_op(ort_cuda_session* s, const char* name, const void* 
              "MatMulInteger: a_zp must be scalar or per-row [M]");
   if (M == 0) return ORT_CUDA_OK;
   DeviceGuard g(s->device);
+  OpTimer timer(s, "MatMulInteger");
   const size_t zbytes = a_zp ? (size_t)a_zp_len : 0;
   return run_op(s, w, A, (size_t)(M * w.K), a_zp, zbytes, reinterpret_cast<float*>(Y), M, flags,
                 [&](const float* dA, const float* dC, float* yl, int64_t ldy) -> int {
@@ -1716,9 +1821,9 @@ ORT_CUDA_API int ort_cuda_matmul_integer(ort_cuda_session* s, const char* name, 
   return matmul_integer_op(s, name, A, M, a_signed, a_zp, a_zp_len, Y, flags);
 }
 
-static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64_t M,
-                    const float* C, int64_t c_rows, int64_t c_cols, float alpha, float beta,
-                    float* Y, int flags) {
+static int dense_op(ort_cuda_session* s, const char* op_type, const char* name,
+                    const float* A, int64_t M, const float* C, int64_t c_rows, int64_t c_cols,
+                    float alpha, float beta, float* Y, int flags) {
   ORTC_CHECK(s && name, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
   ORTC_CHECK(M >= 0, ORT_CUDA_ERR_INVALID_ARG, "M must be >= 0");
   auto it = s->weights.find(name);
@@ -1740,6 +1845,7 @@ static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64
   ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
   const bool transA = (flags & ORT_CUDA_TRANS_A) != 0;
   DeviceGuard g(s->device);
+  OpTimer timer(s, op_type);
   return run_op(s, w, A, (size_t)(M * w.K) * 4, C, C ? (size_t)(c_rows * c_cols) * 4 : 0, Y, M,
                 flags,
                 [&](const float* dA, const float* dC, float* yl, int64_t ldy) -> int {
@@ -1755,13 +1861,14 @@ static int dense_op(ort_cuda_session* s, const char* name, const float* A, int64
 
 ORT_CUDA_API int ort_cuda_matmul(ort_cuda_session* s, const char* name, const float* A,
                                  int64_t M, float* Y, int flags) {
-  return dense_op(s, name, A, M, nullptr, 0, 0, 1.0f, 1.0f, Y, flags & ~ORT_CUDA_TRANS_A);
+  return dense_op(s, "MatMul", name, A, M, nullptr, 0, 0, 1.0f, 1.0f, Y,
+                  flags & ~ORT_CUDA_TRANS_A);
 }
 
 ORT_CUDA_API int ort_cuda_gemm(ort_cuda_session* s, const char* name, const float* A, int64_t M,
                                const float* C, int64_t c_rows, int64_t c_cols, float alpha,
                                float beta, float* Y, int flags) {
-  return dense_op(s, name, A, M, C, c_rows, c_cols, alpha, beta, Y, flags);
+  return dense_op(s, "Gemm", name, A, M, C, c_rows, c_cols, alpha, beta, Y, flags);
 }
 
 ORT_CUDA_API int ort_cuda_matmul_batched(ort_cuda_session* s, const float* A, const float* B,
@@ -1776,6 +1883,7 @@ ORT_CUDA_API int ort_cuda_matmul_batched(ort_cuda_session* s, const float* A, co
   ORTC_CHECK(A && B && Y, ORT_CUDA_ERR_INVALID_ARG, "NULL pointer");
   const int mode = mode_of(s, flags);
   DeviceGuard g(s->device);
+  OpTimer timer(s, "MatMul");
   const bool strict = mode == ORT_CUDA_MODE_STRICT;
   if (!(flags & ORT_CUDA_HOST_IO))
     return launch_simt_batched(A, B, batch, m, k, n, b_batch_stride, Y, strict, s->stream,

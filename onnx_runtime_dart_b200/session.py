@@ -181,6 +181,49 @@ class CudaSession:
         check(_lib.load().ort_cuda_launch_count(self.handle, ctypes.byref(c)))
         return c.value
 
+    # -- per-op-type device profile (ExecutionProfile, onnx_graph.dart:22-47) --
+    def profile(self, on: bool = True) -> None:
+        """Starts (or stops) recording device time per op type."""
+        check(_lib.load().ort_cuda_profile_enable(self.handle, int(on)),
+              "ort_cuda_profile_enable")
+
+    def profile_reset(self) -> None:
+        check(_lib.load().ort_cuda_profile_reset(self.handle), "ort_cuda_profile_reset")
+
+    def profile_entries(self) -> List[tuple]:
+        """[(op type, calls, device microseconds)], longest first."""
+        L = _lib.load()
+        out, i = [], 0
+        buf = ctypes.create_string_buffer(64)
+        calls, us = ctypes.c_int64(), ctypes.c_double()
+        while True:
+            rc = L.ort_cuda_profile_read(self.handle, i, buf, 64, ctypes.byref(calls),
+                                         ctypes.byref(us))
+            if rc == _lib.ERR_NOT_FOUND:
+                return out
+            check(rc, "ort_cuda_profile_read")
+            out.append((buf.value.decode(), calls.value, us.value))
+            i += 1
+
+    def profile_report(self) -> str:
+        """The text of ExecutionProfile.report(): `op  calls  ms  share%`,
+        sorted by cumulative time, then the total."""
+        ent = self.profile_entries()
+        total = sum(us for _, _, us in ent)
+        lines = [f"{'op':<22}{'calls':>7}{'ms':>10}{'share':>8}"]
+        for op, n, us in ent:
+            share = f"{us * 100 / total:.1f}%" if total else ""
+            lines.append(f"{op:<22}{n:>7}{us / 1000:>10.1f}{share:>8}")
+        lines.append(f"{'total':<29}{total / 1000:>10.1f}")
+        return "\n".join(lines)
+
+    def probe_ffma_tflops(self) -> float:
+        """Measured fp32 FFMA throughput of this session's GPU (TFLOP/s)."""
+        v = ctypes.c_double()
+        check(_lib.load().ort_cuda_probe_ffma(self.handle, ctypes.byref(v)),
+              "ort_cuda_probe_ffma")
+        return v.value
+
     # -- CUDA graphs of device-pointer call sequences -----------------------
     def graph_begin(self) -> None:
         """Records the following device-pointer calls instead of running

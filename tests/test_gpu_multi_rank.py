@@ -62,14 +62,33 @@ def _rank_main(rank, port):
             B, sc, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True)
             s.upload_nbits(name, B, sc, z, k=K, n=N, block_size=bs)
             W[name] = (B, sc, z, K, N, bs)
-        # decode: exact mode against the oracle
+        # a dense weight: its sharded Gemm exchanges Y by peer loads (pull),
+        # interleaved below with the GEMV's pushes (both advance one epoch)
+        Wd = rng.standard_normal((256, 640)).astype(np.float32)
+        s.upload_dense("d", Wd, trans_b=False)
+        # decode: exact mode against the oracle, and bit for bit against a
+        # single-GPU session (rank 0): M <= 8 pushes from one GEMV pass, M = 16
+        # from two passes of 8 rows
+        got = {}
         for name in ("tm", "sk"):
             B, sc, z, K, N, bs = W[name]
-            for M in (1, 3):
+            for M in (1, 3, 16):
                 A = rng.standard_normal((M, K)).astype(np.float32)
                 y = s.matmul_nbits(name, A)
+                yd = s.gemm("d", rng.standard_normal((M, 256)).astype(np.float32))
                 ref = O.matmul_nbits(A, B, sc, z, K, N, 4, bs, threads=8)
                 out[f"{name}{M}"] = float(np.abs(y - ref).max() / np.abs(ref).max())
+                got[(name, M)] = (A, y)
+                got[("d", M)] = yd
+        if rank == 0:
+            one = CudaSession(rank)
+            for name in ("tm", "sk"):
+                B, sc, z, K, N, bs = W[name]
+                one.upload_nbits(name, B, sc, z, k=K, n=N, block_size=bs)
+                for M in (1, 3, 16):
+                    A, y = got[(name, M)]
+                    out[f"bitwise_{name}{M}"] = bool(np.array_equal(one.matmul_nbits(name, A), y))
+            one.close()
         # prefill-sized output (4096 x 4096 floats per rank): NCCL path
         B, sc, z, K, N, bs = W["pf"]
         A = rng.standard_normal((4096, K)).astype(np.float32)
@@ -134,7 +153,10 @@ def test_two_gpu_sharded_results():
     for r in range(WORLD):
         ok, val = res[r]
         assert ok, val
-        for key in ("tm1", "tm3", "sk1", "sk3"):
+        for key in ("tm1", "tm3", "tm16", "sk1", "sk3", "sk16"):
             assert val[key] <= 1e-5, (r, key, val[key])
+        if r == 0:
+            for key in ("tm1", "tm3", "tm16", "sk1", "sk3", "sk16"):
+                assert val["bitwise_" + key], key
         assert val["pf"] <= 2e-3, (r, val["pf"])
         assert val["graph_same"], r

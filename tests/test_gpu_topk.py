@@ -54,7 +54,11 @@ def _planted(rng, rows, cols):
 
 
 @pytest.mark.parametrize("rows,cols,k", [(1, 1, 1), (3, 7, 7), (5, 1000, 50), (5, 4096, 1024),
-                                         (2, 128256, 40), (5, 3000, 1)])
+                                         (2, 128256, 40), (5, 3000, 1),
+                                         # segmented rows at the largest k, and a
+                                         # 256000-column row at its k limit (7
+                                         # segments of 40960 columns, 7 x 585 <= 4096)
+                                         (3, 128256, 1024), (2, 256000, 585)])
 @pytest.mark.parametrize("largest", [True, False])
 def test_topk_matches_oracle(sess, rows, cols, k, largest):
     rng = np.random.default_rng(rows * 131 + cols + k)
@@ -98,3 +102,6 @@ def test_topk_rejects_bad_k(sess):
         sess.topk(x, 11)
     with pytest.raises(UnsupportedError):
         sess.topk(np.zeros((1, 2000), np.float32), 1025)
+    # one past the segment limit of a 256000-column row (stated in ort_cuda.h)
+    with pytest.raises(UnsupportedError, match="k <= 585"):
+        sess.topk(np.zeros((1, 256000), np.float32), 586)
