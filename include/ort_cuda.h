@@ -116,6 +116,14 @@ ORT_CUDA_API int ort_cuda_nccl_unique_id(void* id128);
 ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void* nccl_id128,
                                     int mode, int timeout_ms, ort_cuda_session** out);
 
+/* Bound, in milliseconds, of every wait of this rank's kernels for a peer
+ * GPU (its flag or its data) in the exchange of Y (default 1000).  When a
+ * peer does not arrive in time the waiting kernel stops, records the
+ * failure and returns; the next synchronising call reports
+ * ORT_CUDA_ERR_TIMEOUT (a rank that skipped an operation or stopped is
+ * detected this way, without any unbounded wait on the device). */
+ORT_CUDA_API int ort_cuda_set_peer_wait(ort_cuda_session* s, int ms);
+
 /* Frees every device buffer of the session (OnnxModel.dispose,
  * lib/onnx_runtime_dart.dart:140). */
 ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s);
@@ -400,6 +408,27 @@ ORT_CUDA_API int ort_cuda_rotary_embedding(ort_cuda_session* s, const float* X,
 #define ORT_CUDA_TOPK_SMALLEST 0x800
 ORT_CUDA_API int ort_cuda_topk(ort_cuda_session* s, const float* X, int64_t rows, int64_t cols,
                                int64_t ldx, int64_t k, float* values, int64_t* indices, int flags);
+
+/* MatMulNBits followed by ArgMax (ArgMin with ORT_CUDA_ARG_MIN; ties to
+ * the last index with ORT_CUDA_ARG_SELECT_LAST) over the last axis of its
+ * output: the greedy step after lm_head, fused.  The reference runs the two
+ * nodes one after the other (opMatMulNBits, onnx_qlinear_ops.dart:114-156,
+ * then opArgMinMax, onnx_ops.dart:2198-2237, on the last-token logits of
+ * the lastTokenLogits rewrite, onnx_graph.dart:407-470); here, on one GPU
+ * and in the non-STRICT modes for M <= 64, every value the decode GEMV
+ * stores also enters a per-row (value, index) key, CTAs fold their keys
+ * with atomics and the last CTA writes the indices, so no separate pass
+ * re-reads the logits.  Otherwise (N-sharded sessions, STRICT, larger M)
+ * the call runs the two operations in turn; the indices are the same
+ * either way: those of ort_cuda_argmax on this call's logits.
+ *   indices  [M] int64 (device, or host with ORT_CUDA_HOST_IO)
+ *   Y        the [M x N] logits, or NULL when the caller does not want them
+ * flags: ORT_CUDA_HOST_IO, ORT_CUDA_FLAGS_MODE(m), ORT_CUDA_ARG_MIN,
+ * ORT_CUDA_ARG_SELECT_LAST.  The first fused call of a session sets up a
+ * small key buffer; make it before capturing a CUDA graph. */
+ORT_CUDA_API int ort_cuda_matmul_nbits_argmax(ort_cuda_session* s, const char* name,
+                                              const float* A, int64_t M, int64_t* indices,
+                                              float* Y, int flags);
 
 /* _SliceLastSeq (onnx_graph.dart:456-473, inserted before the vocab
  * projection by the lastTokenLogits rewrite, :398-451): Y[o][i] =

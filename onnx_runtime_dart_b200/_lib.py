@@ -112,6 +112,8 @@ SIGNATURES = {
     "ort_cuda_profile_read": (_int, [_vp, _int, _cp, _int, ctypes.POINTER(_i64),
                                      ctypes.POINTER(ctypes.c_double)]),
     "ort_cuda_probe_ffma": (_int, [_vp, ctypes.POINTER(ctypes.c_double)]),
+    "ort_cuda_matmul_nbits_argmax": (_int, [_vp, _cp, _vp, _i64, _vp, _vp, _int]),
+    "ort_cuda_set_peer_wait": (_int, [_vp, _int]),
 }
 
 _lib = None

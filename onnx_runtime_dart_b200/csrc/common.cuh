@@ -158,7 +158,23 @@ struct ort_cuda_session {
   float* chunk_gath = nullptr;
   bool gathered = false;
   cudaStream_t comm_stream = nullptr;  // the chunks' all-gathers and re-layouts
+  // fused MatMulNBits + ArgMax: staging of host A / indices and unwanted
+  // logits (grow-only), and the rows' keys (zero between calls)
+  void* aux = nullptr;
+  size_t aux_bytes = 0;
+  void* amaxbuf = nullptr;
   cudaEvent_t chunk_ev[17] = {};       // chunk c computed; [16]: exchange done
+  // big exchange buffer for prefill-sized outputs (csrc/p2p.cu): flags then
+  // three thirds of bcap floats; bpeer[r] is rank r's, mapped here; chunk
+  // epochs are counted on the host (bepoch, the same on every rank) and
+  // big_ev[e % 3] marks this rank's gather of epoch e done
+  void* bbuf = nullptr;
+  void* bpeer[8] = {};
+  size_t bcap = 0;
+  unsigned long long bepoch = 0;
+  cudaEvent_t big_ev[3] = {};
+  // bound of every wait for a peer GPU's flag or data (ms)
+  int peer_wait_ms = 1000;
   // CUDA graphs captured from the session stream (ort_cuda_graph_*)
   struct Graph {
     cudaGraphExec_t exec;
@@ -215,6 +231,11 @@ int ensure_pinned(ort_cuda_session* s, size_t bytes);
 //    the values into its own Y.  A 64-bit store is single-copy atomic, so
 //    a word whose tag reads e holds this epoch's value: no fence and no
 //    flag is needed between producer and consumer.
+//  - fused ArgMax / ArgMin (amax non-null, independent of the modes above):
+//    every stored value also enters the row's running key (amax_key) in the
+//    CTA's shared memory; each CTA folds its keys into amax[row] with a
+//    global atomic max, and the grid's last CTA writes amax_out[row] and
+//    returns amax[] and its flags to zero (see amax_finish).
 struct YSel {
   float* half0 = nullptr;
   int64_t cap = 0;
@@ -223,7 +244,68 @@ struct YSel {
   int rank = 0, world = 0, row0 = 0;
   int64_t n0 = 0, N = 0, llcap = 0;
   unsigned long long* ll[8] = {};
+  // amax: [amax_rows] keys, then [amax_rows] u32 flags (column 0 is NaN),
+  // then a u32 CTA ticket; zero between calls
+  unsigned long long* amax = nullptr;
+  int64_t* amax_out = nullptr;
+  int amax_rows = 0, amax_min = 0, amax_last = 0;
 };
+
+// ArgMax order of the reference's scan (opArgMinMax, onnx_ops.dart:2198-2237):
+// the best non-NaN element under "larger value, then smaller index" (the
+// larger index with select_last_index; ArgMin ranks -v), -0.0 equal to 0.0,
+// as one unsigned key whose maximum is the answer; 0 for NaN (which wins
+// only as element 0: handled by the column-0 flag).
+__device__ __forceinline__ unsigned long long amax_key(float v, int64_t col, int is_min,
+                                                       int last) {
+  if (v != v) return 0ull;
+  unsigned u = __float_as_uint(is_min ? -v : v);
+  if ((u << 1) == 0u) u = 0u;  // -0.0 -> +0.0
+  const unsigned o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  const unsigned ix = last ? (unsigned)col : 0xFFFFFFFFu - (unsigned)col;
+  return ((unsigned long long)o << 32) | ix;
+}
+// Enters value v of local row m, local column n into the CTA's keys.
+__device__ __forceinline__ void amax_add(const YSel& s, unsigned long long* s_keys,
+                                         unsigned* s_nan0, int m, int n, float v) {
+  const int64_t col = s.n0 + n;
+  if (col == 0 && v != v) atomicOr(s_nan0, 1u << m);
+  const unsigned long long k = amax_key(v, col, s.amax_min, s.amax_last);
+  if (k) atomicMax(s_keys + m, k);
+}
+// Called by every thread of the CTA once its stores are done (after a
+// CTA-wide barrier): folds the CTA's keys of rows row0 .. row0 + M - 1 into
+// the grid's, and the last CTA decodes and resets them.
+__device__ __forceinline__ void amax_finish(const YSel& s, const unsigned long long* s_keys,
+                                            const unsigned* s_nan0, unsigned* s_last, int M) {
+  unsigned long long* keys = s.amax;
+  unsigned* nan0 = reinterpret_cast<unsigned*>(keys + s.amax_rows);
+  unsigned* ticket = nan0 + s.amax_rows;
+  if ((int)threadIdx.x < M) {
+    const int row = s.row0 + (int)threadIdx.x;
+    if (s_keys[threadIdx.x]) atomicMax(keys + row, s_keys[threadIdx.x]);
+    if ((*s_nan0 >> threadIdx.x) & 1u) atomicOr(nan0 + row, 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    *s_last = atomicAdd(ticket, 1u) == gridDim.x * gridDim.y * gridDim.z - 1 ? 1u : 0u;
+  }
+  __syncthreads();
+  if (*s_last) {
+    __threadfence();
+    if ((int)threadIdx.x < M) {
+      const int row = s.row0 + (int)threadIdx.x;
+      const unsigned long long k = *reinterpret_cast<volatile unsigned long long*>(keys + row);
+      const unsigned nf = *reinterpret_cast<volatile unsigned*>(nan0 + row);
+      const unsigned lo = (unsigned)k;
+      s.amax_out[row] = (nf || k == 0ull) ? 0 : (int64_t)(s.amax_last ? lo : 0xFFFFFFFFu - lo);
+      keys[row] = 0ull;
+      nan0[row] = 0u;
+    }
+    if (threadIdx.x == 0) *ticket = 0u;
+  }
+}
 __device__ __forceinline__ unsigned long long ysel_epoch(const YSel& s) {
   return s.ctr ? *reinterpret_cast<const volatile unsigned long long*>(s.ctr) + 1 : 0ull;
 }
@@ -267,6 +349,15 @@ YSel p2p_ysel_push(ort_cuda_session* s, int64_t n0, int64_t N, int row0);
 // words of this epoch and copies them into Y [M, N] (row pitch N); this
 // rank's columns [n0, n0 + nl) are already there.  Advances the epoch.
 int p2p_land(ort_cuda_session* s, int64_t M, int64_t N, int64_t n0, int64_t nl, float* Y);
+// Big exchange buffer of three thirds of at least third_floats floats on
+// every rank (a collective: every rank calls it with the same size); *ok
+// false when a peer could not be mapped (every rank then sees false).
+int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok);
+float* p2p_big_third(ort_cuda_session* s, unsigned long long epoch);
+// Gathers chunk `epoch` ([m, Ns] per rank, in each rank's third epoch % 3)
+// into Y rows (pitch N) on stream st.
+int p2p_chunk_gather(ort_cuda_session* s, unsigned long long epoch, int64_t m, int64_t Ns,
+                     int64_t N, float* Y, cudaStream_t st);
 // `local` null: the producer already wrote the slice with p2p_ysel().
 int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, int64_t N,
                float* Y);

@@ -277,6 +277,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* ibar = xsync + 1;
   uint64_t* abar = ibar + 1;  // [2] a chunk of A staged (bulk copies, M >= 3)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(abar + 2);
+  // fused ArgMax: the CTA's row keys, column-0 NaN flags, last-CTA flag
+  unsigned long long* s_amax = reinterpret_cast<unsigned long long*>(tmem_slot + 2);
+  unsigned* s_nan0 = reinterpret_cast<unsigned*>(s_amax + 8);
+  unsigned* s_last = s_nan0 + 1;
   const bool clustered = p.tile_major && p.csize > 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -297,6 +301,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
     mbar_init(fin, 1);
     mbar_init(xsync, kDeWarps);
+    for (int m = 0; m < 8; m++) s_amax[m] = 0ull;
+    *s_nan0 = 0u;
     mbar_init(ibar, p.csize * kEpiWarps);
     mbar_init(&abar[0], 1);
     mbar_init(&abar[1], 1);
@@ -807,8 +813,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         for (int m = 0; m < M; m++) {
           const float acc = chunk == 0 ? 0.0f + part[m] : ya[m * kTile + nl] + part[m];
           ya[m * kTile + nl] = acc;
-          if (chunk == p.nch - 1 && n < p.N)
+          if (chunk == p.nch - 1 && n < p.N) {
             ysel_store(ysel_base(p.Y, p.ysel), p.ldy, p.ysel, ep, m, n, acc);
+            if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+          }
         }
       } else if (clustered) {
         // into the inbox of the CTA that sums this tile: rank ti % csize,
@@ -865,7 +873,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               for (int u = 0; u < 8; u++) acc = acc + v[u];
             }
             for (; c < p.nch; c++) acc = acc + col[(size_t)c * per];
-            if (n < p.N) ysel_store(Yb, p.ldy, p.ysel, ep, m, n, acc);
+            if (n < p.N) {
+              ysel_store(Yb, p.ldy, p.ysel, ep, m, n, acc);
+              if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+            }
           }
         }
       }
@@ -880,6 +891,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  // the split-K GEMV stores partials only; its chunk-sum kernel does this
+  if (p.ysel.amax && p.tile_major) amax_finish(p.ysel, s_amax, s_nan0, s_last, M);
 }
 
 // Split-K: Y[m, n] = ((0 + part[0]) + part[1]) + ... in chunk order, the same
@@ -889,6 +902,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __restrict__ part,
                                                            float* Y, int64_t ldy, int M, int N,
                                                            int nch, int64_t npad, YSel ysel) {
+  __shared__ unsigned long long s_amax[8];
+  __shared__ unsigned s_nan0, s_last;
+  if (threadIdx.x < 8) s_amax[threadIdx.x] = 0ull;
+  if (threadIdx.x == 0) s_nan0 = 0u;
+  __syncthreads();
   griddep_launch_dependents();
   griddep_wait();
   Y = ysel_base(Y, ysel);
@@ -911,6 +929,11 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
         if (c0 + c < nch) acc = acc + v[c];
     }
     ysel_store(Y, ldy, ysel, ep, m, n, acc);
+    if (ysel.amax) amax_add(ysel, s_amax, &s_nan0, m, n, acc);
+  }
+  if (ysel.amax) {
+    __syncthreads();
+    amax_finish(ysel, s_amax, &s_nan0, &s_last, M);
   }
 }
 

@@ -19,6 +19,7 @@
 // does only after its own read finished: two halves are enough.  The epoch
 // lives on the device, so the sequence replays unchanged from a CUDA graph.
 // No NCCL and no multicast is on the per-operation path.
+#include <algorithm>
 #include <climits>
 #include <cstring>
 #include <vector>
@@ -46,6 +47,7 @@ struct P2PArgs {
   int64_t ldy;
   int M, Ns, N, rank, world;
   int* err;
+  uint64_t wait_ns;  // bound of the wait for the peers' flags
 };
 
 __device__ __forceinline__ unsigned long long next_epoch(const unsigned long long* mine) {
@@ -91,7 +93,7 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
         unsigned long long v;
         asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.mine + r) : "memory");
         if (v >= e) break;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > a.wait_ns) {
           record_error(a.err, KERR_WAIT_PEER);
           ok = 0;
           break;
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const P2PArgs a) {
 __global__ void __launch_bounds__(256) p2p_land_kernel(const unsigned long long* ll0,
                                                        int64_t llcap, unsigned long long* mine,
                                                        float* Y, int M, int N, int n0, int nl,
-                                                       int* err) {
+                                                       int* err, uint64_t wait_ns) {
   __shared__ unsigned long long epoch;
   griddep_launch_dependents();
   griddep_wait();
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(256) p2p_land_kernel(const unsigned long long*
       if (at[u] < 0 || !ok) continue;
       while ((unsigned)(w[u] >> 32) != tag) {
         if (t0 == 0) t0 = globaltimer();
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > wait_ns) {
           record_error(err, KERR_WAIT_PEER);
           ok = false;
           break;
@@ -199,6 +201,105 @@ __global__ void __launch_bounds__(256) p2p_land_kernel(const unsigned long long*
       mine[kDoneSlot] = 0;
       __threadfence();
       *reinterpret_cast<volatile unsigned long long*>(mine + kCtrSlot) = e;
+    }
+  }
+}
+
+// Prefill-sized outputs, one row chunk at a time (p2p_chunk_gather): every
+// rank's GEMM wrote its [m, Ns] chunk into one of the three thirds of its
+// big exchange buffer; this kernel posts the chunk's epoch (a host counter,
+// the same on every rank) into each peer's flag slot for this rank, waits
+// (bounded) for every peer's post of that epoch, and copies all ranks'
+// slices into Y's rows with 16-byte loads and stores.  It runs on the
+// exchange stream beside the next chunk's GEMM: it uses no dynamic shared
+// memory and few registers, so its CTAs fit on the SMs next to the GEMM's.
+struct ChunkArgs {
+  const float* src[8];           // rank r's third holding this chunk, [m][Ns]
+  unsigned long long* flag[8];   // rank r's flag slot for this rank
+  const unsigned long long* mine;  // this rank's flags (slot r posted by rank r)
+  unsigned long long epoch;
+  float* Y;                      // the chunk's first row of Y
+  int64_t ldy;
+  int m, Ns, N, rank, world;
+  int* err;
+  uint64_t wait_ns;
+};
+
+constexpr int kChunkV = 4;  // float4 per thread and round
+
+__global__ void __launch_bounds__(256) p2p_chunk_gather_kernel(const ChunkArgs a) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    // every CTA posts (the same value): whichever is resident first does
+    for (int r = 0; r < a.world; r++)
+      if (r != a.rank)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(a.epoch)
+                     : "memory");
+    const uint64_t t0 = globaltimer();
+    for (int r = 0; r < a.world && ok; r++) {
+      if (r == a.rank) continue;
+      for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.mine + r) : "memory");
+        if (v >= a.epoch) break;
+        if (globaltimer() - t0 > a.wait_ns) {
+          record_error(a.err, KERR_WAIT_PEER);
+          ok = 0;
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const bool vec = (a.N % 4) == 0 && (a.Ns % 4) == 0 && (a.ldy % 4) == 0;
+  // work units: (row, rank, 4-column group) in row-major order of the
+  // rank's slice; slices of a row are contiguous in src
+  const int per_row4 = (a.Ns + 3) / 4;
+  const int64_t units = (int64_t)a.m * a.world * per_row4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u0 < units;
+       u0 += stride * kChunkV) {
+    float4 v[kChunkV];
+    int64_t dst[kChunkV];
+    int cnt[kChunkV];
+#pragma unroll
+    for (int t = 0; t < kChunkV; t++) {
+      const int64_t u = u0 + t * stride;
+      cnt[t] = 0;
+      if (u >= units) continue;
+      const int j4 = (int)(u % per_row4);
+      const int64_t rr = u / per_row4;
+      const int r = (int)(rr % a.world), row = (int)(rr / a.world);
+      const int c0 = r * a.Ns + j4 * 4;
+      cnt[t] = max(0, min(4, a.N - c0));
+      cnt[t] = min(cnt[t], a.Ns - j4 * 4);
+      if (cnt[t] <= 0) continue;
+      const float* s = a.src[r] + (int64_t)row * a.Ns + j4 * 4;
+      dst[t] = (int64_t)row * a.ldy + c0;
+      if (vec && cnt[t] == 4) {
+        v[t] = __ldcv(reinterpret_cast<const float4*>(s));
+      } else {
+        v[t].x = __ldcv(s);
+        v[t].y = cnt[t] > 1 ? __ldcv(s + 1) : 0.f;
+        v[t].z = cnt[t] > 2 ? __ldcv(s + 2) : 0.f;
+        v[t].w = cnt[t] > 3 ? __ldcv(s + 3) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kChunkV; t++) {
+      if (cnt[t] <= 0) continue;
+      float* d = a.Y + dst[t];
+      if (vec && cnt[t] == 4) {
+        *reinterpret_cast<float4*>(d) = v[t];
+      } else {
+        d[0] = v[t].x;
+        if (cnt[t] > 1) d[1] = v[t].y;
+        if (cnt[t] > 2) d[2] = v[t].z;
+        if (cnt[t] > 3) d[3] = v[t].w;
+      }
     }
   }
 }
@@ -281,6 +382,117 @@ int p2p_setup(ort_cuda_session* s) {
   return ORT_CUDA_OK;
 }
 
+namespace {
+constexpr size_t kBigFlagBytes = 4096;
+
+void big_unmap(ort_cuda_session* s) {
+  for (int r = 0; r < 8; r++) {
+    if (s->bpeer[r] && r != s->rank) cudaIpcCloseMemHandle(s->bpeer[r]);
+    s->bpeer[r] = nullptr;
+  }
+  if (s->bbuf) cudaFree(s->bbuf);
+  s->bbuf = nullptr;
+  s->bcap = 0;
+}
+}  // namespace
+
+int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok) {
+  *ok = false;
+  if (!s->p2p_ok || !s->nccl) return ORT_CUDA_OK;
+  if (s->bbuf && s->bcap >= third_floats) {
+    *ok = true;
+    return ORT_CUDA_OK;
+  }
+  // Every rank reaches this with the same size (the shapes are the same on
+  // all ranks).  The old buffer goes first: nobody reads it any more once
+  // every rank has synchronised its streams and passed the handshake below.
+  ORTC_CUDA(cudaDeviceSynchronize());
+  std::vector<char> sync;
+  const char one = 1;
+  int rc = host_allgather(s, &one, 1, &sync);
+  if (rc) return rc;
+  big_unmap(s);
+  const size_t want = (third_floats + 63) / 64 * 64;
+  bool mine_ok = cudaMalloc(&s->bbuf, kBigFlagBytes + 3 * want * 4) == cudaSuccess;
+  if (!mine_ok) {
+    cudaGetLastError();
+    s->bbuf = nullptr;
+  }
+  cudaIpcMemHandle_t h;
+  std::memset(&h, 0, sizeof(h));
+  if (mine_ok) {
+    mine_ok = cudaMemset(s->bbuf, 0, kBigFlagBytes) == cudaSuccess &&
+              cudaDeviceSynchronize() == cudaSuccess &&
+              cudaIpcGetMemHandle(&h, s->bbuf) == cudaSuccess;
+    cudaGetLastError();
+  }
+  std::vector<char> handles;
+  rc = host_allgather(s, &h, sizeof(h), &handles);
+  if (rc) return rc;
+  for (int r = 0; r < s->world && mine_ok; r++) {
+    if (r == s->rank) {
+      s->bpeer[r] = s->bbuf;
+      continue;
+    }
+    cudaIpcMemHandle_t hr;
+    std::memcpy(&hr, handles.data() + r * sizeof(hr), sizeof(hr));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess)
+      s->bpeer[r] = p;
+    else
+      mine_ok = false;
+  }
+  cudaGetLastError();
+  const char c = mine_ok ? 1 : 0;
+  std::vector<char> oks;
+  rc = host_allgather(s, &c, 1, &oks);
+  if (rc) return rc;
+  bool all_ok = true;
+  for (char o : oks) all_ok = all_ok && o == 1;
+  if (!all_ok) {
+    big_unmap(s);
+    return ORT_CUDA_OK;  // every rank keeps the NCCL path
+  }
+  s->bcap = want;
+  *ok = true;
+  return ORT_CUDA_OK;
+}
+
+float* p2p_big_third(ort_cuda_session* s, unsigned long long epoch) {
+  return (float*)((char*)s->bbuf + kBigFlagBytes) + (size_t)(epoch % 3) * s->bcap;
+}
+
+int p2p_chunk_gather(ort_cuda_session* s, unsigned long long epoch, int64_t m, int64_t Ns,
+                     int64_t N, float* Y, cudaStream_t st) {
+  ChunkArgs a;
+  for (int r = 0; r < 8; r++) {
+    a.src[r] = nullptr;
+    a.flag[r] = nullptr;
+  }
+  for (int r = 0; r < s->world; r++) {
+    a.src[r] = (const float*)((char*)s->bpeer[r] + kBigFlagBytes) + (size_t)(epoch % 3) * s->bcap;
+    a.flag[r] = (unsigned long long*)s->bpeer[r] + s->rank;
+  }
+  a.mine = (const unsigned long long*)s->bbuf;
+  a.epoch = epoch;
+  a.Y = Y;
+  a.ldy = N;
+  a.m = (int)m;
+  a.Ns = (int)Ns;
+  a.N = (int)N;
+  a.rank = s->rank;
+  a.world = s->world;
+  a.err = s->err_dev;
+  a.wait_ns = (uint64_t)s->peer_wait_ms * 1000000ull;
+  const int64_t units = m * s->world * ((Ns + 3) / 4);
+  const unsigned blocks = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>((units + 256 * kChunkV - 1) / (256 * kChunkV), s->sm_count * 2));
+  p2p_chunk_gather_kernel<<<blocks, 256, 0, st>>>(a);
+  ORTC_CUDA(cudaGetLastError());
+  s->launches++;
+  return ORT_CUDA_OK;
+}
+
 void p2p_teardown(ort_cuda_session* s) {
   if (s->xbuf && s->nccl) {
     // no rank unmaps or frees before every rank's last read has finished
@@ -288,6 +500,7 @@ void p2p_teardown(ort_cuda_session* s) {
     const char one = 1;
     host_allgather(s, &one, 1, &all);
   }
+  big_unmap(s);
   for (int r = 0; r < 8; r++)
     if (s->xpeer[r] && r != s->rank) cudaIpcCloseMemHandle(s->xpeer[r]);
   if (s->xbuf) cudaFree(s->xbuf);
@@ -337,7 +550,8 @@ int p2p_land(ort_cuda_session* s, int64_t M, int64_t N, int64_t n0, int64_t nl, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   ORTC_CUDA(cudaLaunchKernelEx(&cfg, p2p_land_kernel, ll0, (int64_t)s->llcap, mine, Y, (int)M,
-                               (int)N, (int)n0, (int)nl, s->err_dev));
+                               (int)N, (int)n0, (int)nl, s->err_dev,
+                               (uint64_t)s->peer_wait_ms * 1000000ull));
   s->launches++;
   return ORT_CUDA_OK;
 }
@@ -382,6 +596,7 @@ int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, i
   a.rank = s->rank;
   a.world = s->world;
   a.err = s->err_dev;
+  a.wait_ns = (uint64_t)s->peer_wait_ms * 1000000ull;
   const int64_t total = M * N;
   const unsigned blocks = (unsigned)std::max<int64_t>(
       1, std::min<int64_t>((total + 256 * kPull - 1) / (256 * kPull), s->sm_count * 4));

@@ -431,7 +431,11 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   s->graphs.clear();
   profile_free(s);
   if (s->sync_ev) cudaEventDestroy(s->sync_ev);
+  if (s->aux) cudaFree(s->aux);
+  if (s->amaxbuf) cudaFree(s->amaxbuf);
   for (cudaEvent_t& e : s->chunk_ev)
+    if (e) cudaEventDestroy(e);
+  for (cudaEvent_t& e : s->big_ev)
     if (e) cudaEventDestroy(e);
   if (s->comm_stream) cudaStreamDestroy(s->comm_stream);
   s->comm_stream = nullptr;
@@ -465,6 +469,14 @@ ORT_CUDA_API int ort_cuda_sync(ort_cuda_session* s) {
   ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG, "cannot synchronise during a capture");
   DeviceGuard g(s->device);
   return bounded_sync(s);
+}
+
+ORT_CUDA_API int ort_cuda_set_peer_wait(ort_cuda_session* s, int ms) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  ORTC_CHECK(ms >= 1 && ms <= 600000, ORT_CUDA_ERR_INVALID_ARG,
+             "peer wait must be 1 .. 600000 ms");
+  s->peer_wait_ms = ms;
+  return ORT_CUDA_OK;
 }
 
 ORT_CUDA_API int ort_cuda_rank_info(ort_cuda_session* s, int* rank, int* world) {
@@ -1528,7 +1540,7 @@ size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_t M,
                           float* yloc, float* gath, float* Y, int mode) {
   const int64_t N = w.N, ns = w.ns, G = s->world;
-  const int64_t mc = std::max<int64_t>(256, ((M + 3) / 4 + 127) / 128 * 128);
+  const int64_t mc = std::max<int64_t>(256, ((M + 7) / 8 + 127) / 128 * 128);
   const int64_t nch = (M + mc - 1) / mc;
   ORTC_CHECK(nch <= 16, ORT_CUDA_ERR_INVALID_ARG, "too many prefill chunks");
   if (!s->comm_stream)
@@ -1536,9 +1548,36 @@ int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_
   for (int i = 0; i <= 16; i++)
     if (!s->chunk_ev[i])
       ORTC_CUDA(cudaEventCreateWithFlags(&s->chunk_ev[i], cudaEventDisableTiming));
+  for (int i = 0; i < 3; i++)
+    if (!s->big_ev[i]) ORTC_CUDA(cudaEventCreateWithFlags(&s->big_ev[i], cudaEventDisableTiming));
+  bool big = false;
+  int rc0 = p2p_big_ensure(s, (size_t)(mc * ns), &big);
+  if (rc0) return rc0;
   // the exchange stream starts after everything queued before this call
   ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->stream));
   ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[16], 0));
+  if (big) {
+    // Peer memory: each chunk's GEMM writes into a third of this rank's
+    // big exchange buffer and the chunk gather (pull over NVLink, beside
+    // the next chunk's GEMM) fills Y.  Third e % 3 is written again at epoch
+    // e + 3, after this rank's gather of epoch e + 1 finished: that gather
+    // saw every peer post e + 1, which each does after its gather of e.
+    for (int64_t c = 0; c < nch; c++) {
+      const int64_t r0 = c * mc, m = std::min(mc, M - r0);
+      const unsigned long long e = ++s->bepoch;
+      if (e >= 3) ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->big_ev[(e - 2) % 3], 0));
+      int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, p2p_big_third(s, e), ns, mode, s->stream);
+      if (rc) return rc;
+      ORTC_CUDA(cudaEventRecord(s->chunk_ev[c], s->stream));
+      ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[c], 0));
+      rc = p2p_chunk_gather(s, e, m, ns, N, Y + r0 * N, s->comm_stream);
+      if (rc) return rc;
+      ORTC_CUDA(cudaEventRecord(s->big_ev[e % 3], s->comm_stream));
+    }
+    ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->comm_stream));
+    ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->chunk_ev[16], 0));
+    return ORT_CUDA_OK;
+  }
   for (int64_t c = 0; c < nch; c++) {
     const int64_t r0 = c * mc, m = std::min(mc, M - r0);
     int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, yloc + r0 * ns, ns, mode, s->stream);
@@ -1669,6 +1708,26 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
   return ORT_CUDA_OK;
 }
 
+// Tensor-core GEMV over m <= 8 rows: timed plan choice on the first eager
+// call for (w, m), then the launch.
+int gemv_call(ort_cuda_session* s, Weight& w, const float* a, int64_t m, float* y, int64_t ly,
+              const YSel* ysp) {
+  if (w.nl == 0) return ORT_CUDA_OK;  // a rank without columns
+  int rc;
+  if (w.gemv_plan[m] < 0 && !s->capturing && gemv_tuning_enabled()) {
+    rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, -1) * 4);
+    if (rc) return rc;
+    rc = tune_tc_gemv(w, a, m, y, ly, (float*)s->kscratch, s->err_dev, s->sm_count, s->stream,
+                      ysp);
+    if (rc) return rc;
+  }
+  const int plan = tc_gemv_plan(w, m, s->sm_count);
+  rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, plan) * 4);
+  if (rc) return rc;
+  return launch_tc_gemv(w, plan, a, m, y, ly, (float*)s->kscratch, s->err_dev, s->sm_count,
+                        s->stream, &s->launches, ysp);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1694,24 +1753,9 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if (mode == ORT_CUDA_MODE_STRICT)
                     return launch_simt_gemm(w, dA, M, false, yl, ldy, true, 1.0f, 1.0f, nullptr,
                                             0, 0, 0, s->stream, &s->launches);
-                  // tensor-core GEMV over rows [r, r + m): timed plan choice on
-                  // the first eager call for (w, m), then the launch
                   auto gemv_rows = [&](const float* a, int64_t m, float* y, int64_t ly,
                                        const YSel* ysp) -> int {
-                    if (w.nl == 0) return ORT_CUDA_OK;  // a rank without columns
-                    int rc;
-                    if (w.gemv_plan[m] < 0 && !s->capturing && gemv_tuning_enabled()) {
-                      rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, -1) * 4);
-                      if (rc) return rc;
-                      rc = tune_tc_gemv(w, a, m, y, ly, (float*)s->kscratch, s->err_dev,
-                                        s->sm_count, s->stream, ysp);
-                      if (rc) return rc;
-                    }
-                    const int plan = tc_gemv_plan(w, m, s->sm_count);
-                    rc = ensure_kscratch(s, tc_gemv_partial_floats(w, m, s->sm_count, plan) * 4);
-                    if (rc) return rc;
-                    return launch_tc_gemv(w, plan, a, m, y, ly, (float*)s->kscratch, s->err_dev,
-                                          s->sm_count, s->stream, &s->launches, ysp);
+                    return gemv_call(s, w, a, m, y, ly, ysp);
                   };
                   // every rank takes the same path (the exchange that follows
                   // depends on it), also a rank that holds no columns
@@ -1766,6 +1810,118 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   return launch_simt_gemm(w, dA, M, false, yl, ldy, false, 1.0f, 1.0f, nullptr, 0,
                                           0, 0, s->stream, &s->launches);
                 });
+}
+
+}  // extern "C"
+
+namespace {
+
+int ensure_aux(ort_cuda_session* s, size_t bytes) {
+  if (bytes <= s->aux_bytes) return ORT_CUDA_OK;
+  ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+             "a buffer would grow while a CUDA graph is being captured; run every "
+             "operation of the graph once before capturing it");
+  const size_t want = bytes + bytes / 4 + (1 << 20);
+  if (s->aux) {
+    ORTC_CUDA(cudaStreamSynchronize(s->stream));
+    ORTC_CUDA(cudaFree(s->aux));
+    s->aux = nullptr;
+    s->aux_bytes = 0;
+  }
+  ORTC_CUDA(cudaMalloc(&s->aux, want));
+  s->aux_bytes = want;
+  return ORT_CUDA_OK;
+}
+
+constexpr int64_t kAmaxRows = 64;  // rows of the fused path's keys (8 GEMV passes of 8)
+
+// MatMulNBits then ArgMax/ArgMin over each row of Y, device pointers.
+int nbits_argmax_dev(ort_cuda_session* s, Weight& w, const char* name, const float* dA,
+                     int64_t M, int64_t* dI, float* dY, int flags) {
+  const int mode = mode_of(s, flags);
+  const int arg_flags = flags & (ORT_CUDA_ARG_MIN | ORT_CUDA_ARG_SELECT_LAST);
+  int cmax = 0;
+  for (int m = 8; m >= 1 && !cmax; m--)
+    if (tc_gemv_ok(w, m)) cmax = m;
+  const bool fused = s->world == 1 && mode != ORT_CUDA_MODE_STRICT && cmax > 0 &&
+                     M <= 8 * cmax && M <= kAmaxRows && w.N < (int64_t)UINT32_MAX;
+  if (!fused) {
+    // the same result from the two separate operations
+    const int mflags = flags & (ORT_CUDA_MODE_OVERRIDE | 0xF000);
+    int rc = ort_cuda_matmul_nbits(s, name, dA, M, dY, mflags);
+    if (rc) return rc;
+    return ort_cuda_argmax(s, dY, M, w.N, w.N, dI, arg_flags);
+  }
+  if (!s->amaxbuf) {
+    ORTC_CHECK(!s->capturing, ORT_CUDA_ERR_INVALID_ARG,
+               "the first fused MatMulNBits + ArgMax call of a session sets it up; make one "
+               "before capturing a CUDA graph");
+    const size_t bytes = (size_t)kAmaxRows * 12 + 256;
+    ORTC_CUDA(cudaMalloc(&s->amaxbuf, bytes));
+    ORTC_CUDA(cudaMemsetAsync(s->amaxbuf, 0, bytes, s->stream));
+  }
+  for (int64_t r = 0; r < M; r += cmax) {
+    const int64_t m = std::min<int64_t>(cmax, M - r);
+    YSel ys;
+    ys.amax = static_cast<unsigned long long*>(s->amaxbuf);
+    ys.amax_out = dI;
+    ys.amax_rows = (int)M;
+    ys.amax_min = (arg_flags & ORT_CUDA_ARG_MIN) ? 1 : 0;
+    ys.amax_last = (arg_flags & ORT_CUDA_ARG_SELECT_LAST) ? 1 : 0;
+    ys.row0 = (int)r;
+    int rc = gemv_call(s, w, dA + r * w.K, m, dY + r * w.N, w.N, &ys);
+    if (rc) return rc;
+  }
+  return ORT_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+ORT_CUDA_API int ort_cuda_matmul_nbits_argmax(ort_cuda_session* s, const char* name,
+                                              const float* A, int64_t M, int64_t* indices,
+                                              float* Y, int flags) {
+  ORTC_CHECK(s && name && A && indices, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 0, ORT_CUDA_ERR_INVALID_ARG, "M must be >= 0");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  Weight& w = it->second;
+  ORTC_CHECK(w.kind == W_NBITS, ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + name + "' is not a MatMulNBits weight");
+  if (M == 0) return ORT_CUDA_OK;
+  ORTC_CHECK(valid_mode(mode_of(s, flags)), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
+  DeviceGuard g(s->device);
+  OpTimer timer(s, "MatMulNBits+ArgMax");
+  // device views: A and the indices staged when host, Y in session scratch
+  // when the caller wants no logits (or has them on the host)
+  const size_t ab = (size_t)(M * w.K) * 4, yb = (size_t)(M * w.N) * 4, ib = (size_t)M * 8;
+  size_t off = 0;
+  const size_t a_off = off;
+  if (host) off += al256(ab);
+  const size_t y_off = off;
+  if (host || !Y) off += al256(yb);
+  const size_t i_off = off;
+  if (host) off += al256(ib);
+  int rc = off ? ensure_aux(s, off) : ORT_CUDA_OK;
+  if (rc) return rc;
+  char* aux = static_cast<char*>(s->aux);
+  const float* dA = A;
+  if (host) {
+    ORTC_CUDA(cudaMemcpyAsync(aux + a_off, A, ab, cudaMemcpyHostToDevice, s->stream));
+    dA = reinterpret_cast<const float*>(aux + a_off);
+  }
+  float* dY = (host || !Y) ? reinterpret_cast<float*>(aux + y_off) : Y;
+  int64_t* dI = host ? reinterpret_cast<int64_t*>(aux + i_off) : indices;
+  rc = nbits_argmax_dev(s, w, name, dA, M, dI, dY, flags & ~ORT_CUDA_HOST_IO);
+  if (rc || !host) return rc;
+  ORTC_CUDA(cudaMemcpyAsync(indices, dI, ib, cudaMemcpyDeviceToHost, s->stream));
+  if (Y) ORTC_CUDA(cudaMemcpyAsync(Y, dY, yb, cudaMemcpyDeviceToHost, s->stream));
+  return bounded_sync(s);
 }
 
 }  // extern "C"

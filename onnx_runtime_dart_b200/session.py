@@ -161,6 +161,10 @@ class CudaSession:
             self._set_stream_raw(cur)
             self._followed = cur
 
+    def set_peer_wait(self, ms: int) -> None:
+        """Bound of every wait for a peer GPU in the exchange of Y (ms)."""
+        check(_lib.load().ort_cuda_set_peer_wait(self.handle, int(ms)), "ort_cuda_set_peer_wait")
+
     def sync(self) -> None:
         check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")
 
@@ -660,6 +664,40 @@ class CudaSession:
             yp, layout | (_lib.ROTARY_INTERLEAVED if interleaved else 0) | hflag),
             "ort_cuda_rotary_embedding")
         return y
+
+    def matmul_nbits_argmax(self, name: str, a, *, is_min: bool = False,
+                            select_last: bool = False, logits: bool = False, flags: int = 0):
+        """MatMulNBits followed by ArgMax (ArgMin) over the last axis of its
+        output, fused on the device (ort_cuda_matmul_nbits_argmax): the
+        greedy selection after lm_head.  Returns the int64 indices of shape
+        a.shape[:-1] (and the logits when logits=True).  A torch CUDA tensor
+        stays on its device (stream-ordered); a numpy array runs through
+        host buffers, synchronously."""
+        kind, k, n = self.weights[name]
+        shape = tuple(a.shape)
+        if shape[-1] != k:
+            raise ValueError(f"MatMulNBits: A last dim {shape[-1]} != K {k}")
+        m = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        flags |= (_lib.ARG_MIN if is_min else 0) | (_lib.ARG_SELECT_LAST if select_last else 0)
+        L = _lib.load()
+        if hasattr(a, "data_ptr"):
+            import torch
+            self._follow_torch_stream()
+            a = a.contiguous()
+            idx = torch.empty(shape[:-1], dtype=torch.int64, device=a.device)
+            y = torch.empty(shape[:-1] + (n,), dtype=torch.float32, device=a.device) \
+                if logits else None
+            check(L.ort_cuda_matmul_nbits_argmax(self.handle, name.encode(), a.data_ptr(), m,
+                                                 idx.data_ptr(), _ptr(y), flags),
+                  "ort_cuda_matmul_nbits_argmax")
+            return (idx, y) if logits else idx
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        idx = np.empty(shape[:-1], np.int64)
+        y = np.empty(shape[:-1] + (n,), np.float32) if logits else None
+        check(L.ort_cuda_matmul_nbits_argmax(self.handle, name.encode(), a.ctypes.data, m,
+                                             idx.ctypes.data, _ptr(y), flags | _lib.HOST_IO),
+              "ort_cuda_matmul_nbits_argmax")
+        return (idx, y) if logits else idx
 
     def matmul_nbits(self, name: str, a: Tensorish, flags: int = 0, out=None):
         kind, k, n = self.weights[name]

@@ -160,3 +160,81 @@ def test_two_gpu_sharded_results():
                 assert val["bitwise_" + key], key
         assert val["pf"] <= 2e-3, (r, val["pf"])
         assert val["graph_same"], r
+
+
+def _timeout_entry(rank, port, q):
+    import sys
+    sys.path.insert(0, ROOT)
+    try:
+        q.put((rank, True, _timeout_main(rank, port)))
+    except Exception:
+        q.put((rank, False, traceback.format_exc()))
+
+
+def _timeout_main(rank, port):
+    """Rank 1 skips an operation: rank 0's wait for its columns runs out
+    after the session's (short) peer-wait bound, the kernel returns, the
+    next synchronising call reports ORT_CUDA_ERR_TIMEOUT, and both sessions
+    still close.  The failure is made on the host (a rank that does not
+    call); nothing faults or hangs on the GPU."""
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle as O
+    from onnx_runtime_dart_b200 import CudaSession, StateError, _lib
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=WORLD, timeout=datetime.timedelta(seconds=60))
+    try:
+        obj = [CudaSession.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        s = CudaSession(rank, rank=rank, world=WORLD, nccl_id=obj[0], timeout_ms=30000)
+        s.set_peer_wait(50)
+        rng = np.random.default_rng(3)
+        K, N = 1024, 4096
+        B, sc, z = O.make_nbits_weight(rng, K, N, 128, zero_points=True)
+        s.upload_nbits("w", B, sc, z, k=K, n=N, block_size=128)
+        a = torch.randn(1, K, device="cuda")
+        y = s.matmul_nbits("w", a)  # together: plans timed, exchange completes
+        s.sync()
+        out = {"first_ok": bool(torch.isfinite(y).all())}
+        dist.barrier()
+        if rank == 0:
+            s.matmul_nbits("w", a)  # rank 1 never takes part
+            try:
+                s.sync()
+                out["timeout"] = None
+            except StateError as e:
+                out["timeout"] = e.code if hasattr(e, "code") else str(e)
+                out["msg"] = str(e)
+        dist.barrier()
+        s.close()
+        out["closed"] = True
+        return out
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < WORLD, reason="needs two GPUs")
+def test_two_gpu_peer_wait_expires():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_timeout_entry, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            r, ok, val = q.get(timeout=300)
+            res[r] = (ok, val)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(WORLD):
+        ok, val = res[r]
+        assert ok, val
+        assert val["first_ok"] and val["closed"], (r, val)
+    from onnx_runtime_dart_b200 import _lib
+    assert res[0][1]["timeout"] == _lib.ERR_TIMEOUT, res[0][1]
