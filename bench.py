@@ -376,6 +376,54 @@ def leg_nbits(bench, tag, projs, weights, M, mode, bs, scale_bytes, zp, reps, fl
     return out
 
 
+def leg_cfg4_grouped(bench, c4, w4, M, reps, hbm):
+    """cfg4's decode step with each layer's sibling projections fused
+    (ort_cuda_fuse_nbits: q/k/v and gate/up) and run as one operation each
+    (ort_cuda_matmul_nbits_group): 4 operations per layer instead of 7, the
+    same weights, bytes and results."""
+    torch = bench.torch
+    from onnx_runtime_dart_b200.workloads import nbits_bytes
+    sess, dev = bench.sess, bench.dev
+    for p in c4:
+        B, s, z = w4[p.name]
+        sess.upload_nbits("g." + p.name, B, s, z, k=p.K, n=p.N, block_size=BS)
+    steps = []
+    for layer in range(16):
+        pre = f"g.l{layer}."
+        sess.fuse_nbits(pre + "qkv", [pre + "q", pre + "k", pre + "v"], drop_parts=True)
+        sess.fuse_nbits(pre + "gate_up", [pre + "gate", pre + "up"], drop_parts=True)
+        steps += [("group", pre + "qkv", 2048), ("one", pre + "o", 2048),
+                  ("group", pre + "gate_up", 2048), ("one", pre + "down", 8192)]
+    steps.append(("one", "g.lm_head", 2048))
+    gen = torch.Generator(device=dev).manual_seed(SEED + 40)
+    A = {K: torch.randn(M, K, device=dev, generator=gen) for K in (2048, 8192)}
+    outs = {}
+    for kind, nm, K in steps:
+        if kind == "group":
+            outs[nm] = sess.matmul_nbits_group(nm, A[K])
+        else:
+            outs[nm] = sess.matmul_nbits(nm, A[K])
+
+    def step():
+        for kind, nm, K in steps:
+            if kind == "group":
+                sess.matmul_nbits_group(nm, A[K], outs=outs[nm])
+            else:
+                sess.matmul_nbits(nm, A[K], out=outs[nm])
+
+    ms = bench.max_over_ranks([bench.time_fn(step, reps, False)])[0]
+    for kind, nm, K in steps:
+        sess.drop_weight(nm)
+    bytes_step = sum(nbits_bytes(p.K, p.N, BS, M, 2, False) for p in c4)
+    gbs = bytes_step / (ms * 1e-3) / 1e9
+    return {"workload": "cfg4 decode step at M=4 with sibling projections fused: per layer "
+                        "qkv (q,k,v) and gate_up (gate,up) as one operation each, o, down; "
+                        "plus lm_head (65 operations instead of 113; same weights and bytes)",
+            "M": M, "mode": "exact", "ms_per_step": ms, "value": gbs, "unit": "GB/s",
+            "bound": "hbm", "frac": gbs / hbm, "bytes_per_step": bytes_step,
+            "l2": "weights larger than L2"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -629,6 +677,8 @@ def main():
             "k/v 2048x512, o 2048x2048, gate/up 2048x8192, down 8192x2048) + lm_head "
             "2048x128256 at M=4; bits 4, block 128, fp16 scales, no zero points", hbm, tpk,
             cpu)
+        configs["cfg4_decode_m4_grouped"] = leg_cfg4_grouped(
+            bench, c4, w4, 4, max(1, min(args.steps, 20)), hbm)
         configs["cfg4_prefill_m2048"] = leg_nbits(
             bench, "c4p", c4, w4, PREFILL_M, "mma_f16", BS, 2, False, 3, False,
             "cfg4 prefill: the same 113 projections at M=2048 (4 x 512 tokens), fp16 "

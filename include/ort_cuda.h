@@ -56,9 +56,11 @@ extern "C" {
 #define ORT_CUDA_MODE_STRICT 1
 /* tcgen05 tensor-core MMA on 16-bit operands with fp32 accumulation in
  * TMEM.  F16 operands use per-row / per-column power-of-two range
- * normalisation and meet 2e-3 max-relative error with cosine >= 0.99999;
- * BF16 operands are offered for callers that accept bf16 rounding
- * (about 2.5e-3 max-relative on N(0,1) inputs). */
+ * normalisation; BF16 operands are split into two bf16 terms (hi and lo)
+ * and every product formed from three MMAs (A_hi.W_hi + A_lo.W_hi +
+ * A_hi.W_lo), keeping about 16 significant bits of each operand at three
+ * times the tensor work.  Both meet 2e-3 max-relative error with cosine
+ * >= 0.99999 (the bf16 mode stays near 1e-5). */
 #define ORT_CUDA_MODE_MMA_F16 2
 #define ORT_CUDA_MODE_MMA_BF16 3
 
@@ -429,6 +431,31 @@ ORT_CUDA_API int ort_cuda_topk(ort_cuda_session* s, const float* X, int64_t rows
 ORT_CUDA_API int ort_cuda_matmul_nbits_argmax(ort_cuda_session* s, const char* name,
                                               const float* A, int64_t M, int64_t* indices,
                                               float* Y, int flags);
+
+/* Sibling MatMulNBits nodes that read the same input (q, k, v of an
+ * attention block; gate and up of a SwiGLU MLP) are separate nodes in the
+ * reference's graph (opMatMulNBits per node, onnx_graph.dart:1584-1596).
+ * ort_cuda_fuse_nbits makes one weight `fused` whose output columns are
+ * the parts' columns side by side (2 .. 4 parts with the same K, block
+ * size, zero-point presence and scale type, already uploaded); with
+ * ORT_CUDA_FUSE_DROP_PARTS the parts are freed, else they stay usable
+ * alone (their memory is then held twice).  On an N-sharded session the
+ * group is only recorded (the parts stay, ORT_CUDA_FUSE_DROP_PARTS has no
+ * effect): the group call then runs the parts in turn.
+ * ort_cuda_matmul_nbits_group runs the whole group as one operation and
+ * writes part i's [M x N_i] output to Ys[i]: on one GPU at decode sizes one
+ * GEMV launch streams every part's weights, so the fixed cost of a launch
+ * (dependency release, activation build, first MMA, sums) is paid once for
+ * the group.  Each part's result is bit for bit the one
+ * ort_cuda_matmul_nbits gives for that part.  Ys[] holds DEVICE pointers,
+ * or host pointers with ORT_CUDA_HOST_IO (then A is a host pointer too);
+ * ort_cuda_matmul_nbits(s, fused, ...) gives the side-by-side [M x N]. */
+#define ORT_CUDA_FUSE_DROP_PARTS 0x1
+ORT_CUDA_API int ort_cuda_fuse_nbits(ort_cuda_session* s, const char* fused,
+                                     const char* const* names, int n, int flags);
+ORT_CUDA_API int ort_cuda_matmul_nbits_group(ort_cuda_session* s, const char* fused,
+                                             const float* A, int64_t M, float* const* Ys,
+                                             int flags);
 
 /* _SliceLastSeq (onnx_graph.dart:456-473, inserted before the vocab
  * projection by the lastTokenLogits rewrite, :398-451): Y[o][i] =

@@ -51,6 +51,7 @@ ROTARY = 0x80  # attention flags
 ROTARY_INTERLEAVED = 0x200
 ROTARY_BHSD = 0x400
 TOPK_SMALLEST = 0x800
+FUSE_DROP_PARTS = 0x1  # ort_cuda_fuse_nbits flags
 
 # Every symbol include/ort_cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -114,6 +115,8 @@ SIGNATURES = {
     "ort_cuda_probe_ffma": (_int, [_vp, ctypes.POINTER(ctypes.c_double)]),
     "ort_cuda_matmul_nbits_argmax": (_int, [_vp, _cp, _vp, _i64, _vp, _vp, _int]),
     "ort_cuda_set_peer_wait": (_int, [_vp, _int]),
+    "ort_cuda_fuse_nbits": (_int, [_vp, _cp, ctypes.POINTER(_cp), _int, _int]),
+    "ort_cuda_matmul_nbits_group": (_int, [_vp, _cp, _vp, _i64, ctypes.POINTER(_vp), _int]),
 }
 
 _lib = None

@@ -32,7 +32,8 @@ int cuda_fail(cudaError_t e, const char* what);
   } while (0)
 
 // ---- weights -------------------------------------------------------------
-enum WeightKind { W_NBITS = 1, W_DENSE = 2, W_INT8 = 3 };
+enum WeightKind { W_NBITS = 1, W_DENSE = 2, W_INT8 = 3, W_GROUP = 4 };
+constexpr int kMaxSegs = 4;  // weights in one fused group (ort_cuda_fuse_nbits)
 
 // One uploaded initializer, resident for the session.  For an N-sharded
 // session only this rank's columns [n0, n0 + nl) are stored.
@@ -75,6 +76,13 @@ struct Weight {
   CUtensorMap tmW8;
   // decode GEMV: the plan (candidate index) timing chose for each M in 1..8
   int8_t gemv_plan[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
+  // a fused group (ort_cuda_fuse_nbits): the parts' names and first columns
+  // (part_col[i] .. part_col[i + 1]); on an N-sharded session only the names
+  // are kept (no fused copy) and the group call runs the parts in turn
+  int nparts = 0;
+  std::string part_name[kMaxSegs];
+  int64_t part_col[kMaxSegs + 1] = {};
+  bool group_only = false;
 };
 
 // ---- device layout of a MatMulNBits weight ---------------------------------
@@ -249,6 +257,13 @@ struct YSel {
   unsigned long long* amax = nullptr;
   int64_t* amax_out = nullptr;
   int amax_rows = 0, amax_min = 0, amax_last = 0;
+  // segmented output (nseg > 0, a fused group of weights on one GPU):
+  // column n in [seg_start[j], seg_start[j + 1]) goes to
+  // seg_y[j][m * seg_ld[j] + n - seg_start[j]]
+  int nseg = 0;
+  int64_t seg_start[kMaxSegs + 1] = {};
+  float* seg_y[kMaxSegs] = {};
+  int64_t seg_ld[kMaxSegs] = {};
 };
 
 // ArgMax order of the reference's scan (opArgMinMax, onnx_ops.dart:2198-2237):
@@ -318,6 +333,19 @@ __device__ __forceinline__ float* ysel_base(float* Y, const YSel& s) {
 // dependency wait.
 __device__ __forceinline__ void ysel_store(float* Yb, int64_t ldy, const YSel& s,
                                            unsigned long long e, int m, int n, float v) {
+  if (s.nseg) {
+    float* y = s.seg_y[0];
+    int64_t ld = s.seg_ld[0], st = 0;
+#pragma unroll
+    for (int t = 1; t < kMaxSegs; t++)  // constant indices: no local copy
+      if (t < s.nseg && n >= s.seg_start[t]) {
+        y = s.seg_y[t];
+        ld = s.seg_ld[t];
+        st = s.seg_start[t];
+      }
+    y[m * ld + (n - st)] = v;
+    return;
+  }
   Yb[m * ldy + n] = v;
   if (s.push) {
     const unsigned long long word = (e << 32) | (unsigned long long)__float_as_uint(v);
@@ -506,9 +534,13 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
                        int64_t* launches);
 int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
-                          int* err, int sm_count, cudaStream_t st, int64_t* launches);
+                          int* err, int sm_count, cudaStream_t st, int64_t* launches,
+                          int reserve_sms = 0);
+// reserve_sms: SMs the fused fp16 GEMM leaves free for a kernel beside it
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
-                     int64_t ldy, int mode, cudaStream_t st);
+                     int64_t ldy, int mode, cudaStream_t st, int reserve_sms = 0);
+// SMs a chunk gather of the sharded prefill runs on, beside the GEMM
+constexpr int kGatherSms = 16;
 int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, bool transA,
                      float* Y, int64_t ldy, int mode, float alpha, float beta, const float* C,
                      int64_t c_rows, int64_t c_cols, int64_t c_col0, cudaStream_t st);

@@ -33,6 +33,8 @@
 
 #include <algorithm>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
@@ -338,7 +340,8 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
 
 int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
-                          int* err, int sm_count, cudaStream_t st, int64_t* launches) {
+                          int* err, int sm_count, cudaStream_t st, int64_t* launches,
+                          int reserve_sms) {
   if (M == 0 || w.nl == 0) return ORT_CUDA_OK;
   const int64_t K = w.K, nl = w.nl, col_bytes = (int64_t)w.nb * w.bs / 2;
   CUtensorMap tmA, tmQ, tmSZ;
@@ -368,15 +371,17 @@ int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_e
   p.bps = bps;
   p.bs_shift = bs_shift;
   p.stage_tx = kABytes + kQBytes + (uint32_t)bps * PBN * 4;
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
+  if (dev >= 64 || !(configured.load() >> dev & 1ull)) {
     ORTC_CUDA(cudaFuncSetAttribute(nbits_gemm_f16_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemP));
-    configured |= 1ull << (dev & 63);
+    if (dev < 64) configured.fetch_or(1ull << dev);
   }
-  const int grid = std::min(p.tiles, sm_count);
+  // persistent: one CTA per SM, leaving reserve_sms SMs to a kernel that
+  // runs beside it (this GEMM's shared memory leaves no room on its SMs)
+  const int grid = std::min(p.tiles, std::max(1, sm_count - reserve_sms));
   nbits_gemm_f16_kernel<<<grid, kThreadsP, kSmemP, st>>>(tmA, tmQ, tmSZ, p);
   ORTC_CUDA(cudaGetLastError());
   (*launches)++;

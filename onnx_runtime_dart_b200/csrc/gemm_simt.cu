@@ -250,6 +250,103 @@ __global__ void unshard_kernel(const float* __restrict__ g, float* __restrict__ 
   }
 }
 
+// Exact-mode dense GEMM (FFMA), row-major A with K % 4 == 0 and a weight
+// of row pitch ldw % 4 == 0, both 16-byte aligned: 64 x 64 tiles, 16-k
+// stages double-buffered through registers, one float4 of A and one of W
+// per thread and stage; A is stored transposed in shared memory so each
+// thread reads its 4 rows and 4 columns with one 16-byte load each per k.
+// Every output still accumulates with fma in ascending k from 0, as the
+// general kernel does (the exact mode's arithmetic), so the two kernels
+// give the same bits.
+constexpr int XBM = 64, XBN = 64, XBK = 16;
+
+__global__ void __launch_bounds__(256)
+    sgemm_exact_kernel(const float* __restrict__ A, int64_t M, int K, int N,
+                       const float* __restrict__ W, int64_t ldw, float* __restrict__ Y,
+                       int64_t ldy, Epi epi) {
+  __shared__ __align__(16) float As[2][XBK][XBM];
+  __shared__ __align__(16) float Bs[2][XBK][XBN];
+  const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * XBM;
+  const int n0 = blockIdx.x * XBN;
+  // loader coordinates: A row t / 4, k quad t % 4; W k row t / 16, n quad t % 16
+  const int ar = t >> 2, ak = (t & 3) * 4;
+  const int bk = t >> 4, bn = (t & 15) * 4;
+  const int64_t am = m0 + ar;
+  const int gn = n0 + bn;
+  auto load = [&](int k0, float4& va, float4& vb) {
+    va = make_float4(0.f, 0.f, 0.f, 0.f);
+    vb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (am < M && k0 + ak < K)  // K % 4 == 0: the quad is whole
+      va = __ldg(reinterpret_cast<const float4*>(A + am * K + k0 + ak));
+    const int k = k0 + bk;
+    if (k < K) {
+      const float* wr = W + (int64_t)k * ldw;
+      if (gn + 3 < N) {
+        vb = __ldg(reinterpret_cast<const float4*>(wr + gn));
+      } else {
+        if (gn < N) vb.x = __ldg(wr + gn);
+        if (gn + 1 < N) vb.y = __ldg(wr + gn + 1);
+        if (gn + 2 < N) vb.z = __ldg(wr + gn + 2);
+      }
+    }
+  };
+  auto store = [&](int buf, const float4& va, const float4& vb) {
+    As[buf][ak + 0][ar] = va.x;
+    As[buf][ak + 1][ar] = va.y;
+    As[buf][ak + 2][ar] = va.z;
+    As[buf][ak + 3][ar] = va.w;
+    *reinterpret_cast<float4*>(&Bs[buf][bk][bn]) = vb;
+  };
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+  float4 va, vb;
+  load(0, va, vb);
+  store(0, va, vb);
+  __syncthreads();
+  const int nst = (K + XBK - 1) / XBK;
+  for (int s = 0; s < nst; s++) {
+    const int buf = s & 1;
+    if (s + 1 < nst) load((s + 1) * XBK, va, vb);
+#pragma unroll
+    for (int kk = 0; kk < XBK; kk++) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+    }
+    if (s + 1 < nst) {
+      store(buf ^ 1, va, vb);
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (epi.alpha != 1.0f) v = __fmul_rn(v, epi.alpha);
+      if (epi.has_c) {
+        const int64_t cn = epi.c_col0 + n;
+        float c = epi.C[(epi.c_rows == 1 ? 0 : m) * epi.c_cols + (epi.c_cols == 1 ? 0 : cn)];
+        if (epi.beta != 1.0f) c = __fmul_rn(c, epi.beta);
+        v = __fadd_rn(v, c);
+      }
+      Y[m * ldy + n] = v;
+    }
+  }
+}
+
 template <bool STRICT, typename Src>
 int run_simt(const float* A, int64_t M, int K, int N, bool transA, const Src& src, float* Y,
              int64_t ldy, const Epi& epi, int64_t batch, int64_t batch_a, int64_t batch_y,
@@ -293,6 +390,17 @@ int launch_simt_gemm(const Weight& w, const float* A, int64_t M, bool transA, fl
     }
   } else {
     DenseSrc src{w.W, w.nl};
+    const bool fast = !strict && !transA && K % 4 == 0 && w.nl % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(w.W) & 15) == 0 &&
+                      (M + XBM - 1) / XBM <= 65535;
+    if (fast) {
+      dim3 grid((unsigned)((N + XBN - 1) / XBN), (unsigned)((M + XBM - 1) / XBM));
+      sgemm_exact_kernel<<<grid, 256, 0, st>>>(A, M, K, N, w.W, w.nl, Y, ldy, epi);
+      ORTC_CUDA(cudaGetLastError());
+      (*launches)++;
+      return ORT_CUDA_OK;
+    }
     rc = strict ? run_simt<true>(A, M, K, tail_lo, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches)
                 : run_simt<false>(A, M, K, N, transA, src, Y, ldy, epi, 1, 0, 0, 0, st, launches);
     if (rc == ORT_CUDA_OK && tail_lo < N) {

@@ -7,7 +7,13 @@
 // normalisation per A row (e_m) and per weight column (f_n) so that the
 // largest magnitude of a row/column lands in [2^14, 2^15) — the scaling is
 // exact in fp32 and keeps f16's 11-bit precision away from overflow and
-// subnormals — or bf16 without normalisation.  A is converted per call
+// subnormals — or, in the bf16 mode, a two-term bf16 split of each value
+// (hi = bf16(v), lo = bf16(v - hi): 16 significant bits together) stored
+// as two planes, hi then lo.  The bf16 product is formed from three MMAs,
+// A_hi.W_hi + A_lo.W_hi + A_hi.W_lo (the dropped A_lo.W_lo is below 2^-16
+// of the product), so its error is about 2^-16 relative per product
+// instead of bf16's 2^-9 — inside the mode's 2e-3 bar with a wide margin —
+// at three times the tensor-core work.  A is converted per call
 // (one warp per row); dense weights are converted once per session and kept;
 // int4 weights are dequantised per call, W = (q - zp) * scale, into a 16-bit
 // scratch operand.
@@ -25,6 +31,8 @@
 // error code, drains its copies and returns.
 #include <cuda_bf16.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
@@ -33,13 +41,17 @@ namespace ortc {
 namespace {
 
 constexpr int TBM = 128, TBN = 256, TBK = 64;
-constexpr int kStages = 4;
 constexpr uint32_t kABytes = TBM * TBK * 2;            // 16 KB
 constexpr uint32_t kBBytes = TBN * TBK * 2;            // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;    // 48 KB
 constexpr uint32_t kTmemCols = 256;
 constexpr int kThreads = 192;
-constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+// one plane: 4 stages of A + W (48 KB); split: 2 stages of A_hi, A_lo, W_hi, W_lo (96 KB)
+template <bool SPLIT>
+struct Ring {
+  static constexpr int kStages = SPLIT ? 2 : 4;
+  static constexpr uint32_t kStageBytes = (SPLIT ? 2 : 1) * (kABytes + kBBytes);
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
 
 struct Epilogue {
   float* Y;
@@ -64,9 +76,13 @@ __device__ __forceinline__ float scale_pow2(float v, int e) {
   return v * pow2f(e);
 }
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     mma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    int K, uint32_t idesc, Epilogue ep) {
+                    const __grid_constant__ CUtensorMap tmA2,
+                    const __grid_constant__ CUtensorMap tmB2, int K, uint32_t idesc, Epilogue ep) {
+  constexpr int kStages = Ring<SPLIT>::kStages;
+  constexpr uint32_t kStageBytes = Ring<SPLIT>::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -99,6 +115,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tensormap(&tmA);
       prefetch_tensormap(&tmB);
+      if (SPLIT) {
+        prefetch_tensormap(&tmA2);
+        prefetch_tensormap(&tmB2);
+      }
       bool ok = true;
       int issued = 0;
       for (int kb = 0; kb < nk; kb++) {
@@ -113,6 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[s], kStageBytes);
         tma_load_2d(st, &tmA, &full[s], kb * TBK, m0);
         tma_load_2d(st + kABytes, &tmB, &full[s], kb * TBK, n0);
+        if (SPLIT) {  // [A_hi][W_hi][A_lo][W_lo]
+          tma_load_2d(st + kABytes + kBBytes, &tmA2, &full[s], kb * TBK, m0);
+          tma_load_2d(st + 2 * kABytes + kBBytes, &tmB2, &full[s], kb * TBK, n0);
+        }
         issued = kb + 1;
       }
       if (!ok) {
@@ -137,9 +161,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sa = smem_u32(smem + s * kStageBytes);
         const uint32_t sb = sa + kABytes;
 #pragma unroll
-        for (int kk = 0; kk < TBK / 16; kk++)
+        for (int kk = 0; kk < TBK / 16; kk++) {
           mma_f16_ss(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), idesc,
                      (kb | kk) != 0);
+          if (SPLIT) {
+            const uint32_t sa2 = sb + kBBytes, sb2 = sa2 + kABytes;
+            mma_f16_ss(tmem, smem_desc_sw128(sa2 + kk * 32), smem_desc_sw128(sb + kk * 32),
+                       idesc, true);  // A_lo . W_hi
+            mma_f16_ss(tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb2 + kk * 32),
+                       idesc, true);  // A_hi . W_lo
+          }
+        }
         mma_commit(&empty[s]);
       }
       mma_commit(accum);  // arrives once all issued MMAs are complete
@@ -201,6 +233,11 @@ __device__ __forceinline__ uint16_t to16(float v) {
   if (BF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
   return __half_as_ushort(__float2half_rn(v));
 }
+// The low term of the bf16 split: bf16(v - float(bf16(v))).
+__device__ __forceinline__ uint16_t bf16_lo(float v, uint16_t hi) {
+  const float h = __uint_as_float((uint32_t)hi << 16);
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v - h));
+}
 
 // A [M, K] (or [K, M] with transA) fp32 -> 16-bit [M, K] (+ row exponent
 // for f16).  One warp per row.
@@ -220,7 +257,13 @@ __global__ void a16_kernel(const float* __restrict__ A, int M, int K, bool trans
     if (lane == 0) row_exp[m] = e;
   }
   uint16_t* o = out + (int64_t)m * K;
-  for (int k = lane; k < K; k += 32) o[k] = to16<BF16>(BF16 ? at(k) : scale_pow2(at(k), -e));
+  uint16_t* lo = out + (int64_t)M * K + (int64_t)m * K;  // bf16: the low plane
+  for (int k = lane; k < K; k += 32) {
+    const float v = at(k);
+    const uint16_t h = to16<BF16>(BF16 ? v : scale_pow2(v, -e));
+    o[k] = h;
+    if (BF16) lo[k] = bf16_lo(v, h);
+  }
 }
 
 // The same conversion for row-major A with K % 4 == 0 and a 16-byte
@@ -244,6 +287,7 @@ __global__ void a16_vec_kernel(const float* __restrict__ A, int M, int K,
     if (lane == 0) row_exp[warp] = e;
   }
   uint2* o = reinterpret_cast<uint2*>(out + (int64_t)warp * K);
+  uint2* lo = reinterpret_cast<uint2*>(out + (int64_t)M * K + (int64_t)warp * K);
   for (int i = lane; i < k4; i += 32) {
     const float4 v = __ldg(row + i);
     const uint32_t a = to16<BF16>(BF16 ? v.x : scale_pow2(v.x, -e));
@@ -251,6 +295,11 @@ __global__ void a16_vec_kernel(const float* __restrict__ A, int M, int K,
     const uint32_t c = to16<BF16>(BF16 ? v.z : scale_pow2(v.z, -e));
     const uint32_t d = to16<BF16>(BF16 ? v.w : scale_pow2(v.w, -e));
     o[i] = make_uint2(a | (b << 16), c | (d << 16));
+    if (BF16) {
+      const uint32_t la = bf16_lo(v.x, (uint16_t)a), lb = bf16_lo(v.y, (uint16_t)b);
+      const uint32_t lc = bf16_lo(v.z, (uint16_t)c), ld = bf16_lo(v.w, (uint16_t)d);
+      lo[i] = make_uint2(la | (lb << 16), lc | (ld << 16));
+    }
   }
 }
 
@@ -277,7 +326,9 @@ __global__ void w16_dense_kernel(const float* __restrict__ W, int K, int nl,
     const int n = n0 + i, k = k0 + threadIdx.x;
     if (n < nl && k < K) {
       const float v = t[threadIdx.x][i];
-      out[(int64_t)n * K + k] = to16<BF16>(BF16 ? v : scale_pow2(v, -col_exp[n]));
+      const uint16_t h = to16<BF16>(BF16 ? v : scale_pow2(v, -col_exp[n]));
+      out[(int64_t)n * K + k] = h;
+      if (BF16) out[(int64_t)nl * K + (int64_t)n * K + k] = bf16_lo(v, h);
     }
   }
 }
@@ -314,7 +365,9 @@ __global__ void w16_nbits_kernel(const uint8_t* __restrict__ B, const float* __r
       const int blk = k / bs;
       const float z = Z ? (float)nbits_zp(Z, z_pitch, n, blk) : 8.0f;
       const float w = __fmul_rn((float)nbits_q(word, j) - z, S[(int64_t)blk * s_pitch + n]);
-      out[n * K + k] = to16<BF16>(BF16 ? w : scale_pow2(w, -e));
+      const uint16_t h = to16<BF16>(BF16 ? w : scale_pow2(w, -e));
+      out[n * K + k] = h;
+      if (BF16) out[(int64_t)nl * K + n * K + k] = bf16_lo(w, h);
     }
   }
 }
@@ -325,26 +378,45 @@ int launch_gemm(ort_cuda_session* s, const uint16_t* A16, const int* row_exp, in
                 int64_t c_cols, int64_t c_col0, cudaStream_t st) {
   const CUtensorMapDataType dt =
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tmA, tmB;
+  // bf16: two planes each (hi at A16 / W16, lo one plane later)
+  CUtensorMap tmA, tmB, tmA2, tmB2;
   int rc = encode_tma_2d(&tmA, dt, A16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TBK, TBM,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_tma_2d(&tmB, dt, W16, (uint64_t)K, (uint64_t)nl, (uint64_t)K * 2, TBK, TBN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  tmA2 = tmA;
+  tmB2 = tmB;
+  if (bf16) {
+    rc = encode_tma_2d(&tmA2, dt, A16 + M * K, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, TBK,
+                       TBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_tma_2d(&tmB2, dt, W16 + nl * K, (uint64_t)K, (uint64_t)nl, (uint64_t)K * 2, TBK,
+                       TBN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
   Epilogue ep{Y, ldy, (int)M, (int)nl, bf16 ? nullptr : row_exp, bf16 ? nullptr : col_exp,
               alpha, beta, C, c_rows, c_cols, c_col0, C != nullptr, s->err_dev};
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};  // per device, both variants
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    ORTC_CUDA(cudaFuncSetAttribute(mma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kSmemBytes));
-    configured |= 1ull << (dev & 63);
+  if (dev >= 64 || !(configured.load() >> dev & 1ull)) {
+    ORTC_CUDA(cudaFuncSetAttribute(mma_gemm_kernel<false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)Ring<false>::kSmemBytes));
+    ORTC_CUDA(cudaFuncSetAttribute(mma_gemm_kernel<true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)Ring<true>::kSmemBytes));
+    if (dev < 64) configured.fetch_or(1ull << dev);
   }
   dim3 grid((unsigned)((nl + TBN - 1) / TBN), (unsigned)((M + TBM - 1) / TBM));
-  mma_gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(tmA, tmB, (int)K,
-                                                       idesc_f16(bf16 ? 1 : 0, TBM, TBN), ep);
+  if (bf16)
+    mma_gemm_kernel<true><<<grid, kThreads, Ring<true>::kSmemBytes, st>>>(
+        tmA, tmB, tmA2, tmB2, (int)K, idesc_f16(1, TBM, TBN), ep);
+  else
+    mma_gemm_kernel<false><<<grid, kThreads, Ring<false>::kSmemBytes, st>>>(
+        tmA, tmB, tmA2, tmB2, (int)K, idesc_f16(0, TBM, TBN), ep);
   ORTC_CUDA(cudaGetLastError());
   s->launches++;
   return ORT_CUDA_OK;
@@ -358,7 +430,7 @@ int convert_a(ort_cuda_session* s, const float* A, int64_t M, int64_t K, bool tr
               size_t off, uint16_t** A16, int** row_exp, cudaStream_t st) {
   char* base = (char*)s->kscratch + off;
   *A16 = (uint16_t*)base;
-  *row_exp = (int*)(base + al256((size_t)(M * K) * 2));
+  *row_exp = (int*)(base + al256((size_t)(M * K) * 2 * (bf16 ? 2 : 1)));
   const int64_t threads = M * 32;
   const unsigned blocks = (unsigned)((threads + 255) / 256);
   const bool vec = !transA && K % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
@@ -375,7 +447,9 @@ int convert_a(ort_cuda_session* s, const float* A, int64_t M, int64_t K, bool tr
   return ORT_CUDA_OK;
 }
 
-size_t a_scratch_bytes(int64_t M, int64_t K) { return al256((size_t)(M * K) * 2) + al256((size_t)M * 4); }
+size_t a_scratch_bytes(int64_t M, int64_t K, bool bf16 = false) {
+  return al256((size_t)(M * K) * 2 * (bf16 ? 2 : 1)) + al256((size_t)M * 4);
+}
 
 }  // namespace
 
@@ -400,7 +474,7 @@ int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
     if (w.col_exp) cudaFree(w.col_exp);
     w.W16 = nullptr;
     w.col_exp = nullptr;
-    ORTC_CUDA(cudaMalloc(&w.W16, (size_t)(nl * K) * 2));
+    ORTC_CUDA(cudaMalloc(&w.W16, (size_t)(nl * K) * 2 * (bf16 ? 2 : 1)));  // bf16: hi, lo
     ORTC_CUDA(cudaMalloc(&w.col_exp, (size_t)nl * 4));
     if (!bf16) {
       wcol_exp_kernel<<<(unsigned)((nl + 255) / 256), 256, 0, st>>>(w.W, (int)K, (int)nl, w.col_exp);
@@ -417,7 +491,7 @@ int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
     s->launches++;
     w.w16_mode = mode;
   }
-  int rc = ensure_kscratch(s, a_scratch_bytes(M, K));
+  int rc = ensure_kscratch(s, a_scratch_bytes(M, K, bf16));
   if (rc) return rc;
   uint16_t* A16;
   int* rexp;
@@ -428,7 +502,7 @@ int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
 }
 
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
-                     int64_t ldy, int mode, cudaStream_t st) {
+                     int64_t ldy, int mode, cudaStream_t st, int reserve_sms) {
   if (w.nl == 0 || M == 0) return ORT_CUDA_OK;
   const bool bf16 = mode == ORT_CUDA_MODE_MMA_BF16;
   const int64_t K = w.K, nl = w.nl;
@@ -456,10 +530,10 @@ int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
     rc = convert_a(s, A, M, K, false, false, 0, &A16, &rexp, st);
     if (rc) return rc;
     return launch_nbits_gemm_f16(w, A16, rexp, M, w.sz16, w.col_exp, Y, ldy, s->err_dev,
-                                 s->sm_count, st, &s->launches);
+                                 s->sm_count, st, &s->launches, reserve_sms);
   }
-  const size_t a_bytes = a_scratch_bytes(M, K);
-  const size_t w_bytes = al256((size_t)(nl * K) * 2);
+  const size_t a_bytes = a_scratch_bytes(M, K, bf16);
+  const size_t w_bytes = al256((size_t)(nl * K) * 2 * (bf16 ? 2 : 1));
   const size_t e_bytes = al256((size_t)nl * 4);
   int rc = ensure_kscratch(s, a_bytes + w_bytes + e_bytes);
   if (rc) return rc;

@@ -225,9 +225,10 @@ struct ChunkArgs {
   uint64_t wait_ns;
 };
 
-constexpr int kChunkV = 4;  // float4 per thread and round
+constexpr int kChunkV = 8;         // float4 per thread and round
+constexpr int kChunkThreads = 512;  // two CTAs per free SM
 
-__global__ void __launch_bounds__(256) p2p_chunk_gather_kernel(const ChunkArgs a) {
+__global__ void __launch_bounds__(kChunkThreads, 2) p2p_chunk_gather_kernel(const ChunkArgs a) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
@@ -254,52 +255,37 @@ __global__ void __launch_bounds__(256) p2p_chunk_gather_kernel(const ChunkArgs a
   }
   __syncthreads();
   if (!ok) return;
+  // One (row, rank) slice at a time per CTA: the slice's Ns values are
+  // contiguous in the source third and land at columns r * Ns .. of Y's row.
   const bool vec = (a.N % 4) == 0 && (a.Ns % 4) == 0 && (a.ldy % 4) == 0;
-  // work units: (row, rank, 4-column group) in row-major order of the
-  // rank's slice; slices of a row are contiguous in src
-  const int per_row4 = (a.Ns + 3) / 4;
-  const int64_t units = (int64_t)a.m * a.world * per_row4;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t u0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u0 < units;
-       u0 += stride * kChunkV) {
-    float4 v[kChunkV];
-    int64_t dst[kChunkV];
-    int cnt[kChunkV];
+  const int slices = a.m * a.world;
+  for (int sl = blockIdx.x; sl < slices; sl += gridDim.x) {
+    const int row = sl / a.world, r = sl - row * a.world;
+    const int c0 = r * a.Ns;
+    const int len = min(a.Ns, a.N - c0);  // the last rank's slice may be short
+    if (len <= 0) continue;
+    const float* src = a.src[r] + (int64_t)row * a.Ns;
+    float* dst = a.Y + (int64_t)row * a.ldy + c0;
+    if (vec) {
+      const int n4 = len / 4;
+      const float4* s4 = reinterpret_cast<const float4*>(src);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      for (int j0 = threadIdx.x; j0 < n4; j0 += blockDim.x * kChunkV) {
+        float4 v[kChunkV];
 #pragma unroll
-    for (int t = 0; t < kChunkV; t++) {
-      const int64_t u = u0 + t * stride;
-      cnt[t] = 0;
-      if (u >= units) continue;
-      const int j4 = (int)(u % per_row4);
-      const int64_t rr = u / per_row4;
-      const int r = (int)(rr % a.world), row = (int)(rr / a.world);
-      const int c0 = r * a.Ns + j4 * 4;
-      cnt[t] = max(0, min(4, a.N - c0));
-      cnt[t] = min(cnt[t], a.Ns - j4 * 4);
-      if (cnt[t] <= 0) continue;
-      const float* s = a.src[r] + (int64_t)row * a.Ns + j4 * 4;
-      dst[t] = (int64_t)row * a.ldy + c0;
-      if (vec && cnt[t] == 4) {
-        v[t] = __ldcv(reinterpret_cast<const float4*>(s));
-      } else {
-        v[t].x = __ldcv(s);
-        v[t].y = cnt[t] > 1 ? __ldcv(s + 1) : 0.f;
-        v[t].z = cnt[t] > 2 ? __ldcv(s + 2) : 0.f;
-        v[t].w = cnt[t] > 3 ? __ldcv(s + 3) : 0.f;
-      }
-    }
+        for (int t = 0; t < kChunkV; t++) {
+          const int j = j0 + t * blockDim.x;
+          if (j < n4) v[t] = __ldcg(s4 + j);
+        }
 #pragma unroll
-    for (int t = 0; t < kChunkV; t++) {
-      if (cnt[t] <= 0) continue;
-      float* d = a.Y + dst[t];
-      if (vec && cnt[t] == 4) {
-        *reinterpret_cast<float4*>(d) = v[t];
-      } else {
-        d[0] = v[t].x;
-        if (cnt[t] > 1) d[1] = v[t].y;
-        if (cnt[t] > 2) d[2] = v[t].z;
-        if (cnt[t] > 3) d[3] = v[t].w;
+        for (int t = 0; t < kChunkV; t++) {
+          const int j = j0 + t * blockDim.x;
+          if (j < n4) d4[j] = v[t];
+        }
       }
+      for (int j = n4 * 4 + threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(src + j);
+    } else {
+      for (int j = threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(src + j);
     }
   }
 }
@@ -484,10 +470,10 @@ int p2p_chunk_gather(ort_cuda_session* s, unsigned long long epoch, int64_t m, i
   a.world = s->world;
   a.err = s->err_dev;
   a.wait_ns = (uint64_t)s->peer_wait_ms * 1000000ull;
-  const int64_t units = m * s->world * ((Ns + 3) / 4);
-  const unsigned blocks = (unsigned)std::max<int64_t>(
-      1, std::min<int64_t>((units + 256 * kChunkV - 1) / (256 * kChunkV), s->sm_count * 2));
-  p2p_chunk_gather_kernel<<<blocks, 256, 0, st>>>(a);
+  // two CTAs on each SM the GEMM beside it leaves free
+  const unsigned blocks =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>(m * s->world, 2 * kGatherSms));
+  p2p_chunk_gather_kernel<<<blocks, kChunkThreads, 0, st>>>(a);
   ORTC_CUDA(cudaGetLastError());
   s->launches++;
   return ORT_CUDA_OK;

@@ -1540,7 +1540,13 @@ size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_t M,
                           float* yloc, float* gath, float* Y, int mode) {
   const int64_t N = w.N, ns = w.ns, G = s->world;
-  const int64_t mc = std::max<int64_t>(256, ((M + 7) / 8 + 127) / 128 * 128);
+  // Chunks of whole 128-row tile rows, each at least two waves of the GEMM's
+  // 128 x 256 tiles on this GPU (a chunk of fewer tiles leaves SMs idle and
+  // costs more than its overlap saves); at most 8 chunks.
+  const int64_t col_tiles = (ns + 255) / 256;
+  int64_t rows_for_waves = (2 * s->sm_count + col_tiles - 1) / col_tiles * 128;
+  int64_t mc = std::max<int64_t>(rows_for_waves, ((M + 7) / 8 + 127) / 128 * 128);
+  if (mc > M) mc = M;
   const int64_t nch = (M + mc - 1) / mc;
   ORTC_CHECK(nch <= 16, ORT_CUDA_ERR_INVALID_ARG, "too many prefill chunks");
   if (!s->comm_stream)
@@ -1566,7 +1572,10 @@ int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_
       const int64_t r0 = c * mc, m = std::min(mc, M - r0);
       const unsigned long long e = ++s->bepoch;
       if (e >= 3) ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->big_ev[(e - 2) % 3], 0));
-      int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, p2p_big_third(s, e), ns, mode, s->stream);
+      // the gather of the previous chunk runs beside this GEMM on the SMs
+      // it leaves free
+      int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, p2p_big_third(s, e), ns, mode, s->stream,
+                                nch > 1 ? kGatherSms : 0);
       if (rc) return rc;
       ORTC_CUDA(cudaEventRecord(s->chunk_ev[c], s->stream));
       ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[c], 0));
@@ -1800,7 +1809,7 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   if ((mode == ORT_CUDA_MODE_MMA_F16 || mode == ORT_CUDA_MODE_MMA_BF16) &&
                       mma_supported_shape(M, w.K)) {
                     // the same decision on every rank: it depends on shapes only
-                    if (s->chunk_gath && M >= 512 && !s->capturing && s->nccl) {
+                    if (s->chunk_gath && M >= 256 && !s->capturing && s->nccl) {
                       s->gathered = true;
                       return nbits_prefill_chunked(s, w, dA, M, yl, s->chunk_gath, s->chunk_y,
                                                    mode);
@@ -1925,6 +1934,199 @@ ORT_CUDA_API int ort_cuda_matmul_nbits_argmax(ort_cuda_session* s, const char* n
 }
 
 }  // extern "C"
+
+ORT_CUDA_API int ort_cuda_fuse_nbits(ort_cuda_session* s, const char* fused,
+                                     const char* const* names, int n, int flags) {
+  ORTC_CHECK(s && fused && names, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(n >= 2 && n <= kMaxSegs, ORT_CUDA_ERR_INVALID_ARG,
+             "a fused group holds 2 .. " + std::to_string(kMaxSegs) + " weights");
+  std::vector<Weight*> parts;
+  for (int i = 0; i < n; i++) {
+    ORTC_CHECK(names[i] && std::strcmp(names[i], fused) != 0, ORT_CUDA_ERR_INVALID_ARG,
+               "the fused name must differ from its parts");
+    auto it = s->weights.find(names[i]);
+    ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+               std::string("no weight named '") + names[i] + "'");
+    ORTC_CHECK(it->second.kind == W_NBITS && it->second.nparts == 0, ORT_CUDA_ERR_INVALID_ARG,
+               std::string("weight '") + names[i] + "' is not a plain MatMulNBits weight");
+    parts.push_back(&it->second);
+  }
+  const Weight& p0 = *parts[0];
+  for (Weight* p : parts)
+    ORTC_CHECK(p->K == p0.K && p->bs == p0.bs && p->has_zp == p0.has_zp &&
+                   (p->scales16 != nullptr) == (p0.scales16 != nullptr),
+               ORT_CUDA_ERR_INVALID_ARG,
+               "fused weights need the same K, block size, zero points and scale type");
+  DeviceGuard g(s->device);
+  Weight w;
+  w.kind = W_NBITS;
+  w.K = p0.K;
+  w.bs = p0.bs;
+  w.nb = p0.nb;
+  w.has_zp = p0.has_zp;
+  w.nparts = n;
+  int64_t N = 0;
+  for (int i = 0; i < n; i++) {
+    w.part_name[i] = names[i];
+    w.part_col[i] = N;
+    N += parts[i]->N;
+  }
+  w.part_col[n] = N;
+  w.N = N;
+  if (s->world > 1) {
+    // sharded: each part keeps its own shards and exchange; the group call
+    // runs them in turn
+    w.kind = W_GROUP;
+    w.group_only = true;
+    auto it = s->weights.find(fused);
+    if (it != s->weights.end()) {
+      free_weight(it->second);
+      s->weights.erase(it);
+    }
+    s->weights.emplace(fused, w);
+    return ORT_CUDA_OK;
+  }
+  w.n0 = 0;
+  w.nl = w.ns = N;
+  const int64_t col_bytes = (int64_t)w.nb * w.bs / 2, nb = w.nb, zrows = (nb + 1) / 2;
+  w.s_pitch = (N + 3) / 4 * 4;
+  auto cleanup = [&](int rc) {
+    free_weight(w);
+    return rc;
+  };
+  cudaError_t e = cudaMalloc(&w.B, (size_t)(N * col_bytes));
+  if (e == cudaSuccess) e = cudaMalloc(&w.scales, (size_t)(nb * w.s_pitch * 4));
+  if (e == cudaSuccess) e = cudaMemsetAsync(w.scales, 0, (size_t)(nb * w.s_pitch * 4), s->stream);
+  if (e == cudaSuccess && p0.scales16) {
+    w.s16_pitch = (N + 7) / 8 * 8;
+    e = cudaMalloc(&w.scales16, (size_t)(nb * w.s16_pitch * 2));
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(w.scales16, 0, (size_t)(nb * w.s16_pitch * 2), s->stream);
+  }
+  if (e == cudaSuccess && w.has_zp) {
+    w.z_pitch = (N + 15) / 16 * 16;
+    e = cudaMalloc(&w.zp, (size_t)(zrows * w.z_pitch));
+    if (e == cudaSuccess) e = cudaMemsetAsync(w.zp, 0, (size_t)(zrows * w.z_pitch), s->stream);
+  }
+  for (int i = 0; i < n && e == cudaSuccess; i++) {
+    const Weight& p = *parts[i];
+    const int64_t c0 = w.part_col[i];
+    e = cudaMemcpyAsync(w.B + c0 * col_bytes, p.B, (size_t)(p.nl * col_bytes),
+                        cudaMemcpyDeviceToDevice, s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(w.scales + c0, (size_t)(w.s_pitch * 4), p.scales,
+                            (size_t)(p.s_pitch * 4), (size_t)(p.nl * 4), (size_t)nb,
+                            cudaMemcpyDeviceToDevice, s->stream);
+    if (e == cudaSuccess && w.scales16)
+      e = cudaMemcpy2DAsync(w.scales16 + c0, (size_t)(w.s16_pitch * 2), p.scales16,
+                            (size_t)(p.s16_pitch * 2), (size_t)(p.nl * 2), (size_t)nb,
+                            cudaMemcpyDeviceToDevice, s->stream);
+    if (e == cudaSuccess && w.zp)
+      e = cudaMemcpy2DAsync(w.zp + c0, (size_t)w.z_pitch, p.zp, (size_t)p.z_pitch, (size_t)p.nl,
+                            (size_t)zrows, cudaMemcpyDeviceToDevice, s->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return cleanup(cuda_fail(e, "fuse MatMulNBits weights"));
+  int rc = prepare_nbits_tc(w);
+  if (rc) return cleanup(rc);
+  if (flags & ORT_CUDA_FUSE_DROP_PARTS)
+    for (int i = 0; i < n; i++) {
+      auto it = s->weights.find(names[i]);
+      free_weight(it->second);
+      s->weights.erase(it);
+    }
+  auto it = s->weights.find(fused);
+  if (it != s->weights.end()) {
+    free_weight(it->second);
+    s->weights.erase(it);
+  }
+  s->weights.emplace(fused, w);
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_matmul_nbits_group(ort_cuda_session* s, const char* fused,
+                                             const float* A, int64_t M, float* const* Ys,
+                                             int flags) {
+  ORTC_CHECK(s && fused && A && Ys, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  ORTC_CHECK(M >= 0, ORT_CUDA_ERR_INVALID_ARG, "M must be >= 0");
+  auto it = s->weights.find(fused);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + fused + "'");
+  Weight& w = it->second;
+  ORTC_CHECK(w.nparts >= 2, ORT_CUDA_ERR_INVALID_ARG,
+             std::string("weight '") + fused + "' is not a fused group");
+  for (int i = 0; i < w.nparts; i++)
+    ORTC_CHECK(Ys[i], ORT_CUDA_ERR_INVALID_ARG, "NULL output of part " + std::to_string(i));
+  if (M == 0) return ORT_CUDA_OK;
+  if (w.group_only) {  // N-sharded session: the parts in turn, each exchanged
+    for (int i = 0; i < w.nparts; i++) {
+      const int rc = ort_cuda_matmul_nbits(s, w.part_name[i].c_str(), A, M, Ys[i], flags);
+      if (rc) return rc;
+    }
+    return ORT_CUDA_OK;
+  }
+  const int mode = mode_of(s, flags);
+  ORTC_CHECK(valid_mode(mode), ORT_CUDA_ERR_INVALID_ARG, "unknown mode");
+  const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
+  ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
+             "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
+  DeviceGuard g(s->device);
+  OpTimer timer(s, "MatMulNBits");
+  int cmax = 0;
+  for (int m = 8; m >= 1 && !cmax; m--)
+    if (tc_gemv_ok(w, m)) cmax = m;
+  const bool gemv = mode != ORT_CUDA_MODE_STRICT && cmax > 0 && M <= 8 * cmax;
+  // device views: staged A / outputs for host buffers, one [M, N] scratch
+  // when the op runs whole and is split afterwards
+  const size_t ab = (size_t)(M * w.K) * 4, yb = (size_t)(M * w.N) * 4;
+  size_t off = 0;
+  const size_t a_off = off;
+  if (host) off += al256(ab);
+  const size_t y_off = off;
+  if (host || !gemv) off += al256(yb);
+  int rc = off ? ensure_aux(s, off) : ORT_CUDA_OK;
+  if (rc) return rc;
+  char* aux = static_cast<char*>(s->aux);
+  const float* dA = A;
+  if (host) {
+    ORTC_CUDA(cudaMemcpyAsync(aux + a_off, A, ab, cudaMemcpyHostToDevice, s->stream));
+    dA = reinterpret_cast<const float*>(aux + a_off);
+  }
+  float* scratch = reinterpret_cast<float*>(aux + y_off);
+  // part i of the output: in the caller's buffer, or (host) at column
+  // part_col[i] of rows of pitch N in scratch
+  auto part_y = [&](int i) -> float* { return host ? nullptr : Ys[i]; };
+  if (gemv) {
+    for (int64_t r = 0; r < M; r += cmax) {
+      const int64_t m = std::min<int64_t>(cmax, M - r);
+      YSel ys;
+      ys.nseg = w.nparts;
+      for (int i = 0; i < w.nparts; i++) {
+        const int64_t ni = w.part_col[i + 1] - w.part_col[i];
+        ys.seg_start[i] = w.part_col[i];
+        ys.seg_y[i] = host ? scratch + r * w.N + w.part_col[i] : part_y(i) + r * ni;
+        ys.seg_ld[i] = host ? w.N : ni;
+      }
+      ys.seg_start[w.nparts] = w.N;
+      rc = gemv_call(s, w, dA + r * w.K, m, scratch, w.N, &ys);
+      if (rc) return rc;
+    }
+  } else {
+    const int mflags = flags & (ORT_CUDA_MODE_OVERRIDE | 0xF000);
+    rc = ort_cuda_matmul_nbits(s, fused, dA, M, scratch, mflags);
+    if (rc) return rc;
+  }
+  if (!host && gemv) return ORT_CUDA_OK;
+  // split the [M, N] rows of scratch into the parts
+  for (int i = 0; i < w.nparts; i++) {
+    const int64_t ni = w.part_col[i + 1] - w.part_col[i];
+    ORTC_CUDA(cudaMemcpy2DAsync(Ys[i], (size_t)(ni * 4), scratch + w.part_col[i],
+                                (size_t)(w.N * 4), (size_t)(ni * 4), (size_t)M,
+                                host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice,
+                                s->stream));
+  }
+  return host ? bounded_sync(s) : ORT_CUDA_OK;
+}
 
 static int matmul_integer_op(ort_cuda_session* s, const char* name, const void* A, int64_t M,
                              int a_signed, const void* a_zp, int64_t a_zp_len, int32_t* Y,

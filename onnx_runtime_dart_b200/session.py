@@ -665,6 +665,53 @@ class CudaSession:
             "ort_cuda_rotary_embedding")
         return y
 
+    def fuse_nbits(self, fused: str, names: Sequence[str], drop_parts: bool = False) -> None:
+        """One weight `fused` whose columns are those of `names` side by
+        side (ort_cuda_fuse_nbits): sibling nodes that read the same input
+        (q/k/v, gate/up) then run as one operation (matmul_nbits_group)."""
+        parts = [self.weights[n] for n in names]
+        k = parts[0][1]
+        arr = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        check(_lib.load().ort_cuda_fuse_nbits(self.handle, fused.encode(), arr, len(names),
+                                              _lib.FUSE_DROP_PARTS if drop_parts else 0),
+              "ort_cuda_fuse_nbits")
+        widths = [p[2] for p in parts]
+        self.weights[fused] = ("nbits", k, sum(widths))
+        self._groups = getattr(self, "_groups", {})
+        self._groups[fused] = widths
+        if drop_parts and self.world == 1:  # a sharded session keeps the parts
+            for n in names:
+                self.weights.pop(n, None)
+
+    def matmul_nbits_group(self, fused: str, a, flags: int = 0, outs=None):
+        """Every part of a fused group on the same A (ort_cuda_matmul_nbits_group):
+        a list of outputs, part by part.  A torch CUDA tensor gives torch
+        tensors (stream-ordered); a numpy array runs through host buffers."""
+        kind, k, _ = self.weights[fused]
+        widths = self._groups[fused]
+        shape = tuple(a.shape)
+        if shape[-1] != k:
+            raise ValueError(f"MatMulNBits: A last dim {shape[-1]} != K {k}")
+        m = int(np.prod(shape[:-1], dtype=np.int64)) if len(shape) > 1 else 1
+        L = _lib.load()
+        if hasattr(a, "data_ptr"):
+            import torch
+            self._follow_torch_stream()
+            a = a.contiguous()
+            if outs is None:
+                outs = [torch.empty(shape[:-1] + (w,), dtype=torch.float32, device=a.device)
+                        for w in widths]
+            ptrs = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+            check(L.ort_cuda_matmul_nbits_group(self.handle, fused.encode(), a.data_ptr(), m,
+                                                ptrs, flags), "ort_cuda_matmul_nbits_group")
+            return outs
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        outs = [np.empty(shape[:-1] + (w,), np.float32) for w in widths]
+        ptrs = (ctypes.c_void_p * len(outs))(*[o.ctypes.data for o in outs])
+        check(L.ort_cuda_matmul_nbits_group(self.handle, fused.encode(), a.ctypes.data, m, ptrs,
+                                            flags | _lib.HOST_IO), "ort_cuda_matmul_nbits_group")
+        return outs
+
     def matmul_nbits_argmax(self, name: str, a, *, is_min: bool = False,
                             select_last: bool = False, logits: bool = False, flags: int = 0):
         """MatMulNBits followed by ArgMax (ArgMin) over the last axis of its

@@ -1,8 +1,11 @@
 """tcgen05 MMA modes against the oracle (prefill-sized M).
 
-Bars: MMA_F16 max|dY|/max|Y_ref| <= 2e-3 and cosine >= 0.99999 (the
-stated bf16-MMA tolerance, met with f16 operands).  MMA_BF16 (literal bf16
-operands) is held to the error bf16 rounding produces: 5e-3 / 0.99999.
+Bars: max|dY|/max|Y_ref| <= 2e-3 and cosine >= 0.99999 for both tensor-core
+modes (the stated bf16-MMA tolerance).  MMA_F16 meets it with range-
+normalised f16 operands; MMA_BF16 with bf16 operands split into hi and lo
+terms (three MMAs per product), which stays far inside the bar (its
+measured error is also checked against a tighter 1e-4 in
+test_bf16_split_precision).
 """
 import numpy as np
 import pytest
@@ -13,7 +16,7 @@ from tests.conftest import cosine, max_rel
 pytestmark = pytest.mark.gpu
 
 F16_TOL, F16_COS = 2e-3, 0.99999
-BF16_TOL, BF16_COS = 5e-3, 0.99999
+BF16_TOL, BF16_COS = 2e-3, 0.99999
 
 
 @pytest.fixture(scope="module")
@@ -137,3 +140,33 @@ def test_nbits_prefill_full_size_vs_torch(sess):
     ref = (torch.from_numpy(A).to(dev).double() @ W.T).cpu().numpy()
     sess.drop_weight("big")
     _check(ref, y, "mma_f16")
+
+
+@pytest.mark.parametrize("K,N,bs", [(4096, 6144, 128), (14336, 4096, 128), (1024, 3072, 32)])
+def test_bf16_split_precision(sess, K, N, bs):
+    """The bf16 mode at the benchmark's projection shapes (M=256): inside
+    2e-3 / 0.99999, and in fact near fp32 (<= 1e-4): the hi/lo split keeps
+    16 significant bits of each operand."""
+    rng = np.random.default_rng(K + N)
+    B, s, z = O.make_nbits_weight(rng, K, N, bs, zero_points=True, scale_dtype=np.float16)
+    A = rng.standard_normal((256, K)).astype(np.float32)
+    sess.upload_nbits("bs", B, s, z, k=K, n=N, block_size=bs)
+    y = sess.matmul_nbits("bs", A, flags=_flags("mma_bf16"))
+    ref = O.matmul_nbits(A, B, s.astype(np.float32), z, K, N, 4, bs, threads=8)
+    _check(ref, y, "mma_bf16")
+    assert max_rel(ref, y) <= 1e-4, max_rel(ref, y)
+    sess.drop_weight("bs")
+
+
+def test_bf16_wide_dynamic_range_rows(sess):
+    """bf16 keeps fp32's exponent range: rows scaled by 2^+-60 stay accurate."""
+    rng = np.random.default_rng(24)
+    A = rng.standard_normal((128, 256)).astype(np.float32)
+    A[0] *= 2.0 ** 60
+    A[1] *= 2.0 ** -60
+    W = rng.standard_normal((256, 64)).astype(np.float32)
+    sess.upload_dense("dr2", W)
+    y = sess.matmul("dr2", A, flags=_flags("mma_bf16"))
+    ref = O.matmul_kernel(A, W)
+    for r in (0, 1, 2):
+        assert max_rel(ref[r], y[r]) <= BF16_TOL
