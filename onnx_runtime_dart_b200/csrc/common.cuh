@@ -172,15 +172,14 @@ struct ort_cuda_session {
   size_t aux_bytes = 0;
   void* amaxbuf = nullptr;
   cudaEvent_t chunk_ev[17] = {};       // chunk c computed; [16]: exchange done
-  // big exchange buffer for prefill-sized outputs (csrc/p2p.cu): flags then
-  // three thirds of bcap floats; bpeer[r] is rank r's, mapped here; chunk
-  // epochs are counted on the host (bepoch, the same on every rank) and
-  // big_ev[e % 3] marks this rank's gather of epoch e done
+  // big exchange buffer for prefill-sized outputs (csrc/p2p.cu): a flag
+  // header then two halves of bcap floats, each [source rank][M][Ns];
+  // bpeer[r] is rank r's, mapped here; epochs are counted on the host
+  // (bepoch, the same on every rank)
   void* bbuf = nullptr;
   void* bpeer[8] = {};
   size_t bcap = 0;
   unsigned long long bepoch = 0;
-  cudaEvent_t big_ev[3] = {};
   // bound of every wait for a peer GPU's flag or data (ms)
   int peer_wait_ms = 1000;
   // CUDA graphs captured from the session stream (ort_cuda_graph_*)
@@ -364,6 +363,7 @@ int check_kernel_error(ort_cuda_session* s);
 // Waits for the session stream; with a communicator, bounded by the
 // session timeout (the communicator is aborted on expiry).
 int bounded_sync(ort_cuda_session* s);
+struct PrefillPush;  // push mode of the sharded prefill GEMM (defined below)
 // Peer-memory all-gather of Y for N-sharded sessions (p2p.cu).
 int p2p_setup(ort_cuda_session* s);
 void p2p_teardown(ort_cuda_session* s);
@@ -377,15 +377,22 @@ YSel p2p_ysel_push(ort_cuda_session* s, int64_t n0, int64_t N, int row0);
 // words of this epoch and copies them into Y [M, N] (row pitch N); this
 // rank's columns [n0, n0 + nl) are already there.  Advances the epoch.
 int p2p_land(ort_cuda_session* s, int64_t M, int64_t N, int64_t n0, int64_t nl, float* Y);
-// Big exchange buffer of three thirds of at least third_floats floats on
+// Big exchange buffer of two halves of at least half_floats floats on
 // every rank (a collective: every rank calls it with the same size); *ok
 // false when a peer could not be mapped (every rank then sees false).
-int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok);
-float* p2p_big_third(ort_cuda_session* s, unsigned long long epoch);
-// Gathers chunk `epoch` ([m, Ns] per rank, in each rank's third epoch % 3)
-// into Y rows (pitch N) on stream st.
-int p2p_chunk_gather(ort_cuda_session* s, unsigned long long epoch, int64_t m, int64_t Ns,
-                     int64_t N, float* Y, cudaStream_t st);
+int p2p_big_ensure(ort_cuda_session* s, size_t half_floats, bool* ok);
+// Push-mode prefill (see PrefillPush): before the GEMM, waits (bounded)
+// until every peer has consumed epoch - 2 from the half this epoch reuses;
+// after it, lands the peers' blocks of `epoch` into Y [M, N] and tells
+// each peer that its block was consumed.  The big buffer holds two halves
+// of at least M * N floats.
+int p2p_push_prepare(ort_cuda_session* s, unsigned long long epoch, int64_t M, int64_t ns,
+                     PrefillPush* push);
+int p2p_push_land(ort_cuda_session* s, unsigned long long epoch, int64_t M, int64_t ns,
+                  int64_t N, float* Y);
+// A rank without columns posts its empty block of the epoch ready.
+int p2p_push_post(ort_cuda_session* s, const PrefillPush& push);
+
 // `local` null: the producer already wrote the slice with p2p_ysel().
 int p2p_gather(ort_cuda_session* s, const float* local, int64_t M, int64_t Ns, int64_t N,
                float* Y);
@@ -530,17 +537,32 @@ int launch_unshard(const float* g, float* Y, int64_t world, int64_t M, int64_t N
 int mma_supported_shape(int64_t M, int64_t K);
 // Fused int4 prefill GEMM (fp16 MMA mode), csrc/gemm_nbits_tc.cu.
 bool nbits_gemm_f16_ok(const Weight& w);
+// nbits_gemm_f16_ok without the rank's own column count (the same on every rank)
+bool nbits_gemm_f16_layout_ok(const Weight& w);
 int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaStream_t st,
                        int64_t* launches);
 int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
-                          int reserve_sms = 0);
+                          int reserve_sms = 0, const PrefillPush* push = nullptr);
+// N-sharded prefill, push mode of the fused fp16 GEMM: besides its own
+// columns in Y, every output row slice [row][0, nl) is stored into each
+// peer's landing area land[r] (this rank's block of it, [M][Ns] floats);
+// when every CTA has finished (each storing thread fences at system scope),
+// the last CTA posts `epoch` into flag[r] of every peer.
+struct PrefillPush {
+  float* land[8] = {};
+  unsigned long long* flag[8] = {};
+  unsigned* ticket = nullptr;  // this rank's CTA ticket, zero between calls
+  unsigned long long epoch = 0;
+  int64_t ns = 0;
+  int rank = 0, world = 0;
+};
 // reserve_sms: SMs the fused fp16 GEMM leaves free for a kernel beside it
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
-                     int64_t ldy, int mode, cudaStream_t st, int reserve_sms = 0);
-// SMs a chunk gather of the sharded prefill runs on, beside the GEMM
-constexpr int kGatherSms = 16;
+                     int64_t ldy, int mode, cudaStream_t st, int reserve_sms = 0,
+                     const PrefillPush* push = nullptr);
+
 int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, bool transA,
                      float* Y, int64_t ldy, int mode, float alpha, float beta, const float* C,
                      int64_t c_rows, int64_t c_cols, int64_t c_col0, cudaStream_t st);

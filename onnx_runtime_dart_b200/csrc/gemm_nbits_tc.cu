@@ -67,6 +67,7 @@ struct PParams {
   int bps;       // quantisation blocks per 64-k stage (>= 1)
   int bs_shift;  // log2(block size)
   uint32_t stage_tx;
+  PrefillPush push;  // world == 0: no peers
 };
 
 __device__ __forceinline__ float pow2f(int e) {
@@ -285,8 +286,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         for (int j = 0; j < 32; j++) {
           const int e = __shfl_sync(0xffffffffu, my_e, j);
           const int row = rbase + j;
-          if (row < p.M && n < p.N)
-            p.Y[(int64_t)row * p.ldy + n] = scale_pow2(buf[j * 33 + lane], e + f);
+          if (row < p.M && n < p.N) {
+            const float v = scale_pow2(buf[j * 33 + lane], e + f);
+            p.Y[(int64_t)row * p.ldy + n] = v;
+            // push mode: the same value into every peer's landing block
+#pragma unroll
+            for (int r = 0; r < 8; r++)
+              if (r < p.push.world && r != p.push.rank)
+                p.push.land[r][(int64_t)row * p.push.ns + n] = v;
+          }
         }
         __syncwarp();
       }
@@ -295,11 +303,26 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (lane == 0) mbar_arrive(&tm_empty[d]);
     }
   }
+  // push mode: this thread's stores to the peers are visible system-wide
+  // before the CTA counts itself done; the last CTA posts the epoch
+  if (p.push.world > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  if (p.push.world > 0 && threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(p.push.ticket, 1u) == gridDim.x - 1) {
+      *p.push.ticket = 0u;
+      __threadfence_system();
+      for (int r = 0; r < p.push.world; r++)
+        if (r != p.push.rank)
+          asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.push.flag[r]),
+                       "l"(p.push.epoch)
+                       : "memory");
+    }
   }
 }
 
@@ -322,10 +345,12 @@ __global__ void nbits_sz16_kernel(const float* __restrict__ S, int64_t s_pitch,
 
 }  // namespace
 
-bool nbits_gemm_f16_ok(const Weight& w) {
+bool nbits_gemm_f16_layout_ok(const Weight& w) {
   const int64_t col_bytes = (int64_t)w.nb * w.bs / 2;
-  return w.nl > 0 && col_bytes % 16 == 0 && w.bs >= 16 && (w.bs & (w.bs - 1)) == 0;
+  return col_bytes % 16 == 0 && w.bs >= 16 && (w.bs & (w.bs - 1)) == 0;
 }
+
+bool nbits_gemm_f16_ok(const Weight& w) { return w.nl > 0 && nbits_gemm_f16_layout_ok(w); }
 
 int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaStream_t st,
                        int64_t* launches) {
@@ -341,7 +366,7 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
 int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
-                          int reserve_sms) {
+                          int reserve_sms, const PrefillPush* push) {
   if (M == 0 || w.nl == 0) return ORT_CUDA_OK;
   const int64_t K = w.K, nl = w.nl, col_bytes = (int64_t)w.nb * w.bs / 2;
   CUtensorMap tmA, tmQ, tmSZ;
@@ -371,6 +396,7 @@ int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_e
   p.bps = bps;
   p.bs_shift = bs_shift;
   p.stage_tx = kABytes + kQBytes + (uint32_t)bps * PBN * 4;
+  if (push) p.push = *push;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);

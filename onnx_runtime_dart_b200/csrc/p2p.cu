@@ -205,87 +205,123 @@ __global__ void __launch_bounds__(256) p2p_land_kernel(const unsigned long long*
   }
 }
 
-// Prefill-sized outputs, one row chunk at a time (p2p_chunk_gather): every
-// rank's GEMM wrote its [m, Ns] chunk into one of the three thirds of its
-// big exchange buffer; this kernel posts the chunk's epoch (a host counter,
-// the same on every rank) into each peer's flag slot for this rank, waits
-// (bounded) for every peer's post of that epoch, and copies all ranks'
-// slices into Y's rows with 16-byte loads and stores.  It runs on the
-// exchange stream beside the next chunk's GEMM: it uses no dynamic shared
-// memory and few registers, so its CTAs fit on the SMs next to the GEMM's.
-struct ChunkArgs {
-  const float* src[8];           // rank r's third holding this chunk, [m][Ns]
-  unsigned long long* flag[8];   // rank r's flag slot for this rank
-  const unsigned long long* mine;  // this rank's flags (slot r posted by rank r)
+// Prefill-sized outputs (push mode, see PrefillPush): the fused GEMM of
+// every rank stores its [M, Ns] block straight into each peer's big
+// exchange buffer (half epoch & 1, block [source rank]) from its epilogue
+// and its last CTA posts the epoch into the peer's ready slot for it.  The
+// header of a rank's big buffer holds 64-bit slots: [0, 8) ready epoch
+// posted by source r; [8, 16) consumed epoch posted by reader r (the
+// reader finished copying this rank's block); 16: the GEMM's CTA ticket;
+// 17: the landing kernel's CTA ticket.
+constexpr int kReadySlot = 0, kConsumedSlot = 8, kGemmTicketSlot = 16, kLandTicketSlot = 17;
+constexpr int kLandV = 8;          // float4 per thread and round
+constexpr int kLandThreads = 512;
+
+// Copies rank r's [m, Ns] block (src[r], row pitch Ns) into columns
+// r * Ns .. of Y (row pitch ldy, N columns) for every rank but `skip`,
+// one (row, rank) slice at a time per CTA.
+__device__ void copy_slices(const float* const* src, float* Y, int64_t ldy, int m, int Ns, int N,
+                            int world, int skip) {
+  const bool vec = (N % 4) == 0 && (Ns % 4) == 0 && (ldy % 4) == 0;
+  const int slices = m * world;
+  for (int sl = blockIdx.x; sl < slices; sl += gridDim.x) {
+    const int row = sl / world, r = sl - row * world;
+    if (r == skip) continue;
+    const int c0 = r * Ns;
+    const int len = min(Ns, N - c0);  // the last rank's slice may be short
+    if (len <= 0) continue;
+    const float* sp = src[r] + (int64_t)row * Ns;
+    float* dst = Y + (int64_t)row * ldy + c0;
+    if (vec) {
+      const int n4 = len / 4;
+      const float4* s4 = reinterpret_cast<const float4*>(sp);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      for (int j0 = threadIdx.x; j0 < n4; j0 += blockDim.x * kLandV) {
+        float4 v[kLandV];
+#pragma unroll
+        for (int t = 0; t < kLandV; t++) {
+          const int j = j0 + t * blockDim.x;
+          if (j < n4) v[t] = __ldcg(s4 + j);
+        }
+#pragma unroll
+        for (int t = 0; t < kLandV; t++) {
+          const int j = j0 + t * blockDim.x;
+          if (j < n4) d4[j] = v[t];
+        }
+      }
+      for (int j = n4 * 4 + threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(sp + j);
+    } else {
+      for (int j = threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(sp + j);
+    }
+  }
+}
+
+// Waits (bounded) until every peer has posted at least `need` in the slots
+// [base, base + world) of this rank's header (not its own).
+__device__ bool wait_slots(const unsigned long long* slots, int world, int rank,
+                           unsigned long long need, int* err, uint64_t wait_ns) {
+  const uint64_t t0 = globaltimer();
+  for (int r = 0; r < world; r++) {
+    if (r == rank) continue;
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(slots + r) : "memory");
+      if (v >= need) break;
+      if (globaltimer() - t0 > wait_ns) {
+        record_error(err, KERR_WAIT_PEER);
+        return false;
+      }
+      __nanosleep(128);
+    }
+  }
+  return true;
+}
+
+// Before a push-mode GEMM: every peer has consumed epoch need from the half
+// this epoch overwrites.
+__global__ void p2p_push_wait_kernel(const unsigned long long* header, int world, int rank,
+                                     unsigned long long need, int* err, uint64_t wait_ns) {
+  if (threadIdx.x == 0) wait_slots(header + kConsumedSlot, world, rank, need, err, wait_ns);
+}
+
+// A rank holding no columns runs no GEMM: it posts its (empty) block ready.
+__global__ void p2p_push_post_kernel(PrefillPush p) {
+  if (threadIdx.x == 0)
+    for (int r = 0; r < p.world; r++)
+      if (r != p.rank)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.flag[r]), "l"(p.epoch)
+                     : "memory");
+}
+
+struct LandArgs {
+  const float* src[8];             // this rank's half: the block of source r
+  unsigned long long* consumed[8];  // source r's consumed slot for this rank
+  unsigned long long* header;      // this rank's header
   unsigned long long epoch;
-  float* Y;                      // the chunk's first row of Y
-  int64_t ldy;
+  float* Y;
   int m, Ns, N, rank, world;
   int* err;
   uint64_t wait_ns;
 };
 
-constexpr int kChunkV = 8;         // float4 per thread and round
-constexpr int kChunkThreads = 512;  // two CTAs per free SM
-
-__global__ void __launch_bounds__(kChunkThreads, 2) p2p_chunk_gather_kernel(const ChunkArgs a) {
+__global__ void __launch_bounds__(kLandThreads, 2) p2p_push_land_kernel(const LandArgs a) {
   __shared__ int ok;
-  if (threadIdx.x == 0) {
-    ok = 1;
-    // every CTA posts (the same value): whichever is resident first does
-    for (int r = 0; r < a.world; r++)
-      if (r != a.rank)
-        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.flag[r]), "l"(a.epoch)
-                     : "memory");
-    const uint64_t t0 = globaltimer();
-    for (int r = 0; r < a.world && ok; r++) {
-      if (r == a.rank) continue;
-      for (;;) {
-        unsigned long long v;
-        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a.mine + r) : "memory");
-        if (v >= a.epoch) break;
-        if (globaltimer() - t0 > a.wait_ns) {
-          record_error(a.err, KERR_WAIT_PEER);
-          ok = 0;
-          break;
-        }
-        __nanosleep(128);
-      }
-    }
-  }
+  if (threadIdx.x == 0)
+    ok = wait_slots(a.header + kReadySlot, a.world, a.rank, a.epoch, a.err, a.wait_ns) ? 1 : 0;
   __syncthreads();
-  if (!ok) return;
-  // One (row, rank) slice at a time per CTA: the slice's Ns values are
-  // contiguous in the source third and land at columns r * Ns .. of Y's row.
-  const bool vec = (a.N % 4) == 0 && (a.Ns % 4) == 0 && (a.ldy % 4) == 0;
-  const int slices = a.m * a.world;
-  for (int sl = blockIdx.x; sl < slices; sl += gridDim.x) {
-    const int row = sl / a.world, r = sl - row * a.world;
-    const int c0 = r * a.Ns;
-    const int len = min(a.Ns, a.N - c0);  // the last rank's slice may be short
-    if (len <= 0) continue;
-    const float* src = a.src[r] + (int64_t)row * a.Ns;
-    float* dst = a.Y + (int64_t)row * a.ldy + c0;
-    if (vec) {
-      const int n4 = len / 4;
-      const float4* s4 = reinterpret_cast<const float4*>(src);
-      float4* d4 = reinterpret_cast<float4*>(dst);
-      for (int j0 = threadIdx.x; j0 < n4; j0 += blockDim.x * kChunkV) {
-        float4 v[kChunkV];
-#pragma unroll
-        for (int t = 0; t < kChunkV; t++) {
-          const int j = j0 + t * blockDim.x;
-          if (j < n4) v[t] = __ldcg(s4 + j);
-        }
-#pragma unroll
-        for (int t = 0; t < kChunkV; t++) {
-          const int j = j0 + t * blockDim.x;
-          if (j < n4) d4[j] = v[t];
-        }
-      }
-      for (int j = n4 * 4 + threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(src + j);
-    } else {
-      for (int j = threadIdx.x; j < len; j += blockDim.x) dst[j] = __ldcg(src + j);
+  if (ok) copy_slices(a.src, a.Y, a.N, a.m, a.Ns, a.N, a.world, a.rank);
+  // the last CTA tells every source that its block of this epoch is consumed
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned* ticket = reinterpret_cast<unsigned*>(a.header + kLandTicketSlot);
+    if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
+      *ticket = 0u;
+      __threadfence_system();
+      for (int r = 0; r < a.world; r++)
+        if (r != a.rank)
+          asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.consumed[r]), "l"(a.epoch)
+                       : "memory");
     }
   }
 }
@@ -382,10 +418,10 @@ void big_unmap(ort_cuda_session* s) {
 }
 }  // namespace
 
-int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok) {
+int p2p_big_ensure(ort_cuda_session* s, size_t half_floats, bool* ok) {
   *ok = false;
   if (!s->p2p_ok || !s->nccl) return ORT_CUDA_OK;
-  if (s->bbuf && s->bcap >= third_floats) {
+  if (s->bbuf && s->bcap >= half_floats) {
     *ok = true;
     return ORT_CUDA_OK;
   }
@@ -398,8 +434,8 @@ int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok) {
   int rc = host_allgather(s, &one, 1, &sync);
   if (rc) return rc;
   big_unmap(s);
-  const size_t want = (third_floats + 63) / 64 * 64;
-  bool mine_ok = cudaMalloc(&s->bbuf, kBigFlagBytes + 3 * want * 4) == cudaSuccess;
+  const size_t want = (half_floats + 63) / 64 * 64;
+  bool mine_ok = cudaMalloc(&s->bbuf, kBigFlagBytes + 2 * want * 4) == cudaSuccess;
   if (!mine_ok) {
     cudaGetLastError();
     s->bbuf = nullptr;
@@ -440,40 +476,71 @@ int p2p_big_ensure(ort_cuda_session* s, size_t third_floats, bool* ok) {
     return ORT_CUDA_OK;  // every rank keeps the NCCL path
   }
   s->bcap = want;
+  s->bepoch = 0;  // every rank restarts its epochs with the zeroed header
   *ok = true;
   return ORT_CUDA_OK;
 }
 
-float* p2p_big_third(ort_cuda_session* s, unsigned long long epoch) {
-  return (float*)((char*)s->bbuf + kBigFlagBytes) + (size_t)(epoch % 3) * s->bcap;
+namespace {
+float* big_half(void* base, size_t cap, unsigned long long epoch) {
+  return (float*)((char*)base + kBigFlagBytes) + (size_t)(epoch & 1) * cap;
+}
+}  // namespace
+
+int p2p_push_prepare(ort_cuda_session* s, unsigned long long epoch, int64_t M, int64_t ns,
+                     PrefillPush* push) {
+  unsigned long long* header = (unsigned long long*)s->bbuf;
+  if (epoch >= 3) {
+    p2p_push_wait_kernel<<<1, 32, 0, s->stream>>>(header, s->world, s->rank, epoch - 2,
+                                                  s->err_dev,
+                                                  (uint64_t)s->peer_wait_ms * 1000000ull);
+    ORTC_CUDA(cudaGetLastError());
+    s->launches++;
+  }
+  *push = PrefillPush();
+  for (int r = 0; r < s->world; r++) {
+    push->land[r] = big_half(s->bpeer[r], s->bcap, epoch) + (size_t)s->rank * M * ns;
+    push->flag[r] = (unsigned long long*)s->bpeer[r] + kReadySlot + s->rank;
+  }
+  push->ticket = reinterpret_cast<unsigned*>(header + kGemmTicketSlot);
+  push->epoch = epoch;
+  push->ns = ns;
+  push->rank = s->rank;
+  push->world = s->world;
+  return ORT_CUDA_OK;
 }
 
-int p2p_chunk_gather(ort_cuda_session* s, unsigned long long epoch, int64_t m, int64_t Ns,
-                     int64_t N, float* Y, cudaStream_t st) {
-  ChunkArgs a;
+int p2p_push_post(ort_cuda_session* s, const PrefillPush& push) {
+  p2p_push_post_kernel<<<1, 32, 0, s->stream>>>(push);
+  ORTC_CUDA(cudaGetLastError());
+  s->launches++;
+  return ORT_CUDA_OK;
+}
+
+int p2p_push_land(ort_cuda_session* s, unsigned long long epoch, int64_t M, int64_t ns,
+                  int64_t N, float* Y) {
+  LandArgs a;
   for (int r = 0; r < 8; r++) {
     a.src[r] = nullptr;
-    a.flag[r] = nullptr;
+    a.consumed[r] = nullptr;
   }
   for (int r = 0; r < s->world; r++) {
-    a.src[r] = (const float*)((char*)s->bpeer[r] + kBigFlagBytes) + (size_t)(epoch % 3) * s->bcap;
-    a.flag[r] = (unsigned long long*)s->bpeer[r] + s->rank;
+    a.src[r] = big_half(s->bbuf, s->bcap, epoch) + (size_t)r * M * ns;
+    a.consumed[r] = (unsigned long long*)s->bpeer[r] + kConsumedSlot + s->rank;
   }
-  a.mine = (const unsigned long long*)s->bbuf;
+  a.header = (unsigned long long*)s->bbuf;
   a.epoch = epoch;
   a.Y = Y;
-  a.ldy = N;
-  a.m = (int)m;
-  a.Ns = (int)Ns;
+  a.m = (int)M;
+  a.Ns = (int)ns;
   a.N = (int)N;
   a.rank = s->rank;
   a.world = s->world;
   a.err = s->err_dev;
   a.wait_ns = (uint64_t)s->peer_wait_ms * 1000000ull;
-  // two CTAs on each SM the GEMM beside it leaves free
-  const unsigned blocks =
-      (unsigned)std::max<int64_t>(1, std::min<int64_t>(m * s->world, 2 * kGatherSms));
-  p2p_chunk_gather_kernel<<<blocks, kChunkThreads, 0, st>>>(a);
+  const unsigned blocks = (unsigned)std::max<int64_t>(
+      1, std::min<int64_t>(M * s->world, (int64_t)s->sm_count * 2));
+  p2p_push_land_kernel<<<blocks, kLandThreads, 0, s->stream>>>(a);
   ORTC_CUDA(cudaGetLastError());
   s->launches++;
   return ORT_CUDA_OK;

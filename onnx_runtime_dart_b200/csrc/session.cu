@@ -435,8 +435,6 @@ ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s) {
   if (s->amaxbuf) cudaFree(s->amaxbuf);
   for (cudaEvent_t& e : s->chunk_ev)
     if (e) cudaEventDestroy(e);
-  for (cudaEvent_t& e : s->big_ev)
-    if (e) cudaEventDestroy(e);
   if (s->comm_stream) cudaStreamDestroy(s->comm_stream);
   s->comm_stream = nullptr;
   s->sync_ev = nullptr;
@@ -1531,12 +1529,13 @@ namespace {
 size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // N-sharded MatMulNBits in a tensor-core mode whose output is too large for
-// the peer exchange buffers (prefill): the rows are cut into chunks, and
-// while the session stream runs the GEMM of chunk c + 1, the exchange
-// stream all-gathers chunk c (NCCL) and re-lays it into Y, so the NVLink
-// transfer overlaps the tensor-core work instead of following it.  yloc is
-// [M, Ns], gath [G, M, Ns] (chunk c's gather lands at rows r0.. of every
-// rank's part, contiguous per chunk), Y [M, N].
+// the peer exchange buffers (prefill).  With the fp16 fused GEMM and mapped
+// peers the GEMM pushes its output to the peers itself (below).  Otherwise
+// the rows are cut into chunks, and while the session stream runs the GEMM
+// of chunk c + 1, the exchange stream all-gathers chunk c (NCCL) and
+// re-lays it into Y, so the NVLink transfer overlaps the tensor-core work.
+// yloc is [M, Ns], gath [G, M, Ns] (chunk c's gather lands at rows r0.. of
+// every rank's part, contiguous per chunk), Y [M, N].
 int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_t M,
                           float* yloc, float* gath, float* Y, int mode) {
   const int64_t N = w.N, ns = w.ns, G = s->world;
@@ -1554,39 +1553,29 @@ int nbits_prefill_chunked(ort_cuda_session* s, Weight& w, const float* A, int64_
   for (int i = 0; i <= 16; i++)
     if (!s->chunk_ev[i])
       ORTC_CUDA(cudaEventCreateWithFlags(&s->chunk_ev[i], cudaEventDisableTiming));
-  for (int i = 0; i < 3; i++)
-    if (!s->big_ev[i]) ORTC_CUDA(cudaEventCreateWithFlags(&s->big_ev[i], cudaEventDisableTiming));
-  bool big = false;
-  int rc0 = p2p_big_ensure(s, (size_t)(mc * ns), &big);
-  if (rc0) return rc0;
+  // Push mode (fp16 fused GEMM, peers mapped): the whole GEMM at once, its
+  // epilogue storing each row slice into every peer's big buffer as well as
+  // into this rank's columns of Y; a landing kernel then copies the peers'
+  // blocks into Y (local memory only).  Every rank decides alike: the
+  // conditions depend on shapes and on the mapping all ranks agreed on.
+  if (mode == ORT_CUDA_MODE_MMA_F16 && nbits_gemm_f16_layout_ok(w)) {
+    bool big = false;
+    int rc = p2p_big_ensure(s, (size_t)(G * M * ns), &big);
+    if (rc) return rc;
+    if (big) {
+      const unsigned long long e = ++s->bepoch;
+      PrefillPush push;
+      rc = p2p_push_prepare(s, e, M, ns, &push);
+      if (rc) return rc;
+      rc = w.nl > 0 ? launch_mma_nbits(s, w, A, M, Y + w.n0, N, mode, s->stream, 0, &push)
+                    : p2p_push_post(s, push);
+      if (rc) return rc;
+      return p2p_push_land(s, e, M, ns, N, Y);
+    }
+  }
   // the exchange stream starts after everything queued before this call
   ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->stream));
   ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[16], 0));
-  if (big) {
-    // Peer memory: each chunk's GEMM writes into a third of this rank's
-    // big exchange buffer and the chunk gather (pull over NVLink, beside
-    // the next chunk's GEMM) fills Y.  Third e % 3 is written again at epoch
-    // e + 3, after this rank's gather of epoch e + 1 finished: that gather
-    // saw every peer post e + 1, which each does after its gather of e.
-    for (int64_t c = 0; c < nch; c++) {
-      const int64_t r0 = c * mc, m = std::min(mc, M - r0);
-      const unsigned long long e = ++s->bepoch;
-      if (e >= 3) ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->big_ev[(e - 2) % 3], 0));
-      // the gather of the previous chunk runs beside this GEMM on the SMs
-      // it leaves free
-      int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, p2p_big_third(s, e), ns, mode, s->stream,
-                                nch > 1 ? kGatherSms : 0);
-      if (rc) return rc;
-      ORTC_CUDA(cudaEventRecord(s->chunk_ev[c], s->stream));
-      ORTC_CUDA(cudaStreamWaitEvent(s->comm_stream, s->chunk_ev[c], 0));
-      rc = p2p_chunk_gather(s, e, m, ns, N, Y + r0 * N, s->comm_stream);
-      if (rc) return rc;
-      ORTC_CUDA(cudaEventRecord(s->big_ev[e % 3], s->comm_stream));
-    }
-    ORTC_CUDA(cudaEventRecord(s->chunk_ev[16], s->comm_stream));
-    ORTC_CUDA(cudaStreamWaitEvent(s->stream, s->chunk_ev[16], 0));
-    return ORT_CUDA_OK;
-  }
   for (int64_t c = 0; c < nch; c++) {
     const int64_t r0 = c * mc, m = std::min(mc, M - r0);
     int rc = launch_mma_nbits(s, w, A + r0 * w.K, m, yloc + r0 * ns, ns, mode, s->stream);
