@@ -96,6 +96,7 @@ __device__ __forceinline__ uint32_t deq2(uint32_t h, uint32_t zz, uint32_t s) {
   return d;
 }
 
+template <bool PUSH>
 __global__ void __launch_bounds__(kThreadsP, 1)
     nbits_gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmQ,
@@ -289,11 +290,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           if (row < p.M && n < p.N) {
             const float v = scale_pow2(buf[j * 33 + lane], e + f);
             p.Y[(int64_t)row * p.ldy + n] = v;
-            // push mode: the same value into every peer's landing block
+            if constexpr (PUSH) {  // the same value into every peer's landing block
 #pragma unroll
-            for (int r = 0; r < 8; r++)
-              if (r < p.push.world && r != p.push.rank)
-                p.push.land[r][(int64_t)row * p.push.ns + n] = v;
+              for (int r = 0; r < 8; r++)
+                if (r < p.push.world && r != p.push.rank)
+                  p.push.land[r][(int64_t)row * p.push.ns + n] = v;
+            }
           }
         }
         __syncwarp();
@@ -305,14 +307,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   }
   // push mode: this thread's stores to the peers are visible system-wide
   // before the CTA counts itself done; the last CTA posts the epoch
-  if (p.push.world > 0) __threadfence_system();
+  if (PUSH) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  if (p.push.world > 0 && threadIdx.x == 0) {
+  if (PUSH && threadIdx.x == 0) {
     __threadfence_system();
     if (atomicAdd(p.push.ticket, 1u) == gridDim.x - 1) {
       *p.push.ticket = 0u;
@@ -401,14 +403,19 @@ int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_e
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !(configured.load() >> dev & 1ull)) {
-    ORTC_CUDA(cudaFuncSetAttribute(nbits_gemm_f16_kernel,
+    ORTC_CUDA(cudaFuncSetAttribute(nbits_gemm_f16_kernel<false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemP));
+    ORTC_CUDA(cudaFuncSetAttribute(nbits_gemm_f16_kernel<true>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemP));
     if (dev < 64) configured.fetch_or(1ull << dev);
   }
   // persistent: one CTA per SM, leaving reserve_sms SMs to a kernel that
   // runs beside it (this GEMM's shared memory leaves no room on its SMs)
   const int grid = std::min(p.tiles, std::max(1, sm_count - reserve_sms));
-  nbits_gemm_f16_kernel<<<grid, kThreadsP, kSmemP, st>>>(tmA, tmQ, tmSZ, p);
+  if (push)
+    nbits_gemm_f16_kernel<true><<<grid, kThreadsP, kSmemP, st>>>(tmA, tmQ, tmSZ, p);
+  else
+    nbits_gemm_f16_kernel<false><<<grid, kThreadsP, kSmemP, st>>>(tmA, tmQ, tmSZ, p);
   ORTC_CUDA(cudaGetLastError());
   (*launches)++;
   return ORT_CUDA_OK;
