@@ -776,18 +776,19 @@ def main():
         traffic, traffic_note = None, None
         tp = os.path.join(ROOT, "profiles", "gemv_lm_head_traffic.json")
         if os.path.exists(tp):
-            tr = json.load(open(tp))
-            if world == 1 and tr.get("plan") == plans.get(big.name):
-                traffic = tr["dram_bytes_per_launch"]
-                traffic_note = f"ncu capture of the same plan ({tr.get('kernel')})"
-            elif world > 1:
-                # the capture is of the full weight on one GPU; a rank's shard
-                # moves its share of it
-                traffic = tr["dram_bytes_per_launch"] * (bb - ba) / big.N
-                traffic_note = "1-GPU ncu capture scaled to this rank's column shard"
+            tr = json.load(open(tp)).get("plans", {})
+            key = str(plans.get(big.name))
+            if key in tr and world == 1:
+                traffic = tr[key]
+                traffic_note = f"ncu capture of the same plan ({key}), all of the op's launches"
+            elif key in tr:
+                # a 1-GPU capture of the full weight; a rank's shard moves its
+                # share of it (the traffic grows with the columns)
+                traffic = tr[key] * (bb - ba) / big.N
+                traffic_note = f"1-GPU ncu capture of plan {key} scaled to this rank's shard"
             else:
-                traffic_note = (f"no capture of the plan this run chose ({plans.get(big.name)}); "
-                                f"the committed one is of plan {tr.get('plan')}")
+                traffic_note = (f"no capture of the plan this run chose ({key}); captured: "
+                                f"{sorted(tr)}")
         cpu = None
         if do_cpu:
             v, reps, dt, b = cpu_sample(projs, weights, args.cpu_seconds, threads)

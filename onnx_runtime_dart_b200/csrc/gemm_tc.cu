@@ -91,7 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * TBM, n0 = blockIdx.x * TBN;
+  // row tiles vary fastest: CTAs resident together share a weight tile (read
+  // from DRAM about once) and re-read A, which stays in L2
+  const int m0 = blockIdx.x * TBM, n0 = blockIdx.y * TBN;
   const int nk = (K + TBK - 1) / TBK;
 
   if (threadIdx.x == 0) {
@@ -410,7 +412,9 @@ int launch_gemm(ort_cuda_session* s, const uint16_t* A16, const int* row_exp, in
                                    (int)Ring<true>::kSmemBytes));
     if (dev < 64) configured.fetch_or(1ull << dev);
   }
-  dim3 grid((unsigned)((nl + TBN - 1) / TBN), (unsigned)((M + TBM - 1) / TBM));
+  ORTC_CHECK((nl + TBN - 1) / TBN <= 65535, ORT_CUDA_ERR_UNSUPPORTED,
+             "tensor-core GEMM: more than 65535 column tiles");
+  dim3 grid((unsigned)((M + TBM - 1) / TBM), (unsigned)((nl + TBN - 1) / TBN));
   if (bf16)
     mma_gemm_kernel<true><<<grid, kThreads, Ring<true>::kSmemBytes, st>>>(
         tmA, tmB, tmA2, tmB2, (int)K, idesc_f16(1, TBM, TBN), ep);

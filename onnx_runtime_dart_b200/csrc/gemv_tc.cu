@@ -55,6 +55,8 @@
 #include <cstdlib>
 #include <vector>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
@@ -241,7 +243,10 @@ __device__ __forceinline__ void x_digits(float4 a, const RowScale& r, uint32_t& 
   w2 = __byte_perm(hi01, hi23, 0x5410);
 }
 
-template <int M>
+// EXT: the stores go through ysel_store (push to peers, segmented output of
+// a fused group, fused ArgMax keys); without it, the plain stores of a
+// single-GPU or pull-mode call, with none of those branches in the epilogue.
+template <int M, bool EXT>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
                    const __grid_constant__ CUtensorMap tmZ, const TcParams p) {
@@ -301,8 +306,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
     mbar_init(fin, 1);
     mbar_init(xsync, kDeWarps);
-    for (int m = 0; m < 8; m++) s_amax[m] = 0ull;
-    *s_nan0 = 0u;
+    if (EXT) {
+      for (int m = 0; m < 8; m++) s_amax[m] = 0ull;
+      *s_nan0 = 0u;
+    }
     mbar_init(ibar, p.csize * kEpiWarps);
     mbar_init(&abar[0], 1);
     mbar_init(&abar[1], 1);
@@ -714,7 +721,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (lane == 0 && egrp == 0)
       for (int e = 0; e < p.nd; e++) mbar_arrive(&ready[e]);
     griddep_wait();  // outputs and split-K scratch may still be in use upstream
-    const unsigned long long ep = ysel_epoch(p.ysel);  // push mode's tag
+    const unsigned long long ep = EXT ? ysel_epoch(p.ysel) : 0ull;  // push mode's tag
     __syncwarp();    // .aligned cluster barrier: the whole warp, converged
     if (clustered) cluster_wait();
     const int set = (int)blockIdx.x / p.csize;
@@ -814,8 +821,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const float acc = chunk == 0 ? 0.0f + part[m] : ya[m * kTile + nl] + part[m];
           ya[m * kTile + nl] = acc;
           if (chunk == p.nch - 1 && n < p.N) {
-            ysel_store(ysel_base(p.Y, p.ysel), p.ldy, p.ysel, ep, m, n, acc);
-            if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+            if constexpr (EXT) {
+              ysel_store(ysel_base(p.Y, p.ysel), p.ldy, p.ysel, ep, m, n, acc);
+              if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+            } else {
+              ysel_base(p.Y, p.ysel)[m * p.ldy + n] = acc;
+            }
           }
         }
       } else if (clustered) {
@@ -874,8 +885,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
             for (; c < p.nch; c++) acc = acc + col[(size_t)c * per];
             if (n < p.N) {
-              ysel_store(Yb, p.ldy, p.ysel, ep, m, n, acc);
-              if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+              if constexpr (EXT) {
+                ysel_store(Yb, p.ldy, p.ysel, ep, m, n, acc);
+                if (p.ysel.amax) amax_add(p.ysel, s_amax, s_nan0, m, n, acc);
+              } else {
+                Yb[m * p.ldy + n] = acc;
+              }
             }
           }
         }
@@ -892,25 +907,29 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     tmem_dealloc(tmem, kTmemCols);
   }
   // the split-K GEMV stores partials only; its chunk-sum kernel does this
-  if (p.ysel.amax && p.tile_major) amax_finish(p.ysel, s_amax, s_nan0, s_last, M);
+  if constexpr (EXT)
+    if (p.ysel.amax && p.tile_major) amax_finish(p.ysel, s_amax, s_nan0, s_last, M);
 }
 
 // Split-K: Y[m, n] = ((0 + part[0]) + part[1]) + ... in chunk order, the same
 // sum the tile-major path forms, so both give identical bits.  Launched as a
 // programmatic dependent of the GEMV: its small CTAs become resident beside
 // the GEMV's and wait in griddepcontrol.wait, so no launch gap follows.
+template <bool EXT>
 __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __restrict__ part,
                                                            float* Y, int64_t ldy, int M, int N,
                                                            int nch, int64_t npad, YSel ysel) {
   __shared__ unsigned long long s_amax[8];
   __shared__ unsigned s_nan0, s_last;
-  if (threadIdx.x < 8) s_amax[threadIdx.x] = 0ull;
-  if (threadIdx.x == 0) s_nan0 = 0u;
-  __syncthreads();
   griddep_launch_dependents();
+  if (EXT) {
+    if (threadIdx.x < 8) s_amax[threadIdx.x] = 0ull;
+    if (threadIdx.x == 0) s_nan0 = 0u;
+    __syncthreads();
+  }
   griddep_wait();
   Y = ysel_base(Y, ysel);
-  const unsigned long long ep = ysel_epoch(ysel);
+  const unsigned long long ep = EXT ? ysel_epoch(ysel) : 0ull;
   const int64_t total = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -928,12 +947,18 @@ __global__ void __launch_bounds__(128) gemv_tc_reduce_kernel(const float* __rest
       for (int c = 0; c < 32; c++)
         if (c0 + c < nch) acc = acc + v[c];
     }
-    ysel_store(Y, ldy, ysel, ep, m, n, acc);
-    if (ysel.amax) amax_add(ysel, s_amax, &s_nan0, m, n, acc);
+    if constexpr (EXT) {
+      ysel_store(Y, ldy, ysel, ep, m, n, acc);
+      if (ysel.amax) amax_add(ysel, s_amax, &s_nan0, m, n, acc);
+    } else {
+      Y[m * ldy + n] = acc;
+    }
   }
-  if (ysel.amax) {
-    __syncthreads();
-    amax_finish(ysel, s_amax, &s_nan0, &s_last, M);
+  if constexpr (EXT) {
+    if (ysel.amax) {
+      __syncthreads();
+      amax_finish(ysel, s_amax, &s_nan0, &s_last, M);
+    }
   }
 }
 
@@ -949,13 +974,15 @@ uint32_t tc_stage_bytes(const Weight& w) {
 // Raises the GEMV's shared-memory limit, once per device.
 template <int M>
 int configure_m() {
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kSmemLimit));
-    configured |= 1ull << (dev & 63);
+  if (dev >= 64 || !(configured.load() >> dev & 1ull)) {
+    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit));
+    ORTC_CUDA(cudaFuncSetAttribute(gemv_tc_kernel<M, true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit));
+    if (dev < 64) configured.fetch_or(1ull << dev);
   }
   return ORT_CUDA_OK;
 }
@@ -982,7 +1009,7 @@ int max_clusters_m(int csize) {
       qa[0].val.clusterDim.z = 1;
       qc.attrs = qa;
       qc.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<M>, &qc) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, gemv_tc_kernel<M, false>, &qc) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -1154,7 +1181,13 @@ int launch_m(const Weight& w, TcParams& p, const Plan& pl, cudaStream_t st) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pl.csize > 1 ? 2 : 1;
-  ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M>, w.tmB, w.tmS, w.has_zp ? w.tmZ : w.tmS, p));
+  const bool ext = p.ysel.push || p.ysel.nseg > 0 || p.ysel.amax != nullptr;
+  if (ext)
+    ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M, true>, w.tmB, w.tmS,
+                                 w.has_zp ? w.tmZ : w.tmS, p));
+  else
+    ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_kernel<M, false>, w.tmB, w.tmS,
+                                 w.has_zp ? w.tmZ : w.tmS, p));
   return ORT_CUDA_OK;
 }
 
@@ -1269,8 +1302,15 @@ int launch_plan(const Weight& w, const Plan& pl, const float* A, int64_t M, floa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_reduce_kernel, (const float*)partials, Y, ldy,
-                                 (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile, p.ysel));
+    const bool ext = p.ysel.push || p.ysel.nseg > 0 || p.ysel.amax != nullptr;
+    if (ext)
+      ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_reduce_kernel<true>, (const float*)partials, Y,
+                                   ldy, (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile,
+                                   p.ysel));
+    else
+      ORTC_CUDA(cudaLaunchKernelEx(&cfg, gemv_tc_reduce_kernel<false>, (const float*)partials, Y,
+                                   ldy, (int)M, (int)w.nl, pl.nch, (int64_t)pl.tiles * kTile,
+                                   p.ysel));
     (*launches)++;
   }
   return ORT_CUDA_OK;
