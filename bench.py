@@ -376,13 +376,16 @@ def leg_nbits(bench, tag, projs, weights, M, mode, bs, scale_bytes, zp, reps, fl
     return out
 
 
-def leg_cfg4_grouped(bench, c4, w4, M, reps, hbm):
-    """cfg4's decode step with each layer's sibling projections fused
+def leg_cfg4_grouped(bench, c4, w4, M, reps, hbm, tpk=None, mode="exact"):
+    """cfg4's step with each layer's sibling projections fused
     (ort_cuda_fuse_nbits: q/k/v and gate/up) and run as one operation each
     (ort_cuda_matmul_nbits_group): 4 operations per layer instead of 7, the
-    same weights, bytes and results."""
+    same weights, bytes and results.  Decode (M=4, exact) or prefill
+    (M=2048, fp16)."""
     torch = bench.torch
-    from onnx_runtime_dart_b200.workloads import nbits_bytes
+    from onnx_runtime_dart_b200 import _lib
+    from onnx_runtime_dart_b200.workloads import nbits_bytes, nbits_flops
+    flags = _lib.flags_mode(_lib.MODES[mode])
     sess, dev = bench.sess, bench.dev
     for p in c4:
         B, s, z = w4[p.name]
@@ -400,28 +403,36 @@ def leg_cfg4_grouped(bench, c4, w4, M, reps, hbm):
     outs = {}
     for kind, nm, K in steps:
         if kind == "group":
-            outs[nm] = sess.matmul_nbits_group(nm, A[K])
+            outs[nm] = sess.matmul_nbits_group(nm, A[K], flags=flags)
         else:
-            outs[nm] = sess.matmul_nbits(nm, A[K])
+            outs[nm] = sess.matmul_nbits(nm, A[K], flags=flags)
 
     def step():
         for kind, nm, K in steps:
             if kind == "group":
-                sess.matmul_nbits_group(nm, A[K], outs=outs[nm])
+                sess.matmul_nbits_group(nm, A[K], outs=outs[nm], flags=flags)
             else:
-                sess.matmul_nbits(nm, A[K], out=outs[nm])
+                sess.matmul_nbits(nm, A[K], out=outs[nm], flags=flags)
 
-    ms = bench.max_over_ranks([bench.time_fn(step, reps, False)])[0]
+    ms = bench.max_over_ranks([bench.time_fn(step, reps, False, graph=M <= 16)])[0]
     for kind, nm, K in steps:
         sess.drop_weight(nm)
-    bytes_step = sum(nbits_bytes(p.K, p.N, BS, M, 2, False) for p in c4)
-    gbs = bytes_step / (ms * 1e-3) / 1e9
-    return {"workload": "cfg4 decode step at M=4 with sibling projections fused: per layer "
-                        "qkv (q,k,v) and gate_up (gate,up) as one operation each, o, down; "
-                        "plus lm_head (65 operations instead of 113; same weights and bytes)",
-            "M": M, "mode": "exact", "ms_per_step": ms, "value": gbs, "unit": "GB/s",
-            "bound": "hbm", "frac": gbs / hbm, "bytes_per_step": bytes_step,
-            "l2": "weights larger than L2"}
+    del outs, A
+    out = {"workload": f"cfg4 step at M={M} with sibling projections fused: per layer "
+                       "qkv (q,k,v) and gate_up (gate,up) as one operation each, o, down; "
+                       "plus lm_head (65 operations instead of 113; same weights and results)",
+           "M": M, "mode": mode, "ms_per_step": ms}
+    if M <= 16:
+        bytes_step = sum(nbits_bytes(p.K, p.N, BS, M, 2, False) for p in c4)
+        gbs = bytes_step / (ms * 1e-3) / 1e9
+        out.update({"value": gbs, "unit": "GB/s", "bound": "hbm", "frac": gbs / hbm,
+                    "bytes_per_step": bytes_step, "l2": "weights larger than L2"})
+    else:
+        flops = sum(nbits_flops(p.K, p.N, M) for p in c4)
+        tf = flops / (ms * 1e-3) / 1e12
+        out.update({"value": tf, "unit": "TFLOP/s", "bound": "tensor", "frac": tf / tpk,
+                    "flops_per_step": flops})
+    return out
 
 
 def main():
@@ -683,6 +694,8 @@ def main():
             bench, "c4p", c4, w4, PREFILL_M, "mma_f16", BS, 2, False, 3, False,
             "cfg4 prefill: the same 113 projections at M=2048 (4 x 512 tokens), fp16 "
             "tensor-core mode", hbm, tpk)
+        configs["cfg4_prefill_m2048_grouped"] = leg_cfg4_grouped(
+            bench, c4, w4, PREFILL_M, 3, hbm, tpk, mode="mma_f16")
         del w4
 
         # cfg2: fp32 Gemm with prepacked B (transB=1, alpha=beta=1) at the

@@ -9,22 +9,28 @@
 // gemm_kernel_simd.dart:27-309).  A16 is the activation converted once per
 // call to fp16 with a power-of-two row normalisation e_m; f_n normalises
 // each weight column so its largest |(q - z) * scale| lies in [2^14, 2^15).
-// Packed weights are read once per 128-row band of A straight from their
+// Packed weights are read once per 256-row band of A straight from their
 // upload layout; no 16-bit copy of the weights is written to HBM.
 //
-// Persistent kernel, one CTA per SM, tiles of 128 (m) x 256 (n), 64-k stages:
-//   warp 0      TMA producer: A tile (128 x 64 fp16, 128-byte swizzle), the
-//               packed int4 tile (256 columns x 32 bytes, 32-byte swizzle) and the stage's
-//               {1024 + z, scale'} table (fp16 pairs) into a 4-stage ring
-//   warps 2-9   converters: thread n owns weight column n of the tile; per
-//               8 weights two masks, four byte permutes (nibble | 0x6400 is
-//               the fp16 value 1024 + q), four exact subtractions of
-//               1024 + z and four multiplies by the scale (one rounding),
-//               stored as the MMA's K-major 128-byte-swizzled B tile
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32
-//               accumulators); an elect.sync leader waits once per stage and
-//               issues 4 MMAs (M=128, N=256, K=16), tcgen05.commit frees the
-//               stage and the converted tile
+// Persistent kernel, one CTA per SM, tiles of 256 (m) x 128 (n), 64-k stages.
+// The converted weight tile is the expensive operand (the converter warps
+// bound the kernel), so each one serves 256 rows of A: two M=128 MMAs per
+// 16-k step share it.
+//   warp 0      TMA producer: A tile (256 x 64 fp16, 128-byte swizzle), the
+//               packed int4 tile (128 columns x 32 bytes, 32-byte swizzle)
+//               and the stage's {1024 + z, scale'} table (fp16 pairs) into a
+//               4-stage ring
+//   warps 2-9   converters: threads n and n + 128 share weight column n of
+//               the tile (k 0-31 and 32-63 of the stage); per 8 weights two
+//               masks, four byte permutes (nibble | 0x6400 is the fp16 value
+//               1024 + q), four exact subtractions of 1024 + z and four
+//               multiplies by the scale (one rounding), stored as the MMA's
+//               K-major 128-byte-swizzled B tile
+//   warp 1      allocates 512 TMEM columns (two accumulators, each two
+//               128 x 128 fp32 halves); an elect.sync leader waits once per
+//               stage and issues 8 MMAs (M=128, N=128, K=16: both halves of
+//               A against the same B), tcgen05.commit frees the stage and
+//               the converted tile
 //   warps 10-13 epilogue: tcgen05.ld of the finished accumulator while the
 //               MMAs fill the other one, exact 2^(e_m + f_n) scaling, and
 //               coalesced stores through a per-warp shared-memory transpose
@@ -42,14 +48,15 @@
 namespace ortc {
 namespace {
 
-constexpr int PBM = 128, PBN = 256, PBK = 64;
+constexpr int PBM = 256, PBN = 128, PBK = 64;
+constexpr int kHalf = 128;                           // rows of one MMA (M)
 constexpr int kRaw = 4;                              // producer ring depth
 constexpr int kConv = 3;                             // converted B tiles
-constexpr uint32_t kABytes = PBM * PBK * 2;          // 16 KB fp16 A tile
-constexpr uint32_t kQBytes = PBN * PBK / 2;          // 8 KB packed int4 tile
+constexpr uint32_t kABytes = PBM * PBK * 2;          // 32 KB fp16 A tile
+constexpr uint32_t kQBytes = PBN * PBK / 2;          // 4 KB packed int4 tile
 constexpr uint32_t kSZBytes = PBN * 4 * 4;           // up to 4 blocks per stage
-constexpr uint32_t kRawBytes = kABytes + kQBytes + kSZBytes;  // 28 KB
-constexpr uint32_t kCBytes = PBN * PBK * 2;          // 32 KB fp16 B tile
+constexpr uint32_t kRawBytes = kABytes + kQBytes + kSZBytes;  // 38 KB
+constexpr uint32_t kCBytes = PBN * PBK * 2;          // 16 KB fp16 B tile
 constexpr int kConvWarp0 = 2, kConvWarps = 8, kEpiWarp0 = 10;
 constexpr int kThreadsP = 14 * 32;
 constexpr uint32_t kEpiFloats = 32 * 33;             // per epilogue warp
@@ -179,7 +186,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_f16(0, PBM, PBN);
+      constexpr uint32_t idesc = idesc_f16(0, kHalf, PBN);
       uint32_t g = 0, tcount = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, tcount++) {
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t dt = tmem + d * PBN;
+        const uint32_t dt = tmem + d * (2 * PBN);  // halves at + 0 and + PBN
         for (int kb = 0; kb < nk; kb++, g++) {
           const int s = g % kRaw, c = g % kConv;
           if (!mbar_wait(&conv_full[c], (g / kConv) & 1)) {
@@ -203,8 +210,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const uint32_t sb = smem_u32(conv + c * kCBytes);
 #pragma unroll
           for (int kk = 0; kk < PBK / 16; kk++)
-            mma_f16_ss(dt, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), idesc,
-                       (kb | kk) != 0);
+#pragma unroll
+            for (int h = 0; h < 2; h++)  // rows 128h .. 128h + 127 of A: 16 KB apart
+              mma_f16_ss(dt + h * PBN, smem_desc_sw128(sa + h * (kABytes / 2) + kk * 32),
+                         smem_desc_sw128(sb + kk * 32), idesc, (kb | kk) != 0);
           mma_commit(&raw_empty[s]);
           mma_commit(&conv_empty[c]);
         }
@@ -215,8 +224,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
     __syncwarp();
   } else if (warp < kConvWarp0 + kConvWarps) {
-    // ---------------- converters: thread n owns weight column n ----------
-    const int n = threadIdx.x - kConvWarp0 * 32;
+    // ---------------- converters: column n, words 4 hw .. 4 hw + 3 -------
+    const int tid = threadIdx.x - kConvWarp0 * 32;
+    const int n = tid & (PBN - 1), hw = tid / PBN;
     const uint32_t rowoff = (uint32_t)((n >> 3) * 1024 + (n & 7) * 128);
     const int sw = n & 7;
     uint32_t g = 0;
@@ -237,15 +247,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const uint32_t qa = smem_u32(st + kABytes) + n * 32;
         const uint32_t* sz = reinterpret_cast<const uint32_t*>(st + kABytes + kQBytes);
         const uint32_t qsw = (uint32_t)((n >> 2) & 1) << 4;
-        const uint4 w0 = lds128(qa + qsw), w1 = lds128(qa + (16 ^ qsw));
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint4 w4 = lds128(qa + ((uint32_t)(hw << 4) ^ qsw));
+        const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
         const uint32_t cb = smem_u32(conv + c * kCBytes) + rowoff;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
+        for (int j = 0; j < 4; j++) {
           // word i holds k 8i..8i+7; its block within the stage's table
+          const int i = 4 * hw + j;
           const uint32_t v = sz[((8 * i) >> p.bs_shift) * PBN + n];
           const uint32_t zz = prmt(v, v, 0x1010), sc = prmt(v, v, 0x3232);
-          const uint32_t lo = words[i] & 0x0F0F0F0Fu, hi = (words[i] >> 4) & 0x0F0F0F0Fu;
+          const uint32_t lo = words[j] & 0x0F0F0F0Fu, hi = (words[j] >> 4) & 0x0F0F0F0Fu;
           const uint32_t r0 = deq2(prmt(lo, 0x64646464u, 0x4140), zz, sc);  // k0, k1
           const uint32_t r1 = deq2(prmt(lo, 0x64646464u, 0x4342), zz, sc);  // k2, k3
           const uint32_t r2 = deq2(prmt(hi, 0x64646464u, 0x4140), zz, sc);  // k4, k5
@@ -272,11 +283,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         break;
       }
       tc_fence_after();
-      const int rbase = m0 + q * 32;
-      const int my_e = rbase + lane < p.M ? p.row_exp[rbase + lane] : 0;
+      for (int h = 0; h < 2; h++)
       for (int c0 = 0; c0 < PBN; c0 += 32) {
+        const int rbase = m0 + h * kHalf + q * 32;
+        const int my_e = rbase + lane < p.M ? p.row_exp[rbase + lane] : 0;
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + d * PBN + c0, r);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + d * (2 * PBN) + h * PBN + c0, r);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; j++) buf[lane * 33 + j] = __uint_as_float(r[j]);
