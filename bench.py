@@ -342,10 +342,17 @@ def leg_nbits(bench, tag, projs, weights, M, mode, bs, scale_bytes, zp, reps, fl
     A = {K: torch.randn(M, K, device=dev, generator=gen) for K in sorted({p.K for p in projs})}
     Y = {nm: torch.empty(M, p.N, device=dev) for nm, p in names}
     flags = _lib.flags_mode(_lib.MODES[mode])
+    # the C ABI called directly (as a Dart binding would): the Python
+    # wrapper's own overhead would otherwise bound the eager prefill legs
+    L = _lib.load()
+    h = ctypes.c_void_p(sess.handle)
+    calls = [(nm.encode(), A[p.K].data_ptr(), Y[nm].data_ptr()) for nm, p in names]
 
     def step():
-        for nm, p in names:
-            sess.matmul_nbits(nm, A[p.K], out=Y[nm], flags=flags)
+        for nb_, a_, y_ in calls:
+            rc = L.ort_cuda_matmul_nbits(h, nb_, a_, M, y_, flags)
+            if rc:
+                _lib.check(rc, "ort_cuda_matmul_nbits")
 
     bytes_step = sum(nbits_bytes(p.K, p.N, bs, M, scale_bytes, zp) for p in projs)
     flops_step = sum(nbits_flops(p.K, p.N, M) for p in projs)
@@ -415,12 +422,22 @@ def leg_cfg4_grouped(bench, c4, w4, M, reps, hbm, tpk=None, mode="exact"):
         else:
             outs[nm] = sess.matmul_nbits(nm, A[K], flags=flags)
 
+    L = _lib.load()
+    h = ctypes.c_void_p(sess.handle)
+    calls = []
+    for kind, nm, K in steps:
+        if kind == "group":
+            ptrs = (ctypes.c_void_p * len(outs[nm]))(*[o.data_ptr() for o in outs[nm]])
+            calls.append((L.ort_cuda_matmul_nbits_group, nm.encode(), A[K].data_ptr(), ptrs))
+        else:
+            calls.append((L.ort_cuda_matmul_nbits, nm.encode(), A[K].data_ptr(),
+                          outs[nm].data_ptr()))
+
     def step():
-        for kind, nm, K in steps:
-            if kind == "group":
-                sess.matmul_nbits_group(nm, A[K], outs=outs[nm], flags=flags)
-            else:
-                sess.matmul_nbits(nm, A[K], out=outs[nm], flags=flags)
+        for fn, nb_, a_, y_ in calls:
+            rc = fn(h, nb_, a_, M, y_, flags)
+            if rc:
+                _lib.check(rc, "matmul_nbits")
 
     ms = bench.max_over_ranks([bench.time_fn(step, reps, False, graph=M <= 16)])[0]
     for kind, nm, K in steps:

@@ -66,6 +66,10 @@ struct Weight {
   int64_t w16_rows = 0, w16_k = 0;
   int* col_exp = nullptr;   // [nl_pad] (F16 mode), else nullptr
   uint32_t* sz16 = nullptr;  // nbits f16 MMA: per-(blk,col) {1024 + z, scale * 2^-col_exp} as fp16
+  // the fused prefill GEMM's TMA views of the packed weight and of sz16,
+  // encoded on its first call (they depend on the weight only)
+  CUtensorMap tmQp, tmSZp;
+  bool prefill_maps = false;
   // MatMulInteger weight (W_INT8): this rank's columns K-major [nl][kpitch]
   // (kpitch = K rounded up to 16), their column sums and zero points (int32)
   uint8_t* Wi8 = nullptr;
@@ -541,7 +545,7 @@ bool nbits_gemm_f16_ok(const Weight& w);
 bool nbits_gemm_f16_layout_ok(const Weight& w);
 int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaStream_t st,
                        int64_t* launches);
-int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
+int launch_nbits_gemm_f16(Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
                           int reserve_sms = 0, const PrefillPush* push = nullptr);

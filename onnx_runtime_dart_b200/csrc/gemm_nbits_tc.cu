@@ -377,25 +377,31 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
   return ORT_CUDA_OK;
 }
 
-int launch_nbits_gemm_f16(const Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
+int launch_nbits_gemm_f16(Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
                           int reserve_sms, const PrefillPush* push) {
   if (M == 0 || w.nl == 0) return ORT_CUDA_OK;
   const int64_t K = w.K, nl = w.nl, col_bytes = (int64_t)w.nb * w.bs / 2;
-  CUtensorMap tmA, tmQ, tmSZ;
+  CUtensorMap tmA;
   int rc = encode_tma_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A16, (uint64_t)K, (uint64_t)M,
                          (uint64_t)K * 2, PBK, PBM, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = encode_tma_2d(&tmQ, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes, (uint64_t)nl,
-                     (uint64_t)col_bytes, PBK / 2, PBN, CU_TENSOR_MAP_SWIZZLE_32B);
   if (rc) return rc;
   int bs_shift = 0;
   while ((1 << bs_shift) < w.bs) bs_shift++;
   const int bps = w.bs >= PBK ? 1 : PBK / w.bs;
-  rc = encode_tma_2d(&tmSZ, CU_TENSOR_MAP_DATA_TYPE_UINT32, sz16, (uint64_t)nl, (uint64_t)w.nb,
-                     (uint64_t)w.s_pitch * 4, PBN, bps, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
+  if (!w.prefill_maps) {  // the weight's views, once
+    rc = encode_tma_2d(&w.tmQp, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.B, (uint64_t)col_bytes,
+                       (uint64_t)nl, (uint64_t)col_bytes, PBK / 2, PBN, CU_TENSOR_MAP_SWIZZLE_32B);
+    if (rc) return rc;
+    rc = encode_tma_2d(&w.tmSZp, CU_TENSOR_MAP_DATA_TYPE_UINT32, sz16, (uint64_t)nl,
+                       (uint64_t)w.nb, (uint64_t)w.s_pitch * 4, PBN, bps,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    w.prefill_maps = true;
+  }
+  const CUtensorMap& tmQ = w.tmQp;
+  const CUtensorMap& tmSZ = w.tmSZp;
   PParams p;
   p.Y = Y;
   p.ldy = ldy;
