@@ -25,6 +25,8 @@
 #include <algorithm>
 #include <climits>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -839,13 +841,13 @@ bool decode_ok(const AttnArgs& a, const AttnCfg& c) {
 
 template <int RTP>
 int launch_dec(const AttnArgs& a, size_t smem, int64_t grid, cudaStream_t st) {
-  static unsigned long long attr_set = 0;  // per device
+  static std::atomic<unsigned long long> attr_set{0};  // per device
   int dev = 0;
   ORTC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set >> dev & 1ull)) {
+  if (dev >= 64 || !(attr_set.load() >> dev & 1ull)) {
     ORTC_CUDA(cudaFuncSetAttribute(attn_decode_kernel<RTP>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
-    attr_set |= 1ull << dev;
+    if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   attn_decode_kernel<RTP><<<(unsigned)grid, kDecWarps * 32, smem, st>>>(a);
   ORTC_CUDA(cudaGetLastError());
@@ -854,13 +856,13 @@ int launch_dec(const AttnArgs& a, size_t smem, int64_t grid, cudaStream_t st) {
 
 template <int TX, int TY, int RM, int KC>
 int launch_cfg(const AttnArgs& a, size_t smem, int64_t grid, cudaStream_t st) {
-  static unsigned long long attr_set = 0;  // per device
+  static std::atomic<unsigned long long> attr_set{0};  // per device
   int dev = 0;
   ORTC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set >> dev & 1ull)) {
+  if (dev >= 64 || !(attr_set.load() >> dev & 1ull)) {
     ORTC_CUDA(cudaFuncSetAttribute(attn_kernel<TX, TY, RM, KC>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
-    attr_set |= 1ull << dev;
+    if (dev < 64) attr_set.fetch_or(1ull << dev);
   }
   attn_kernel<TX, TY, RM, KC><<<(unsigned)grid, TX * TY, smem, st>>>(a);
   ORTC_CUDA(cudaGetLastError());

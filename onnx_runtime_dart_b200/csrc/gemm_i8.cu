@@ -19,6 +19,8 @@
 // too small for the SMs split K: the slices add into a zeroed Y with int32
 // atomics (exact and order-free), the first slice adding the correction.
 // Every wait is bounded; on expiry the kernel records an error and returns.
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
@@ -197,13 +199,13 @@ template <int TBA>
 int launch_tba(const CUtensorMap& tmW, const CUtensorMap& tmA, uint32_t idesc, const I8Params& p,
                dim3 grid, cudaStream_t st) {
   constexpr size_t smem = 1024 + kI8Stages * (size_t)(IBW * IBK + TBA * IBK) + 256;
-  static unsigned long long configured = 0;
+  static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
+  if (dev >= 64 || !(configured.load() >> dev & 1ull)) {
     ORTC_CUDA(cudaFuncSetAttribute(matmul_i8_kernel<TBA>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured |= 1ull << (dev & 63);
+    if (dev < 64) configured.fetch_or(1ull << dev);
   }
   matmul_i8_kernel<TBA><<<grid, kI8Threads, smem, st>>>(tmW, tmA, idesc, p);
   ORTC_CUDA(cudaGetLastError());

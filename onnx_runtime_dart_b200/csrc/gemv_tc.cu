@@ -991,11 +991,11 @@ int configure_m() {
 // device, cached; -1 when none can be launched.
 template <int M>
 int max_clusters_m(int csize) {
-  static int cache[64][9];
+  static std::atomic<int> cache[64][9];  // 0: not asked yet (racing threads ask twice)
   int dev = 0;
   cudaGetDevice(&dev);
-  int& mc = cache[dev & 63][csize];
-  if (mc == 0) {
+  std::atomic<int>& mc = cache[dev & 63][csize];
+  if (mc.load() == 0) {
     int n = 0;
     if (configure_m<M>() == ORT_CUDA_OK) {
       cudaLaunchConfig_t qc = {};

@@ -7,8 +7,10 @@ under a profiler with few launches before the one captured.
 
 Weights are seeded random int4 (fp16 scales, packed zero points), as in the
 benchmark; the first `--warmup` launches are untimed, then `--reps` launches
-run back to back between two events.  The session's error word is read
-after the timed launches, so an expired in-kernel wait fails the run.
+run back to back between two events (recorded as one CUDA graph with
+`--graph`, so that the host's per-call cost stays out of the time).  The
+session's error word is read after the timed launches, so an expired
+in-kernel wait fails the run.
 """
 from __future__ import annotations
 
@@ -28,6 +30,9 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--graph", action="store_true",
+                    help="record the timed launches as one CUDA graph and replay it once "
+                         "(device time without the host's per-call cost)")
     ap.add_argument("--plan", type=int, default=None,
                     help="decode-GEMV plan to use (ort_cuda_gemv_plan_set) instead of timing "
                          "the candidates on the first call; M <= 8 in the exact mode")
@@ -56,12 +61,25 @@ def main(argv=None) -> None:
             for _ in range(args.warmup):
                 s.matmul_nbits("w", a, out=y, flags=flags)
             st.synchronize()
+            gid = None
+            if args.graph:
+                s.graph_begin()
+                for _ in range(args.reps):
+                    s.matmul_nbits("w", a, out=y, flags=flags)
+                gid = s.graph_end()
+                s.graph_launch(gid)  # warm replay
+                st.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
-            for _ in range(args.reps):
-                s.matmul_nbits("w", a, out=y, flags=flags)
+            if gid is not None:
+                s.graph_launch(gid)
+            else:
+                for _ in range(args.reps):
+                    s.matmul_nbits("w", a, out=y, flags=flags)
             e1.record(st)
             st.synchronize()
+            if gid is not None:
+                s.graph_drop(gid)
         s.sync()
         us = e0.elapsed_time(e1) * 1000 / args.reps
         plan = s.gemv_plan("w", args.m) if args.mode == "exact" and args.m <= 8 else None

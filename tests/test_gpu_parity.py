@@ -461,7 +461,8 @@ def test_opcase_single_op_timer(capsys):
     import json
     from onnx_runtime_dart_b200 import opcase
     for argv in (["--k", "1024", "--n", "2048", "--m", "1"],
-                 ["--k", "1024", "--n", "1024", "--m", "256", "--mode", "mma_f16"]):
+                 ["--k", "1024", "--n", "1024", "--m", "256", "--mode", "mma_f16"],
+                 ["--k", "1024", "--n", "2048", "--m", "1", "--graph"]):
         opcase.main(argv + ["--reps", "2", "--warmup", "1"])
         line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
         assert line["us_per_launch"] > 0 and line["m"] == int(argv[5])
