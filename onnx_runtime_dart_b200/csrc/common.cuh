@@ -548,7 +548,8 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
 int launch_nbits_gemm_f16(Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
-                          int reserve_sms = 0, const PrefillPush* push = nullptr);
+                          int reserve_sms = 0, const PrefillPush* push = nullptr,
+                          const YSel* seg = nullptr);
 // N-sharded prefill, push mode of the fused fp16 GEMM: besides its own
 // columns in Y, every output row slice [row][0, nl) is stored into each
 // peer's landing area land[r] (this rank's block of it, [M][Ns] floats);
@@ -563,9 +564,11 @@ struct PrefillPush {
   int rank = 0, world = 0;
 };
 // reserve_sms: SMs the fused fp16 GEMM leaves free for a kernel beside it
+// seg: the segmented output of a fused group (YSel's seg_* fields; the
+// fused fp16 GEMM only, boundaries multiples of 32)
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
                      int64_t ldy, int mode, cudaStream_t st, int reserve_sms = 0,
-                     const PrefillPush* push = nullptr);
+                     const PrefillPush* push = nullptr, const YSel* seg = nullptr);
 
 int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, bool transA,
                      float* Y, int64_t ldy, int mode, float alpha, float beta, const float* C,

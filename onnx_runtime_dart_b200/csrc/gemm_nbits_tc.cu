@@ -75,6 +75,13 @@ struct PParams {
   int bs_shift;  // log2(block size)
   uint32_t stage_tx;
   PrefillPush push;  // world == 0: no peers
+  // a fused group's parts (nseg > 0): columns [seg_start[j], seg_start[j+1])
+  // go to seg_y[j] with row pitch seg_ld[j]; every boundary is a multiple of
+  // 32, so one 32-column chunk of the epilogue stays within one part
+  int nseg = 0;
+  int64_t seg_start[kMaxSegs + 1] = {};
+  float* seg_y[kMaxSegs] = {};
+  int64_t seg_ld[kMaxSegs] = {};
 };
 
 __device__ __forceinline__ float pow2f(int e) {
@@ -245,16 +252,23 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         // column n at n*32 + ((h ^ bit 2 of n) << 4)): the 8 columns a
         // quarter-warp reads then cover all 32 banks once
         const uint32_t qa = smem_u32(st + kABytes) + n * 32;
-        const uint32_t* sz = reinterpret_cast<const uint32_t*>(st + kABytes + kQBytes);
+        const uint32_t sza = smem_u32(st + kABytes + kQBytes);  // the stage's table
         const uint32_t qsw = (uint32_t)((n >> 2) & 1) << 4;
         const uint4 w4 = lds128(qa + ((uint32_t)(hw << 4) ^ qsw));
         const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
         const uint32_t cb = smem_u32(conv + c * kCBytes) + rowoff;
+        // word i holds k 8i..8i+7; the {1024 + z, scale} entry of its block
+        // within the stage's table, all four loads issued before any use
+        uint32_t vs[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          asm volatile("ld.shared.u32 %0, [%1];"
+                       : "=r"(vs[j])
+                       : "r"(sza + (uint32_t)((((8 * (4 * hw + j)) >> p.bs_shift) * PBN + n) * 4)));
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          // word i holds k 8i..8i+7; its block within the stage's table
           const int i = 4 * hw + j;
-          const uint32_t v = sz[((8 * i) >> p.bs_shift) * PBN + n];
+          const uint32_t v = vs[j];
           const uint32_t zz = prmt(v, v, 0x1010), sc = prmt(v, v, 0x3232);
           const uint32_t lo = words[j] & 0x0F0F0F0Fu, hi = (words[j] >> 4) & 0x0F0F0F0Fu;
           const uint32_t r0 = deq2(prmt(lo, 0x64646464u, 0x4140), zz, sc);  // k0, k1
@@ -295,13 +309,26 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         __syncwarp();
         const int n = n0 + c0 + lane;
         const int f = n < p.N ? p.col_exp[n] : 0;
+        // the chunk's destination: Y, or the part of a fused group it lies in
+        float* yb = p.Y;
+        int64_t ld = p.ldy, cs = 0;
+        if (p.nseg) {
+          const int nc = n0 + c0;
+#pragma unroll
+          for (int t = 0; t < kMaxSegs; t++)
+            if (t < p.nseg && nc >= p.seg_start[t]) {
+              yb = p.seg_y[t];
+              ld = p.seg_ld[t];
+              cs = p.seg_start[t];
+            }
+        }
 #pragma unroll 4
         for (int j = 0; j < 32; j++) {
           const int e = __shfl_sync(0xffffffffu, my_e, j);
           const int row = rbase + j;
           if (row < p.M && n < p.N) {
             const float v = scale_pow2(buf[j * 33 + lane], e + f);
-            p.Y[(int64_t)row * p.ldy + n] = v;
+            yb[(int64_t)row * ld + (n - cs)] = v;
             if constexpr (PUSH) {  // the same value into every peer's landing block
 #pragma unroll
               for (int r = 0; r < 8; r++)
@@ -380,7 +407,7 @@ int prepare_nbits_sz16(const Weight& w, const int* col_exp, uint32_t* out, cudaS
 int launch_nbits_gemm_f16(Weight& w, const uint16_t* A16, const int* row_exp, int64_t M,
                           const uint32_t* sz16, const int* col_exp, float* Y, int64_t ldy,
                           int* err, int sm_count, cudaStream_t st, int64_t* launches,
-                          int reserve_sms, const PrefillPush* push) {
+                          int reserve_sms, const PrefillPush* push, const YSel* seg) {
   if (M == 0 || w.nl == 0) return ORT_CUDA_OK;
   const int64_t K = w.K, nl = w.nl, col_bytes = (int64_t)w.nb * w.bs / 2;
   CUtensorMap tmA;
@@ -417,6 +444,14 @@ int launch_nbits_gemm_f16(Weight& w, const uint16_t* A16, const int* row_exp, in
   p.bs_shift = bs_shift;
   p.stage_tx = kABytes + kQBytes + (uint32_t)bps * PBN * 4;
   if (push) p.push = *push;
+  if (seg && seg->nseg > 0) {
+    p.nseg = seg->nseg;
+    for (int j = 0; j <= seg->nseg; j++) p.seg_start[j] = seg->seg_start[j];
+    for (int j = 0; j < seg->nseg; j++) {
+      p.seg_y[j] = seg->seg_y[j];
+      p.seg_ld[j] = seg->seg_ld[j];
+    }
+  }
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaGetDevice(&dev);

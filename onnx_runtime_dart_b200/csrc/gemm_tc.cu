@@ -507,7 +507,7 @@ int launch_mma_dense(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
 
 int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, float* Y,
                      int64_t ldy, int mode, cudaStream_t st, int reserve_sms,
-                     const PrefillPush* push) {
+                     const PrefillPush* push, const YSel* seg) {
   if (w.nl == 0 || M == 0) return ORT_CUDA_OK;
   const bool bf16 = mode == ORT_CUDA_MODE_MMA_BF16;
   const int64_t K = w.K, nl = w.nl;
@@ -535,9 +535,10 @@ int launch_mma_nbits(ort_cuda_session* s, Weight& w, const float* A, int64_t M, 
     rc = convert_a(s, A, M, K, false, false, 0, &A16, &rexp, st);
     if (rc) return rc;
     return launch_nbits_gemm_f16(w, A16, rexp, M, w.sz16, w.col_exp, Y, ldy, s->err_dev,
-                                 s->sm_count, st, &s->launches, reserve_sms, push);
+                                 s->sm_count, st, &s->launches, reserve_sms, push, seg);
   }
-  ORTC_CHECK(push == nullptr, ORT_CUDA_ERR_INVALID_ARG, "push mode needs the fused fp16 GEMM");
+  ORTC_CHECK(push == nullptr && (seg == nullptr || seg->nseg == 0), ORT_CUDA_ERR_INVALID_ARG,
+             "push mode and segmented output need the fused fp16 GEMM");
   const size_t a_bytes = a_scratch_bytes(M, K, bf16);
   const size_t w_bytes = al256((size_t)(nl * K) * 2 * (bf16 ? 2 : 1));
   const size_t e_bytes = al256((size_t)nl * 4);

@@ -2065,6 +2065,11 @@ ORT_CUDA_API int ort_cuda_matmul_nbits_group(ort_cuda_session* s, const char* fu
   for (int m = 8; m >= 1 && !cmax; m--)
     if (tc_gemv_ok(w, m)) cmax = m;
   const bool gemv = mode != ORT_CUDA_MODE_STRICT && cmax > 0 && M <= 8 * cmax;
+  // prefill-sized: the fused fp16 GEMM writes each part's columns into its
+  // own buffer when the part boundaries are multiples of 32
+  bool seg_ok = !gemv && !host && mode == ORT_CUDA_MODE_MMA_F16 && nbits_gemm_f16_ok(w) &&
+                mma_supported_shape(M, w.K);
+  for (int i = 1; i < w.nparts; i++) seg_ok = seg_ok && w.part_col[i] % 32 == 0;
   // device views: staged A / outputs for host buffers, one [M, N] scratch
   // when the op runs whole and is split afterwards
   const size_t ab = (size_t)(M * w.K) * 4, yb = (size_t)(M * w.N) * 4;
@@ -2072,7 +2077,7 @@ ORT_CUDA_API int ort_cuda_matmul_nbits_group(ort_cuda_session* s, const char* fu
   const size_t a_off = off;
   if (host) off += al256(ab);
   const size_t y_off = off;
-  if (host || !gemv) off += al256(yb);
+  if (host || (!gemv && !seg_ok)) off += al256(yb);
   int rc = off ? ensure_aux(s, off) : ORT_CUDA_OK;
   if (rc) return rc;
   char* aux = static_cast<char*>(s->aux);
@@ -2101,6 +2106,17 @@ ORT_CUDA_API int ort_cuda_matmul_nbits_group(ort_cuda_session* s, const char* fu
       if (rc) return rc;
     }
   } else {
+    if (seg_ok) {
+      YSel ys;
+      ys.nseg = w.nparts;
+      for (int i = 0; i < w.nparts; i++) {
+        ys.seg_start[i] = w.part_col[i];
+        ys.seg_y[i] = Ys[i];
+        ys.seg_ld[i] = w.part_col[i + 1] - w.part_col[i];
+      }
+      ys.seg_start[w.nparts] = w.N;
+      return launch_mma_nbits(s, w, dA, M, nullptr, w.N, mode, s->stream, 0, nullptr, &ys);
+    }
     const int mflags = flags & (ORT_CUDA_MODE_OVERRIDE | 0xF000);
     rc = ort_cuda_matmul_nbits(s, fused, dA, M, scratch, mflags);
     if (rc) return rc;
