@@ -13,9 +13,15 @@
 // upload layout; no 16-bit copy of the weights is written to HBM.
 //
 // Persistent kernel, one CTA per SM, tiles of 256 (m) x 128 (n), 64-k stages.
-// The converted weight tile is the expensive operand (the converter warps
-// bound the kernel), so each one serves 256 rows of A: two M=128 MMAs per
-// 16-k step share it.
+// The converted weight tile is the expensive operand, so each one serves 256
+// rows of A.  The MMA takes it as its A operand (M = 128 weight columns)
+// and the activation tile as B (N = 256 rows): one M=128, N=256 MMA per
+// 16-k step reads 12 KB of shared memory, where two M=128, N=128 MMAs
+// sharing the weight tile as B read 16 KB; shared-memory bandwidth, which
+// the MMAs share with the TMA writes and the converters, is what bounds the
+// kernel.  D is then transposed (TMEM lane = weight column, TMEM column =
+// activation row), so a warp's epilogue stores for one row are 32
+// consecutive columns: coalesced with no shared-memory transpose.
 //   warp 0      TMA producer: A tile (256 x 64 fp16, 128-byte swizzle), the
 //               packed int4 tile (128 columns x 32 bytes, 32-byte swizzle)
 //               and the stage's {1024 + z, scale'} table (fp16 pairs) into a
@@ -25,15 +31,15 @@
 //               masks, four byte permutes (nibble | 0x6400 is the fp16 value
 //               1024 + q), four exact subtractions of 1024 + z and four
 //               multiplies by the scale (one rounding), stored as the MMA's
-//               K-major 128-byte-swizzled B tile
-//   warp 1      allocates 512 TMEM columns (two accumulators, each two
-//               128 x 128 fp32 halves); an elect.sync leader waits once per
-//               stage and issues 8 MMAs (M=128, N=128, K=16: both halves of
-//               A against the same B), tcgen05.commit frees the stage and
-//               the converted tile
+//               K-major 128-byte-swizzled A tile
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32
+//               accumulators); an elect.sync leader waits once per stage and
+//               issues 4 MMAs (M=128, N=256, K=16), tcgen05.commit frees the
+//               stage and the converted tile
 //   warps 10-13 epilogue: tcgen05.ld of the finished accumulator while the
-//               MMAs fill the other one, exact 2^(e_m + f_n) scaling, and
-//               coalesced stores through a per-warp shared-memory transpose
+//               MMAs fill the other one (warp q owns weight columns
+//               32q .. 32q + 31 of the tile), exact 2^(e_m + f_n) scaling,
+//               one coalesced 128-byte store per row and warp
 // Every wait is bounded; on expiry the kernel records an error and returns.
 #include <cuda_fp16.h>
 
@@ -51,17 +57,15 @@ namespace {
 constexpr int PBM = 256, PBN = 128, PBK = 64;
 constexpr int kHalf = 128;                           // rows of one MMA (M)
 constexpr int kRaw = 4;                              // producer ring depth
-constexpr int kConv = 3;                             // converted B tiles
+constexpr int kConv = 4;                             // converted weight tiles
 constexpr uint32_t kABytes = PBM * PBK * 2;          // 32 KB fp16 A tile
 constexpr uint32_t kQBytes = PBN * PBK / 2;          // 4 KB packed int4 tile
 constexpr uint32_t kSZBytes = PBN * 4 * 4;           // up to 4 blocks per stage
 constexpr uint32_t kRawBytes = kABytes + kQBytes + kSZBytes;  // 38 KB
-constexpr uint32_t kCBytes = PBN * PBK * 2;          // 16 KB fp16 B tile
+constexpr uint32_t kCBytes = PBN * PBK * 2;          // 16 KB fp16 weight tile
 constexpr int kConvWarp0 = 2, kConvWarps = 8, kEpiWarp0 = 10;
 constexpr int kThreadsP = 14 * 32;
-constexpr uint32_t kEpiFloats = 32 * 33;             // per epilogue warp
-constexpr size_t kSmemP =
-    1024 + kRaw * kRawBytes + kConv * kCBytes + 4 * kEpiFloats * 4 + 256;
+constexpr size_t kSmemP = 1024 + kRaw * kRawBytes + kConv * kCBytes + 256;
 
 struct PParams {
   float* Y;
@@ -120,8 +124,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                                              ~uintptr_t(1023));
   uint8_t* raw = smem;
   uint8_t* conv = smem + kRaw * kRawBytes;
-  float* epi = reinterpret_cast<float*>(conv + kConv * kCBytes);
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(epi + 4 * kEpiFloats);
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(conv + kConv * kCBytes);
   uint64_t* raw_empty = raw_full + kRaw;
   uint64_t* conv_full = raw_empty + kRaw;
   uint64_t* conv_empty = conv_full + kConv;
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_f16(0, kHalf, PBN);
+      constexpr uint32_t idesc = idesc_f16(0, kHalf, PBM);
       uint32_t g = 0, tcount = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, tcount++) {
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t dt = tmem + d * (2 * PBN);  // halves at + 0 and + PBN
+        const uint32_t dt = tmem + d * PBM;  // 256 columns: one per row of the A tile
         for (int kb = 0; kb < nk; kb++, g++) {
           const int s = g % kRaw, c = g % kConv;
           if (!mbar_wait(&conv_full[c], (g / kConv) & 1)) {
@@ -216,11 +219,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const uint32_t sa = smem_u32(raw + s * kRawBytes);
           const uint32_t sb = smem_u32(conv + c * kCBytes);
 #pragma unroll
-          for (int kk = 0; kk < PBK / 16; kk++)
-#pragma unroll
-            for (int h = 0; h < 2; h++)  // rows 128h .. 128h + 127 of A: 16 KB apart
-              mma_f16_ss(dt + h * PBN, smem_desc_sw128(sa + h * (kABytes / 2) + kk * 32),
-                         smem_desc_sw128(sb + kk * 32), idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < PBK / 16; kk++)  // D[n, m] += W16[n, k] . A16[m, k]
+            mma_f16_ss(dt, smem_desc_sw128(sb + kk * 32), smem_desc_sw128(sa + kk * 32), idesc,
+                       (kb | kk) != 0);
           mma_commit(&raw_empty[s]);
           mma_commit(&conv_empty[c]);
         }
@@ -286,58 +287,54 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
   } else {
     // ---------------- epilogue ---------------------------------------------
+    // warp q reads TMEM lanes 32q .. 32q + 31: weight columns n0 + 32q + lane
     const int q = warp & 3;
-    float* buf = epi + (warp - kEpiWarp0) * kEpiFloats;
     uint32_t tcount = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, tcount++) {
       const int m0 = (t % p.m_tiles) * PBM, n0 = (t / p.m_tiles) * PBN;
       const int d = tcount & 1;
+      const int n = n0 + q * 32 + lane;
+      const int f = n < p.N ? p.col_exp[n] : 0;
+      // the warp's destination: Y, or the part of a fused group its 32
+      // columns lie in
+      float* yb = p.Y;
+      int64_t ld = p.ldy, cs = 0;
+      if (p.nseg) {
+        const int nc = n0 + q * 32;
+#pragma unroll
+        for (int u = 0; u < kMaxSegs; u++)
+          if (u < p.nseg && nc >= p.seg_start[u]) {
+            yb = p.seg_y[u];
+            ld = p.seg_ld[u];
+            cs = p.seg_start[u];
+          }
+      }
       if (!mbar_wait(&tm_full[d], (tcount >> 1) & 1)) {
         record_error(p.err, KERR_WAIT_MMA);
         break;
       }
       tc_fence_after();
-      for (int h = 0; h < 2; h++)
-      for (int c0 = 0; c0 < PBN; c0 += 32) {
-        const int rbase = m0 + h * kHalf + q * 32;
+      for (int c0 = 0; c0 < PBM; c0 += 32) {
+        const int rbase = m0 + c0;
         const int my_e = rbase + lane < p.M ? p.row_exp[rbase + lane] : 0;
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + d * (2 * PBN) + h * PBN + c0, r);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + d * PBM + c0, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; j++) buf[lane * 33 + j] = __uint_as_float(r[j]);
-        __syncwarp();
-        const int n = n0 + c0 + lane;
-        const int f = n < p.N ? p.col_exp[n] : 0;
-        // the chunk's destination: Y, or the part of a fused group it lies in
-        float* yb = p.Y;
-        int64_t ld = p.ldy, cs = 0;
-        if (p.nseg) {
-          const int nc = n0 + c0;
-#pragma unroll
-          for (int t = 0; t < kMaxSegs; t++)
-            if (t < p.nseg && nc >= p.seg_start[t]) {
-              yb = p.seg_y[t];
-              ld = p.seg_ld[t];
-              cs = p.seg_start[t];
-            }
-        }
-#pragma unroll 4
         for (int j = 0; j < 32; j++) {
           const int e = __shfl_sync(0xffffffffu, my_e, j);
           const int row = rbase + j;
           if (row < p.M && n < p.N) {
-            const float v = scale_pow2(buf[j * 33 + lane], e + f);
+            const float v = scale_pow2(__uint_as_float(r[j]), e + f);
             yb[(int64_t)row * ld + (n - cs)] = v;
             if constexpr (PUSH) {  // the same value into every peer's landing block
 #pragma unroll
-              for (int r = 0; r < 8; r++)
-                if (r < p.push.world && r != p.push.rank)
-                  p.push.land[r][(int64_t)row * p.push.ns + n] = v;
+              for (int u = 0; u < 8; u++)
+                if (u < p.push.world && u != p.push.rank)
+                  p.push.land[u][(int64_t)row * p.push.ns + n] = v;
             }
           }
         }
-        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
