@@ -177,14 +177,6 @@ __device__ __forceinline__ float scale_pow2(float v, int e) {
   return v * pow2f(e);
 }
 
-// (float)d for the int32 bits of an accumulator with |d| < 2^22, exactly:
-// 1.5 * 2^23 + d is a float of exponent 23 whose mantissa holds d, so one
-// integer add and one float subtract replace the quarter-rate conversion.
-// Every D column qualifies: |d| <= bs * 15 * 128 <= 2^20 for bs <= 512.
-__device__ __forceinline__ float i22_to_f(uint32_t d) {
-  return __uint_as_float(d + 0x4B400000u) - 12582912.0f;
-}
-
 // X (int8, K-major, 128-byte swizzle): 128-k atoms of NM rows x 128 bytes,
 // 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint32_t x_addr(uint32_t base, int nm, int j, int k) {
@@ -421,12 +413,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // ---------------- X builder (tile-major) ----------------
     // One warp builds X, the row exponents and the blocks' sums of X for
     // chunk c + 1 as soon as its buffer is free, while the dequantisers
-    // stream chunk c.  (Split-K CTAs build their single chunk once, on the
-    // critical path after the first items are in TMEM: the dequantiser
-    // warps do that together, below.)  Unit i (< 4M) of a lane is 4
-    // consecutive k of row i / 4 at k = 4 (lane + 32 (i % 4)); for M <= 2
-    // the next chunk's units are loaded right after a build, so a build
-    // does not wait for them.
+    // stream chunk c.  (Split-K CTAs build their single chunk once, at the
+    // start and on the critical path: the dequantiser warps do that
+    // together, below.)  Unit i (< 4M) of a lane is 4 consecutive k of row
+    // i / 4 at k = 4 (lane + 32 (i % 4)); for M <= 2 the next chunk's units
+    // are loaded right after a build, so a build does not wait for them.
     for (int i = lane; i < 2 * (int)kXBufBytes / 16; i += 32)
       asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16), "r"(0u)
                    : "memory");
@@ -591,22 +582,16 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int nl = q * 32 + lane;  // column within the tile = TMEM lane
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     bool ok = true;
-    uint32_t xph = 0;
     if (!p.tile_major) {
-      // split-K: the CTA's one chunk of X (digit sums, row exponents), built
-      // by all 8 warps; zero both buffers first
+      // the CTA's one chunk: X, digit sums, row exponents, all 8 warps
       for (int i = threadIdx.x; i < 2 * (int)kXBufBytes / 16; i += kDeWarps * 32)
         asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(smem_u32(Xs) + i * 16),
                      "r"(0u)
                      : "memory");
+      uint32_t xph = 0;
       ok = warp_group_sync(xsync, xph, p.err);
       // parameters of the build, read before the dependency wait
       asm volatile("" ::"l"(p.A), "r"(p.K), "r"(p.a_vec), "r"(p.bs_log2), "r"(p.bs), "r"(p.bpi));
-    }
-    // Split-K builds X once the first items' weights are in TMEM: those do
-    // not depend on the previous kernel, so they are dequantised while it
-    // finishes, and only X waits for its completion.
-    auto build_x = [&]() {
       griddep_wait();  // activations come from the previous kernel in the stream
       constexpr int kU = kChunkK / 4;  // 4-k units per row
       constexpr int kPer = (M * kU + kDeWarps * 32 - 1) / (kDeWarps * 32);
@@ -686,8 +671,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&xfull[xbuf]);
       }
-    };
-    bool x_built = p.tile_major != 0;  // tile-major: the X warp builds
+    }
     int j = 0;
     for_each_item(p, [&](int, int, int) {
       if (!ok) return false;
@@ -723,13 +707,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bempty[bst]);
       j++;
-      if (!x_built && j == kAItems) {  // the TMEM A ring is full
-        build_x();
-        x_built = true;
-      }
       return true;
     });
-    if (!x_built) build_x();  // fewer items than the ring holds, or an error
   } else if (warp < kEpiWarp0 + kEpiWarps) {
     // ---------------- epilogue ----------------
     // Two groups share the items.  Tile-major without a cluster: a tile's
@@ -809,14 +788,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int b = rg * G + slot;
           if (b < p.bpi) {
             const float sc = p.s16 ? __half2float(stile16[b * kTile + nl]) : stile[b * kTile + nl];
-            const float zf = i22_to_f((uint32_t)(zbits >> (4 * b + zsh)) & 0xFu);
+            const float zf = (float)((uint32_t)(zbits >> (4 * b + zsh)) & 0xFu);
 #pragma unroll
             for (int m = 0; m < M; m++) {
               // D_t = sum q * c_t over the block (exact int32); the block's
               // sum (q - z) * X is D - z * sum X
               const int c = (slot * M + m) * 3;
-              const float dq = (i22_to_f(v[c + 2]) * 65536.0f + i22_to_f(v[c + 1]) * 256.0f) +
-                               i22_to_f(v[c]);
+              const float dq = ((float)(int)v[c + 2] * 65536.0f + (float)(int)v[c + 1] * 256.0f) +
+                               (float)(int)v[c];
               y[m] = fmaf(sc, fmaf(-zf, xsum[b * M + m], dq), y[m]);
             }
           }
@@ -1069,7 +1048,7 @@ int max_clusters(int64_t M, int csize) {
 // choice before that: the busiest CTA's cost in items, where a chunk of T
 // tiles costs max(T, 1.5) (the builder warp takes about 1.5 items' time
 // for a chunk's X and hides it only behind that chunk's items) and split-K
-// pays about three items for its X build and its sum; ties go to more
+// pays about three items for the boundary before its sum; ties go to more
 // CTAs, then to the earlier candidate.
 struct Plan {
   bool tile_major;
