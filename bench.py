@@ -921,7 +921,12 @@ def sharded_parity(sess, projs, weights, rank, dev, barrier):
             bit.setdefault(M, True)
             bit[M] = bit[M] and same
         one.close()
+        # which weights this rank keeps whole (size-based placement) and which
+        # it shards
+        place = {p.name: ("replicated" if sess.weight_columns(p.name) == (0, p.N) else "sharded")
+                 for p in projs}
         out = {"ops": len(projs), "reference": "single-GPU session of the same weights on rank 0",
+               "placement": place,
                "bitwise_m1": bit[1], "bitwise_m16": bit[16],
                "prefill_bitwise": bit[PREFILL_M], "prefill_max_rel": rel,
                "prefill_mode": "mma_f16"}

@@ -126,6 +126,24 @@ ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void*
  * detected this way, without any unbounded wait on the device). */
 ORT_CUDA_API int ort_cuda_set_peer_wait(ort_cuda_session* s, int ms);
 
+/* Size-based placement on an N-sharded session.  A MatMulNBits weight
+ * uploaded after this call whose packed bytes (B, scales and zero points) are
+ * at most `bytes` is kept whole on every rank and computed there without any
+ * exchange of Y; larger weights keep their column shard.  Sharding saves
+ * (1 - 1/world) of a weight's stream time but adds the exchange of its
+ * output, a few microseconds per decode op whatever its size.  -1 (the
+ * default) means 30 MB x world / (world - 1), where the two balance; 0 shards
+ * every weight.  The environment variable ORT_CUDA_REPLICATE_BYTES sets it at
+ * ort_cuda_open_rank.  Every rank must use the same value.  Results are the
+ * single-GPU results either way. */
+ORT_CUDA_API int ort_cuda_set_replicate_bytes(ort_cuda_session* s, int64_t bytes);
+
+/* The columns [*n0, *n0 + *nl) of weight `name` held and computed by this
+ * rank: its shard, or 0 and N for a replicated weight or a single-GPU
+ * session. */
+ORT_CUDA_API int ort_cuda_weight_columns(ort_cuda_session* s, const char* name, int64_t* n0,
+                                         int64_t* nl);
+
 /* Frees every device buffer of the session (OnnxModel.dispose,
  * lib/onnx_runtime_dart.dart:140). */
 ORT_CUDA_API int ort_cuda_close(ort_cuda_session* s);

@@ -115,6 +115,8 @@ SIGNATURES = {
     "ort_cuda_probe_ffma": (_int, [_vp, ctypes.POINTER(ctypes.c_double)]),
     "ort_cuda_matmul_nbits_argmax": (_int, [_vp, _cp, _vp, _i64, _vp, _vp, _int]),
     "ort_cuda_set_peer_wait": (_int, [_vp, _int]),
+    "ort_cuda_set_replicate_bytes": (_int, [_vp, _i64]),
+    "ort_cuda_weight_columns": (_int, [_vp, _cp, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
     "ort_cuda_fuse_nbits": (_int, [_vp, _cp, ctypes.POINTER(_cp), _int, _int]),
     "ort_cuda_matmul_nbits_group": (_int, [_vp, _cp, _vp, _i64, ctypes.POINTER(_vp), _int]),
 }

@@ -80,6 +80,9 @@ struct Weight {
   CUtensorMap tmW8;
   // decode GEMV: the plan (candidate index) timing chose for each M in 1..8
   int8_t gemv_plan[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
+  // N-sharded session, size-based placement: the whole weight on every rank
+  // (n0 = 0, nl = ns = N), computed locally with no exchange
+  bool replicated = false;
   // a fused group (ort_cuda_fuse_nbits): the parts' names and first columns
   // (part_col[i] .. part_col[i + 1]); on an N-sharded session only the names
   // are kept (no fused copy) and the group call runs the parts in turn
@@ -186,6 +189,9 @@ struct ort_cuda_session {
   unsigned long long bepoch = 0;
   // bound of every wait for a peer GPU's flag or data (ms)
   int peer_wait_ms = 1000;
+  // MatMulNBits weights of at most this many bytes are replicated on every
+  // rank of an N-sharded session (-1: 30 MB x world / (world - 1))
+  int64_t replicate_bytes = -1;
   // CUDA graphs captured from the session stream (ort_cuda_graph_*)
   struct Graph {
     cudaGraphExec_t exec;

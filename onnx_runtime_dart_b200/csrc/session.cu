@@ -158,6 +158,21 @@ void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_
   *ns = per;
 }
 
+// Size-based placement on an N-sharded session.  Sharding a weight saves
+// (1 - 1/G) of its stream time but adds the exchange of its output (about
+// 4-5 us for a decode op, whatever its size), so a MatMulNBits weight whose
+// packed bytes stay below replicate_bytes (by default 30 MB x G / (G - 1),
+// where the two balance at 6.4 TB/s) is kept whole on every rank and
+// computed locally; its results are the 1-GPU results.  The decision
+// depends on the shape and the session setting only, so every rank makes it
+// alike (ORT_CUDA_REPLICATE_BYTES must be equal on all ranks).
+bool replicate_nbits(const ort_cuda_session* s, int64_t bytes) {
+  if (s->world <= 1) return false;
+  const int64_t lim =
+      s->replicate_bytes >= 0 ? s->replicate_bytes : (int64_t)30000000 * s->world / (s->world - 1);
+  return bytes <= lim;
+}
+
 // A kernel whose bounded wait gave up wrote a code into the host-mapped
 // error word; report it once.
 }  // namespace
@@ -380,6 +395,8 @@ ORT_CUDA_API int ort_cuda_open_rank(int device, int rank, int world, const void*
   s->rank = rank;
   s->world = world;
   s->timeout_ms = timeout_ms;
+  if (const char* env = std::getenv("ORT_CUDA_REPLICATE_BYTES"))
+    s->replicate_bytes = std::strtoll(env, nullptr, 10);
   if (world == 1) return ORT_CUDA_OK;
   ncclUniqueId id;
   std::memcpy(&id, nccl_id128, 128);
@@ -474,6 +491,25 @@ ORT_CUDA_API int ort_cuda_set_peer_wait(ort_cuda_session* s, int ms) {
   ORTC_CHECK(ms >= 1 && ms <= 600000, ORT_CUDA_ERR_INVALID_ARG,
              "peer wait must be 1 .. 600000 ms");
   s->peer_wait_ms = ms;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_set_replicate_bytes(ort_cuda_session* s, int64_t bytes) {
+  ORTC_CHECK(s, ORT_CUDA_ERR_INVALID_ARG, "session is NULL");
+  ORTC_CHECK(bytes >= -1, ORT_CUDA_ERR_INVALID_ARG, "replicate bytes must be >= -1");
+  s->replicate_bytes = bytes;
+  return ORT_CUDA_OK;
+}
+
+ORT_CUDA_API int ort_cuda_weight_columns(ort_cuda_session* s, const char* name, int64_t* n0,
+                                         int64_t* nl) {
+  ORTC_CHECK(s && name && n0 && nl, ORT_CUDA_ERR_INVALID_ARG, "NULL argument");
+  auto it = s->weights.find(name);
+  ORTC_CHECK(it != s->weights.end(), ORT_CUDA_ERR_NOT_FOUND,
+             std::string("no weight named '") + name + "'");
+  const Weight& w = it->second;
+  *n0 = w.group_only ? 0 : w.n0;
+  *nl = w.group_only ? 0 : w.nl;
   return ORT_CUDA_OK;
 }
 
@@ -572,10 +608,17 @@ int upload_nbits_impl(ort_cuda_session* s, const char* name, const BSource& Bsrc
   w.N = N;
   w.bs = block_size;
   w.nb = (int)nb;
-  shard_cols(N, s->rank, s->world, &w.n0, &w.nl, &w.ns);
   w.has_zp = zp != nullptr;
-  const int64_t nl = w.nl;
   const bool f16 = (flags & ORT_CUDA_SCALES_F16) != 0;
+  w.replicated = replicate_nbits(
+      s, N * col_bytes + N * nb * (f16 ? 2 : 4) + (w.has_zp ? N * ((nb + 1) / 2) : 0));
+  if (w.replicated) {
+    w.n0 = 0;
+    w.nl = w.ns = N;
+  } else {
+    shard_cols(N, s->rank, s->world, &w.n0, &w.nl, &w.ns);
+  }
+  const int64_t nl = w.nl;
   auto cleanup = [&](int rc) {
     free_weight(w);
     return rc;
@@ -1619,7 +1662,7 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
   const int64_t N = w.N;
-  const bool sharded = s->world > 1;
+  const bool sharded = s->world > 1 && !w.replicated;
   WsLayout L;
   size_t off = 0;
   if (host) {
@@ -1841,7 +1884,7 @@ int nbits_argmax_dev(ort_cuda_session* s, Weight& w, const char* name, const flo
   int cmax = 0;
   for (int m = 8; m >= 1 && !cmax; m--)
     if (tc_gemv_ok(w, m)) cmax = m;
-  const bool fused = s->world == 1 && mode != ORT_CUDA_MODE_STRICT && cmax > 0 &&
+  const bool fused = (s->world == 1 || w.replicated) && mode != ORT_CUDA_MODE_STRICT && cmax > 0 &&
                      M <= 8 * cmax && M <= kAmaxRows && w.N < (int64_t)UINT32_MAX;
   if (!fused) {
     // the same result from the two separate operations
@@ -1962,7 +2005,10 @@ ORT_CUDA_API int ort_cuda_fuse_nbits(ort_cuda_session* s, const char* fused,
   }
   w.part_col[n] = N;
   w.N = N;
-  if (s->world > 1) {
+  bool all_replicated = true;
+  for (Weight* p : parts) all_replicated = all_replicated && p->replicated;
+  w.replicated = s->world > 1 && all_replicated;
+  if (s->world > 1 && !all_replicated) {
     // sharded: each part keeps its own shards and exchange; the group call
     // runs them in turn
     w.kind = W_GROUP;

@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Dict, List, Optional, Sequence, Union
+from typing import Dict, List, Optional, Sequence, Tuple, Union
 
 import numpy as np
 
@@ -164,6 +164,20 @@ class CudaSession:
     def set_peer_wait(self, ms: int) -> None:
         """Bound of every wait for a peer GPU in the exchange of Y (ms)."""
         check(_lib.load().ort_cuda_set_peer_wait(self.handle, int(ms)), "ort_cuda_set_peer_wait")
+
+    def set_replicate_bytes(self, nbytes: int) -> None:
+        """MatMulNBits weights of at most nbytes packed bytes uploaded from now
+        on are kept whole on every rank (no exchange); -1: the default
+        30 MB x world / (world - 1), 0: shard every weight."""
+        check(_lib.load().ort_cuda_set_replicate_bytes(self.handle, int(nbytes)),
+              "ort_cuda_set_replicate_bytes")
+
+    def weight_columns(self, name: str) -> Tuple[int, int]:
+        """(n0, nl): the columns of `name` this rank holds and computes."""
+        n0, nl = ctypes.c_int64(), ctypes.c_int64()
+        check(_lib.load().ort_cuda_weight_columns(self.handle, name.encode(), ctypes.byref(n0),
+                                                  ctypes.byref(nl)), "ort_cuda_weight_columns")
+        return n0.value, nl.value
 
     def sync(self) -> None:
         check(_lib.load().ort_cuda_sync(self.handle), "ort_cuda_sync")

@@ -5,6 +5,9 @@ peer memory (both ranks' exchange buffers mapped with CUDA IPC) when the
 slices fit, else with NCCL.  Two spawned processes, one per GPU, check the
 sharded results against the oracle, a prefill-sized output that takes the
 NCCL path, and a CUDA-graph replay of sharded calls against eager calls.
+These sessions shard every weight (replicate bytes 0); a weight below the
+size-based placement threshold is then kept whole on every rank and must
+give the single-GPU bits with no exchange.
 """
 import datetime
 import multiprocessing as mp
@@ -52,6 +55,7 @@ def _rank_main(rank, port):
         obj = [CudaSession.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         s = CudaSession(rank, rank=rank, world=WORLD, nccl_id=obj[0], timeout_ms=30000)
+        s.set_replicate_bytes(0)  # every weight sharded: the exchange paths under test
         st = torch.cuda.Stream()
         s.set_stream(st.cuda_stream)
         out = {}
@@ -80,6 +84,16 @@ def _rank_main(rank, port):
                 out[f"{name}{M}"] = float(np.abs(y - ref).max() / np.abs(ref).max())
                 got[(name, M)] = (A, y)
                 got[("d", M)] = yd
+        # size-based placement: a weight below the threshold kept whole on
+        # every rank, computed there (interleaved with sharded calls)
+        s.set_replicate_bytes(-1)
+        Br, scr, zr = O.make_nbits_weight(rng, 2048, 3000, 128, zero_points=True)
+        s.upload_nbits("rep", Br, scr, zr, k=2048, n=3000, block_size=128)
+        s.set_replicate_bytes(0)
+        for M in (1, 16, 300):
+            A = rng.standard_normal((M, 2048)).astype(np.float32)
+            got[("rep", M)] = (A, s.matmul_nbits("rep", A))
+            s.matmul_nbits("sk", rng.standard_normal((M, 4096)).astype(np.float32))
         if rank == 0:
             one = CudaSession(rank)
             for name in ("tm", "sk"):
@@ -88,6 +102,10 @@ def _rank_main(rank, port):
                 for M in (1, 3, 16):
                     A, y = got[(name, M)]
                     out[f"bitwise_{name}{M}"] = bool(np.array_equal(one.matmul_nbits(name, A), y))
+            one.upload_nbits("rep", Br, scr, zr, k=2048, n=3000, block_size=128)
+            for M in (1, 16, 300):
+                A, y = got[("rep", M)]
+                out[f"bitwise_rep{M}"] = bool(np.array_equal(one.matmul_nbits("rep", A), y))
             one.close()
         # prefill-sized output (4096 x 4096 floats per rank): NCCL path
         B, sc, z, K, N, bs = W["pf"]
@@ -156,7 +174,7 @@ def test_two_gpu_sharded_results():
         for key in ("tm1", "tm3", "tm16", "sk1", "sk3", "sk16"):
             assert val[key] <= 1e-5, (r, key, val[key])
         if r == 0:
-            for key in ("tm1", "tm3", "tm16", "sk1", "sk3", "sk16"):
+            for key in ("tm1", "tm3", "tm16", "sk1", "sk3", "sk16", "rep1", "rep16", "rep300"):
                 assert val["bitwise_" + key], key
         assert val["pf"] <= 2e-3, (r, val["pf"])
         assert val["graph_same"], r
@@ -188,6 +206,7 @@ def _timeout_main(rank, port):
         obj = [CudaSession.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         s = CudaSession(rank, rank=rank, world=WORLD, nccl_id=obj[0], timeout_ms=30000)
+        s.set_replicate_bytes(0)  # sharded: the op has an exchange to wait in
         s.set_peer_wait(50)
         rng = np.random.default_rng(3)
         K, N = 1024, 4096
