@@ -131,11 +131,13 @@ ORT_CUDA_API int ort_cuda_set_peer_wait(ort_cuda_session* s, int ms);
  * at most `bytes` is kept whole on every rank and computed there without any
  * exchange of Y; larger weights keep their column shard.  Sharding saves
  * (1 - 1/world) of a weight's stream time but adds the exchange of its
- * output, a few microseconds per decode op whatever its size.  -1 (the
- * default) means 30 MB x world / (world - 1), where the two balance; 0 shards
- * every weight.  The environment variable ORT_CUDA_REPLICATE_BYTES sets it at
- * ort_cuda_open_rank.  Every rank must use the same value.  Results are the
- * single-GPU results either way. */
+ * output and leaves the per-launch fixed cost of a decode op unshrunk.  -1
+ * means the default, 10 MB (measured: small decode projections run faster
+ * whole, projections above about 10 MB gain little or lose, and large-M
+ * prefill prefers its shard); 0 shards every weight.  The environment
+ * variable ORT_CUDA_REPLICATE_BYTES sets it at ort_cuda_open_rank.  Every
+ * rank must use the same value.  Results are the single-GPU results either
+ * way. */
 ORT_CUDA_API int ort_cuda_set_replicate_bytes(ort_cuda_session* s, int64_t bytes);
 
 /* The columns [*n0, *n0 + *nl) of weight `name` held and computed by this

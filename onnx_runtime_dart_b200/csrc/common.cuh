@@ -190,7 +190,7 @@ struct ort_cuda_session {
   // bound of every wait for a peer GPU's flag or data (ms)
   int peer_wait_ms = 1000;
   // MatMulNBits weights of at most this many bytes are replicated on every
-  // rank of an N-sharded session (-1: 30 MB x world / (world - 1))
+  // rank of an N-sharded session (-1: the default, 10 MB)
   int64_t replicate_bytes = -1;
   // CUDA graphs captured from the session stream (ort_cuda_graph_*)
   struct Graph {

@@ -159,18 +159,20 @@ void shard_cols(int64_t N, int rank, int world, int64_t* n0, int64_t* nl, int64_
 }
 
 // Size-based placement on an N-sharded session.  Sharding a weight saves
-// (1 - 1/G) of its stream time but adds the exchange of its output (about
-// 4-5 us for a decode op, whatever its size), so a MatMulNBits weight whose
-// packed bytes stay below replicate_bytes (by default 30 MB x G / (G - 1),
-// where the two balance at 6.4 TB/s) is kept whole on every rank and
-// computed locally; its results are the 1-GPU results.  The decision
-// depends on the shape and the session setting only, so every rank makes it
-// alike (ORT_CUDA_REPLICATE_BYTES must be equal on all ranks).
+// (1 - 1/G) of its stream time but adds the exchange of its output and
+// leaves the GEMV's fixed per-launch cost (4-7 us) unshrunk, so a
+// MatMulNBits weight whose packed bytes stay below replicate_bytes (by
+// default kReplicateBytes) is kept whole on every rank and computed locally;
+// its results are the 1-GPU results.  Measured at 2, 4 and 8 B200 (cfg3 and
+// cfg4 projections of 0.5-8.6 MB: 1.4-1.6x faster replicated; the 9-31 MB
+// cfg5 projections: within 2 us either way at M=1, sharded faster at
+// M=4096).  The decision depends on the shape and the session setting only,
+// so every rank makes it alike (ORT_CUDA_REPLICATE_BYTES must be equal on
+// all ranks).
+constexpr int64_t kReplicateBytes = 10000000;
 bool replicate_nbits(const ort_cuda_session* s, int64_t bytes) {
   if (s->world <= 1) return false;
-  const int64_t lim =
-      s->replicate_bytes >= 0 ? s->replicate_bytes : (int64_t)30000000 * s->world / (s->world - 1);
-  return bytes <= lim;
+  return bytes <= (s->replicate_bytes >= 0 ? s->replicate_bytes : kReplicateBytes);
 }
 
 // A kernel whose bounded wait gave up wrote a code into the host-mapped
@@ -1654,10 +1656,13 @@ struct WsLayout {
 
 // Runs one matmul-family op: stages host IO, computes this rank's columns,
 // all-gathers across ranks, writes back.  `compute` gets device A, C, the
-// local output pointer and its leading dimension.
+// local output pointer and its leading dimension.  y_direct: every kernel of
+// `compute` writes Y with plain stores only, so with host buffers on an
+// unsharded op the kernels store straight into the pinned host Y (its
+// device mapping) and no device-to-host copy follows.
 template <typename F>
 int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, const void* C,
-           size_t c_bytes, float* Y, int64_t M, int flags, F&& compute) {
+           size_t c_bytes, float* Y, int64_t M, int flags, F&& compute, bool y_direct = false) {
   const bool host = (flags & ORT_CUDA_HOST_IO) != 0;
   ORTC_CHECK(!(host && s->capturing), ORT_CUDA_ERR_INVALID_ARG,
              "ORT_CUDA_HOST_IO calls synchronise and cannot be captured in a CUDA graph");
@@ -1686,7 +1691,7 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
   const float* dA = static_cast<const float*>(A);
   const float* dC = static_cast<const float*>(C);
   float* dY = Y;
-  bool y_pinned = false;
+  bool y_pinned = false, y_mapped = false;
   if (host) {
     size_t pin_need = a_bytes + c_bytes + (size_t)(M * N) * 4 + 768;
     rc = ensure_pinned(s, pin_need);
@@ -1701,6 +1706,17 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
     }
     dY = (float*)(ws + L.y);
     y_pinned = is_pinned_host(Y);
+    if (y_direct && !sharded) {
+      // the caller's pinned Y, or the session's pinned staging of Y
+      float* hy = y_pinned ? Y : (float*)((char*)s->pinned + al256(al256(a_bytes) + c_bytes + 256));
+      void* dp = nullptr;
+      if (cudaHostGetDevicePointer(&dp, hy, 0) == cudaSuccess) {
+        dY = static_cast<float*>(dp);
+        y_mapped = true;
+      } else {
+        cudaGetLastError();
+      }
+    }
   }
   float* yloc = sharded ? (float*)(ws + L.yloc) : dY;
   const int64_t ldy = sharded ? w.ns : N;
@@ -1735,6 +1751,13 @@ int run_op(ort_cuda_session* s, const Weight& w, const void* A, size_t a_bytes, 
   }
   if (host) {
     const size_t yb = (size_t)(M * N) * 4;
+    if (y_mapped) {  // the kernels wrote the host Y (or its staging) already
+      rc = bounded_sync(s);
+      if (rc) return rc;
+      if (!y_pinned)
+        std::memcpy(Y, (char*)s->pinned + al256(al256(a_bytes) + c_bytes + 256), yb);
+      return ORT_CUDA_OK;
+    }
     if (y_pinned) {
       ORTC_CUDA(cudaMemcpyAsync(Y, dY, yb, cudaMemcpyDeviceToHost, s->stream));
       return bounded_sync(s);
@@ -1850,7 +1873,10 @@ ORT_CUDA_API int ort_cuda_matmul_nbits(ort_cuda_session* s, const char* name, co
                   }
                   return launch_simt_gemm(w, dA, M, false, yl, ldy, false, 1.0f, 1.0f, nullptr, 0,
                                           0, 0, s->stream, &s->launches);
-                });
+                },
+                // decode sizes in the exact and strict modes: the GEMV and the
+                // CUDA-core GEMM, plain stores of Y
+                (mode == ORT_CUDA_MODE_EXACT || mode == ORT_CUDA_MODE_STRICT) && M <= 64);
 }
 
 }  // extern "C"

@@ -168,7 +168,7 @@ class CudaSession:
     def set_replicate_bytes(self, nbytes: int) -> None:
         """MatMulNBits weights of at most nbytes packed bytes uploaded from now
         on are kept whole on every rank (no exchange); -1: the default
-        30 MB x world / (world - 1), 0: shard every weight."""
+        (10 MB), 0: shard every weight."""
         check(_lib.load().ort_cuda_set_replicate_bytes(self.handle, int(nbytes)),
               "ort_cuda_set_replicate_bytes")
 
