@@ -258,27 +258,39 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         const uint4 w4 = lds128(qa + ((uint32_t)(hw << 4) ^ qsw));
         const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
         const uint32_t cb = smem_u32(conv + c * kCBytes) + rowoff;
-        // word i holds k 8i..8i+7; the {1024 + z, scale} entry of its block
-        // within the stage's table, all four loads issued before any use
-        uint32_t vs[4];
+        // word i holds k 8i..8i+7 and takes the {1024 + z, scale} entry of
+        // its block within the stage's table
+        auto convert = [&](const uint32_t (&vs)[4]) {
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-          asm volatile("ld.shared.u32 %0, [%1];"
-                       : "=r"(vs[j])
-                       : "r"(sza + (uint32_t)((((8 * (4 * hw + j)) >> p.bs_shift) * PBN + n) * 4)));
+          for (int j = 0; j < 4; j++) {
+            const int i = 4 * hw + j;
+            const uint32_t v = vs[j];
+            const uint32_t zz = prmt(v, v, 0x1010), sc = prmt(v, v, 0x3232);
+            const uint32_t lo = words[j] & 0x0F0F0F0Fu, hi = (words[j] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t r0 = deq2(prmt(lo, 0x64646464u, 0x4140), zz, sc);  // k0, k1
+            const uint32_t r1 = deq2(prmt(lo, 0x64646464u, 0x4342), zz, sc);  // k2, k3
+            const uint32_t r2 = deq2(prmt(hi, 0x64646464u, 0x4140), zz, sc);  // k4, k5
+            const uint32_t r3 = deq2(prmt(hi, 0x64646464u, 0x4342), zz, sc);  // k6, k7
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(cb + ((i ^ sw) << 4)),
+                         "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+                         : "memory");
+          }
+        };
+        if (p.bs_shift >= 6) {
+          // a block of 64 or more k: one entry serves the whole stage (one
+          // load, and its halves split once instead of per word)
+          uint32_t v;
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(sza + (uint32_t)(n * 4)));
+          const uint32_t vs[4] = {v, v, v, v};
+          convert(vs);
+        } else {
+          uint32_t vs[4];  // all four loads issued before any use
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int i = 4 * hw + j;
-          const uint32_t v = vs[j];
-          const uint32_t zz = prmt(v, v, 0x1010), sc = prmt(v, v, 0x3232);
-          const uint32_t lo = words[j] & 0x0F0F0F0Fu, hi = (words[j] >> 4) & 0x0F0F0F0Fu;
-          const uint32_t r0 = deq2(prmt(lo, 0x64646464u, 0x4140), zz, sc);  // k0, k1
-          const uint32_t r1 = deq2(prmt(lo, 0x64646464u, 0x4342), zz, sc);  // k2, k3
-          const uint32_t r2 = deq2(prmt(hi, 0x64646464u, 0x4140), zz, sc);  // k4, k5
-          const uint32_t r3 = deq2(prmt(hi, 0x64646464u, 0x4342), zz, sc);  // k6, k7
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(cb + ((i ^ sw) << 4)),
-                       "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-                       : "memory");
+          for (int j = 0; j < 4; j++)
+            asm volatile("ld.shared.u32 %0, [%1];"
+                         : "=r"(vs[j])
+                         : "r"(sza + (uint32_t)((((8 * (4 * hw + j)) >> p.bs_shift) * PBN + n) * 4)));
+          convert(vs);
         }
         fence_proxy_async_smem();
         __syncwarp();
